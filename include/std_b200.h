@@ -1,0 +1,165 @@
+/*
+ * std_b200.h -- C ABI of the B200 (sm_100a) STD sparse-to-dense decode path.
+ *
+ * Conventions for every entry point:
+ *   - all tensor pointers are caller-owned DEVICE pointers (bf16 = 16-bit
+ *     bfloat16 bit patterns, contiguous, 16-byte aligned unless stated);
+ *   - `stream` is a cudaStream_t (passed as void*); work is enqueued only,
+ *     nothing synchronises, and every launch is CUDA-graph capturable;
+ *   - return value: 0 ok; 1 bad shape/argument; 2 capacity exceeded;
+ *     3 unsupported device / driver entry point missing; 4 CUDA launch error;
+ *     5 workspace missing or too small.  No exceptions cross the ABI;
+ *   - lengths are device-resident int32 arrays (one entry per request), so a
+ *     decode round never reads them on the host;
+ *   - kernels never allocate; scratch memory is a caller-provided workspace
+ *     whose size is given by the matching *_workspace_bytes() function.  A
+ *     workspace must be zero-filled once before its first use (the kernels
+ *     leave their split counters at zero on exit) and must not be shared by
+ *     launches that can run concurrently;
+ *   - device-side faults are never raised: a wait that exceeds its ~1 s limit
+ *     or an out-of-range index is recorded in a device error word that
+ *     std_get_device_error() reads and clears.
+ *
+ * KV cache layout (both caches): [layers, 2 (K,V), B, Hkv, cap, D] bf16, so
+ * the K (or V) cache of one layer is a contiguous [B, Hkv, cap, D] block.
+ * Reference counterparts are cited as path:line of mcy1123/STD.
+ */
+#ifndef STD_B200_H
+#define STD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- library ---------------------------------------------------------- */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int std_version(void);
+
+/* Reads and clears the device error word of the current device
+ * (0 none, 1 wait timeout, 2 index out of bounds skipped, 3 length > capacity). */
+int std_get_device_error(int* code_out);
+
+/* 1 when the current device is sm_100 (B200), else 0. */
+int std_device_supported(void);
+
+/* ---- (b) sparse draft attention --------------------------------------- */
+
+/* Replaces: std_qwen25vl.py:406-417 (F.scaled_dot_product_attention(q, k, v,
+ * enable_gqa=True), q_len = 1) and triton_attention.py:83-112
+ * (fused_gqa_attention(q, k, v)).
+ * q [B, Hq, D]; k_cache / v_cache: one layer's [B, Hkv, cap, D]; request b
+ * attends to keys 0 .. lens[b]+len_offset-1 (no mask); out [B, Hq, D] bf16;
+ * lse [B, Hq] fp32 natural-log (optional, may be NULL).  Hq = 7*Hkv, D = 128. */
+size_t std_draft_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int cap);
+int std_draft_attn(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens, int len_offset,
+                   int B, int Hq, int Hkv, int D, int cap, void* out, float* lse, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* ---- (c) parallel dense verify attention (also AR dense decode, nq = 1) -- */
+
+/* Replaces: modeling_qwen2_5_vl.py:1096-1133 (repeat_kv + F.sdpa with the
+ * causal mask of :65-101) in the verify forward std_qwen25vl.py:797-803 and in
+ * the AR loop std_qwen25vl.py:584-590.
+ * q [B, nq, Hq, D] (token-major); L = lens[b]+len_offset keys (the nq new
+ * tokens' keys already appended); causal=1: token t sees keys 0 .. L-nq+t;
+ * causal=0: every token sees all L keys (a sequence shard that holds only
+ * past keys).  out [B, nq, Hq, D] bf16; lse [B, nq, Hq] fp32 (optional).
+ * 1 <= nq <= 18, Hq = 7*Hkv, D = 128.  Rows are bit-identical for any nq. */
+size_t std_verify_attn_workspace_bytes(int B, int Hkv, int cap);
+int std_verify_attn(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens, int len_offset,
+                    int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out, float* lse,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Exact (O, LSE) merge of attention partials computed over disjoint key
+ * ranges (sequence shards).  Replaces nothing in the reference (it has no
+ * sequence parallelism); it is the exchange step of sharded verify.
+ * o_parts [n_parts, rows, D] bf16, lse_parts [n_parts, rows] fp32 ->
+ * out [rows, D] bf16, lse_out [rows] (optional). */
+int std_merge_partials(const void* o_parts, const float* lse_parts, int n_parts, int rows, int D, void* out,
+                       float* lse_out, void* stream);
+
+/* ---- (a) prefill-time selection ---------------------------------------- */
+
+/* Replaces: modeling_qwen2_5_vl.py:966-995 (custom fp16 attention weights for
+ * output_attentions=True) + std_qwen25vl.py:204-218 (grouped fp32 sum).
+ * q_text [T, Hq, D] bf16 (text rows, after RoPE); k_cache [Hkv, kstride, D]
+ * bf16 (one request, one layer, rows 0..P-1); row t sits at absolute position
+ * q_start+t and sees keys 0..q_start+t.  scores [Hkv, P] fp32.
+ * write_probs=1 leaves the fp16 probabilities in the workspace as
+ * [Hq, T, pstride] (pstride from std_select_probs_view) for the selection
+ * branch's attention output. */
+size_t std_select_workspace_bytes(int T, int Hq, int P);
+int std_select_scores(const void* q_text, const void* k_cache, long long kstride, int T, int Hq, int Hkv, int D,
+                      int P, int q_start, float scale, float* scores, int write_probs, void* workspace,
+                      size_t workspace_bytes, void* stream);
+int std_select_probs_view(int T, int Hq, int P, long long* pstride_out);
+
+/* Replaces: std_qwen25vl.py:219-222 (index_select visual columns, torch.topk,
+ * map to positions, sort).  For each of n_seg score rows (stride seg_stride):
+ * the K largest scores among visual_pos[0..V-1] (ascending absolute
+ * positions), ties to the lowest position, written ascending to out[n_seg, K]. */
+int std_topk_select(const float* scores, long long seg_stride, int n_seg, const int32_t* visual_pos, int V, int K,
+                    int32_t* out, void* stream);
+
+/* Replaces: std_qwen25vl.py:265-298 (compact_sparse_prompt_cache) and
+ * :301-320 (copy_prompt_cache).  For request b and every layer and KV head,
+ * slot j of the sparse cache receives dense row idx[j] where
+ * idx = sorted(non_visual U topk[layer, head]) (disjoint sets). */
+int std_compact_gather(const void* dense_cache, void* sparse_cache, int layers, int B, int b, int Hkv, int D,
+                       int cap_dense, int cap_sparse, const int32_t* non_visual, int NV, const int32_t* topk, int K,
+                       void* stream);
+
+/* ---- decoder pieces around the library GEMMs --------------------------- */
+
+/* modeling_qwen2_5_vl.py:1336 (embed_tokens): out[b*n+j] = table[tok[b*tok_stride+tok_start+j]]. */
+int std_embed(const void* table, int vocab, int H, const int32_t* tok, int tok_stride, int tok_start, int n, int B,
+              void* out, void* stream);
+/* modeling_qwen2_5_vl.py:183-197 (Qwen2RMSNorm). */
+int std_rmsnorm(const void* x, const void* w, float eps, int M, int H, void* out, void* stream);
+/* modeling_qwen2_5_vl.py:690-732 (RoPE, 1-D positions) + kv_cache.py:54-69
+ * (KVCache.cat): rotates q and k of qkv [B*n, (Hq+2Hkv)*D], writes q_out and
+ * appends k, v at cache slot slot_base[b]+slot_off+j, position
+ * pos_base[b]+pos_off+j, cos/sin tables [max_pos, D/2] bf16. */
+int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, int D, const int32_t* pos_base, int pos_off,
+                    const int32_t* slot_base, int slot_off, const void* cos_t, const void* sin_t, int max_pos,
+                    void* q_out, void* k_cache, void* v_cache, int cap, void* stream);
+/* modeling_qwen2_5_vl.py:674-687 (Qwen2MLP act_fn(gate) * up), gu = [gate | up]. */
+int std_silu_mul(const void* gu, int M, int I, void* out, void* stream);
+/* residual add (modeling_qwen2_5_vl.py:1200-1221). */
+int std_add(const void* a, const void* b, size_t n, void* out, void* stream);
+/* std_qwen25vl.py:98-99, :806 (torch.argmax, first index on ties):
+ * out[(row/n)*out_stride + out_start + row%n] = argmax(logits[row, :V]). */
+int std_argmax_rows(const void* logits, int rows, int V, int n, int out_stride, int out_start, int32_t* out,
+                    void* stream);
+
+/* ---- (d) fused greedy acceptance + rollback ---------------------------- */
+
+/* Replaces: std_qwen25vl.py:806-815 (argmax compare, accepted prefix, bonus),
+ * :910-921 (commit, EOS, max_new_tokens), :923-929 (dense/sparse cache length
+ * rollback) and :931-939 (pending bonus).  Device state, int32 per request:
+ * tok [B, tok_stride] (tok[0] pending bonus, tok[1..gamma] drafts), vpred
+ * [B, vstride] verify-row argmax, dense_next [B] prefill argmax, ctx_len,
+ * dense_len, sparse_len, n_gen, done [B], out_tokens [B, max_new], stats
+ * [B, 4] (rounds, accepted, proposed, last accept), accept_hist [B, hist_cap]
+ * (may be NULL).  pending = 1 when tok[0] holds a pending bonus (every round
+ * after the first). */
+int std_accept_commit(int B, int gamma, int pending, int32_t* tok, int tok_stride, const int32_t* vpred, int vstride,
+                      const int32_t* dense_next, int max_new, int eos, int ignore_eos, int32_t* ctx_len,
+                      int32_t* dense_len, int32_t* sparse_len, int32_t* n_gen, int32_t* done, int32_t* out_tokens,
+                      int32_t* stats, int32_t* accept_hist, int hist_cap, void* stream);
+
+/* AR bookkeeping (std_qwen25vl.py:584-590): record tok[b][0] as generated. */
+int std_ar_commit(int B, int tok_stride, int max_new, int eos, int ignore_eos, const int32_t* tok, int32_t* n_gen,
+                  int32_t* done, int32_t* out_tokens, void* stream);
+/* AR bookkeeping: dense_len[b] += 1 after the step's forward. */
+int std_ar_advance(int B, int32_t* dense_len, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* STD_B200_H */

@@ -1,0 +1,91 @@
+"""ctypes binding of libstd_b200.so (the C ABI declared in include/std_b200.h).
+
+This is the same binding a maintainer of the reference would add next to
+std_repro/triton_attention.py: plain pointers, sizes and a cudaStream_t.  Any
+nonzero status raises RuntimeError, matching the reference's error style
+(std_qwen25vl.py:379-380, :401-402).  There is no fallback: if the library is
+missing the import fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libstd_b200.so")
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+I64 = ctypes.c_longlong
+SZ = ctypes.c_size_t
+F = ctypes.c_float
+PI32 = ctypes.c_void_p
+PF = ctypes.c_void_p
+
+# name -> (restype, argtypes); the single source of truth for the ABI surface
+SIGNATURES: Dict[str, tuple] = {
+    "std_version": (I, []),
+    "std_get_device_error": (I, [P]),
+    "std_device_supported": (I, []),
+    "std_draft_attn_workspace_bytes": (SZ, [I, I, I, I, I]),
+    "std_draft_attn": (I, [P, P, P, PI32, I, I, I, I, I, I, P, PF, P, SZ, P]),
+    "std_verify_attn_workspace_bytes": (SZ, [I, I, I]),
+    "std_verify_attn": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, P, PF, P, SZ, P]),
+    "std_merge_partials": (I, [P, PF, I, I, I, P, PF, P]),
+    "std_select_workspace_bytes": (SZ, [I, I, I]),
+    "std_select_scores": (I, [P, P, I64, I, I, I, I, I, I, F, PF, I, P, SZ, P]),
+    "std_select_probs_view": (I, [I, I, I, P]),
+    "std_topk_select": (I, [PF, I64, I, PI32, I, I, PI32, P]),
+    "std_compact_gather": (I, [P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P]),
+    "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
+    "std_rmsnorm": (I, [P, P, F, I, I, P, P]),
+    "std_rope_append": (I, [P, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I, P]),
+    "std_silu_mul": (I, [P, I, I, P, P]),
+    "std_add": (I, [P, P, SZ, P, P]),
+    "std_argmax_rows": (I, [P, I, I, I, I, I, PI32, P]),
+    "std_accept_commit": (I, [I, I, I, PI32, I, PI32, I, PI32, I, I, I, PI32, PI32, PI32, PI32, PI32, PI32, PI32,
+                              PI32, I, P]),
+    "std_ar_commit": (I, [I, I, I, I, I, PI32, PI32, PI32, PI32, P]),
+    "std_ar_advance": (I, [I, PI32, P]),
+}
+
+_STATUS = {1: "bad shape or argument", 2: "capacity exceeded", 3: "unsupported device or driver entry point",
+           4: "CUDA launch error", 5: "workspace missing or too small"}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the in-tree library (building it first if sources are newer)."""
+    global _lib
+    if _lib is None:
+        from . import build as _build
+
+        if _build.needs_build():
+            _build.build()
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> int:
+    rc = getattr(load(), name)(*args)
+    if rc != 0:
+        raise RuntimeError(f"{name} failed with status {rc} ({_STATUS.get(rc, 'unknown')})")
+    return rc
+
+
+def query(name: str, *args):
+    return getattr(load(), name)(*args)
+
+
+def device_error() -> int:
+    code = ctypes.c_int(0)
+    call("std_get_device_error", ctypes.byref(code))
+    return int(code.value)

@@ -1,0 +1,210 @@
+"""torch-facing wrappers over the C ABI (one call per kernel entry point).
+
+PyTorch only supplies device memory and the current CUDA stream here; every
+call goes through libstd_b200.so.  Tensors must be CUDA, contiguous and of the
+documented dtype -- there is no CPU path and no fallback.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _lib
+
+_WS: Dict[Tuple[str, int], torch.Tensor] = {}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (no CPU path)")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
+    """Zero-initialised scratch buffer, grown on demand, one per (kind, device).
+
+    The kernels leave their split counters at zero, so a buffer is zeroed only
+    when it is (re)allocated.  Allocation happens outside graph capture: call
+    each op once eagerly before capturing it.
+    """
+    key = (kind, device.index if device.index is not None else torch.cuda.current_device())
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+# ----------------------------------------------------------------------------
+# attention
+# ----------------------------------------------------------------------------
+
+def draft_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
+                    len_offset: int = 0, out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
+    """q [B, Hq, D] bf16; caches [B, Hkv, cap, D] bf16; lens [B] int32 (device)."""
+    B, Hq, D = q.shape
+    _, Hkv, cap, _ = k_cache.shape
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t, torch.bfloat16, n)
+    _check(lens, torch.int32, "lens")
+    if out is None:
+        out = torch.empty_like(q)
+    nb = _lib.query("std_draft_attn_workspace_bytes", B, Hq, Hkv, D, cap)
+    ws = workspace("draft", nb, q.device)
+    _lib.call("std_draft_attn", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr(), int(len_offset),
+              B, Hq, Hkv, D, cap, out.data_ptr(), _p(lse), ws.data_ptr(), ws.numel(), _stream())
+    return out
+
+
+def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
+                     len_offset: int, causal: bool = True, out: Optional[torch.Tensor] = None,
+                     lse: Optional[torch.Tensor] = None):
+    """q [B, nq, Hq, D] bf16; caches [B, Hkv, cap, D]; keys = lens[b] + len_offset."""
+    B, nq, Hq, D = q.shape
+    _, Hkv, cap, _ = k_cache.shape
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t, torch.bfloat16, n)
+    _check(lens, torch.int32, "lens")
+    if out is None:
+        out = torch.empty_like(q)
+    nb = _lib.query("std_verify_attn_workspace_bytes", B, Hkv, cap)
+    ws = workspace("verify", nb, q.device)
+    _lib.call("std_verify_attn", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr(),
+              int(len_offset), nq, 1 if causal else 0, B, Hq, Hkv, D, cap, out.data_ptr(), _p(lse), ws.data_ptr(),
+              ws.numel(), _stream())
+    return out
+
+
+def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out: Optional[torch.Tensor] = None,
+                   lse_out: Optional[torch.Tensor] = None):
+    """o_parts [n, rows, D] bf16, lse_parts [n, rows] fp32 -> out [rows, D]."""
+    n, rows, D = o_parts.shape
+    _check(o_parts, torch.bfloat16, "o_parts")
+    _check(lse_parts, torch.float32, "lse_parts")
+    if out is None:
+        out = torch.empty((rows, D), dtype=torch.bfloat16, device=o_parts.device)
+    _lib.call("std_merge_partials", o_parts.data_ptr(), lse_parts.data_ptr(), n, rows, D, out.data_ptr(),
+              _p(lse_out), _stream())
+    return out
+
+
+# ----------------------------------------------------------------------------
+# selection
+# ----------------------------------------------------------------------------
+
+def select_scores(q_text: torch.Tensor, k_rows: torch.Tensor, P: int, q_start: int,
+                  scores: Optional[torch.Tensor] = None, write_probs: bool = False, scale: Optional[float] = None):
+    """q_text [T, Hq, D] bf16; k_rows [Hkv, kstride, D] bf16 -> scores [Hkv, P] fp32.
+
+    With write_probs, also returns the fp16 probabilities view [Hq, T, P].
+    """
+    T, Hq, D = q_text.shape
+    Hkv, kstride, _ = k_rows.shape
+    _check(q_text, torch.bfloat16, "q_text")
+    _check(k_rows, torch.bfloat16, "k_rows")
+    if scores is None:
+        scores = torch.empty((Hkv, P), dtype=torch.float32, device=q_text.device)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    nb = _lib.query("std_select_workspace_bytes", T, Hq, P)
+    ws = workspace("select", nb, q_text.device)
+    _lib.call("std_select_scores", q_text.data_ptr(), k_rows.data_ptr(), kstride, T, Hq, Hkv, D, P, q_start,
+              float(scale), scores.data_ptr(), 1 if write_probs else 0, ws.data_ptr(), ws.numel(), _stream())
+    if not write_probs:
+        return scores
+    import ctypes
+
+    ps = ctypes.c_longlong(0)
+    _lib.call("std_select_probs_view", T, Hq, P, ctypes.byref(ps))
+    probs = ws[: Hq * T * ps.value * 2].view(torch.float16).view(Hq, T, ps.value)[:, :, :P]
+    return scores, probs
+
+
+def topk_select(scores: torch.Tensor, visual_pos: torch.Tensor, k: int, out: Optional[torch.Tensor] = None):
+    """scores [n_seg, P] fp32; visual_pos [V] int32 ascending -> [n_seg, k] int32 ascending."""
+    n_seg, P = scores.shape
+    _check(scores, torch.float32, "scores")
+    _check(visual_pos, torch.int32, "visual_pos")
+    if out is None:
+        out = torch.empty((n_seg, k), dtype=torch.int32, device=scores.device)
+    _lib.call("std_topk_select", scores.data_ptr(), P, n_seg, visual_pos.data_ptr(), visual_pos.numel(), k,
+              out.data_ptr(), _stream())
+    return out
+
+
+def compact_gather(dense_cache: torch.Tensor, sparse_cache: torch.Tensor, b: int, non_visual: torch.Tensor,
+                   topk: torch.Tensor):
+    """caches [layers, 2, B, Hkv, cap, D]; non_visual [NV] int32; topk [layers, Hkv, K] int32."""
+    layers, _, B, Hkv, cap_d, D = dense_cache.shape
+    cap_s = sparse_cache.shape[4]
+    _check(dense_cache, torch.bfloat16, "dense_cache")
+    _check(sparse_cache, torch.bfloat16, "sparse_cache")
+    _check(non_visual, torch.int32, "non_visual")
+    _check(topk, torch.int32, "topk")
+    _lib.call("std_compact_gather", dense_cache.data_ptr(), sparse_cache.data_ptr(), layers, B, b, Hkv, D, cap_d,
+              cap_s, non_visual.data_ptr(), non_visual.numel(), topk.data_ptr(), topk.shape[-1], _stream())
+
+
+# ----------------------------------------------------------------------------
+# decoder pieces
+# ----------------------------------------------------------------------------
+
+def embed(table: torch.Tensor, tok: torch.Tensor, tok_start: int, n: int, out: torch.Tensor):
+    B, stride = tok.shape
+    _lib.call("std_embed", table.data_ptr(), table.shape[0], table.shape[1], tok.data_ptr(), stride, tok_start, n, B,
+              out.data_ptr(), _stream())
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor):
+    H = x.shape[-1]
+    M = x.numel() // H
+    _lib.call("std_rmsnorm", x.data_ptr(), w.data_ptr(), float(eps), M, H, out.data_ptr(), _stream())
+    return out
+
+
+def rope_append(qkv: torch.Tensor, B: int, n: int, Hq: int, Hkv: int, D: int, pos_base: torch.Tensor, pos_off: int,
+                slot_base: torch.Tensor, slot_off: int, cos_t: torch.Tensor, sin_t: torch.Tensor,
+                q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor):
+    cap = k_cache.shape[-2]
+    _lib.call("std_rope_append", qkv.data_ptr(), B, n, Hq, Hkv, D, pos_base.data_ptr(), int(pos_off),
+              slot_base.data_ptr(), int(slot_off), cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape[0],
+              q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), cap, _stream())
+    return q_out
+
+
+def silu_mul(gu: torch.Tensor, out: torch.Tensor):
+    I2 = gu.shape[-1]
+    M = gu.numel() // I2
+    _lib.call("std_silu_mul", gu.data_ptr(), M, I2 // 2, out.data_ptr(), _stream())
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor):
+    _lib.call("std_add", a.data_ptr(), b.data_ptr(), a.numel(), out.data_ptr(), _stream())
+    return out
+
+
+def argmax_rows(logits: torch.Tensor, out: torch.Tensor, n: int = 1, out_stride: int = 1, out_start: int = 0):
+    V = logits.shape[-1]
+    rows = logits.numel() // V
+    _lib.call("std_argmax_rows", logits.data_ptr(), rows, V, n, out_stride, out_start, out.data_ptr(), _stream())
+    return out
+
+
+def device_error() -> int:
+    return _lib.device_error()
