@@ -1,0 +1,339 @@
+"""GPU parity tests of every kernel against the oracle (through the C ABI).
+
+Tolerances (north star): attention outputs max abs <= 2e-2, mean abs <= 2e-3
+against fp32/fp64 math; selection scores and indices bit-exact against the
+oracle; integer work (top-K, compaction, acceptance) exact.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from oracle.inputs import CONFIG0, SMALL, bf16_bits, make_layer_inputs
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+ATOL_MAX, ATOL_MEAN = 2e-2, 2e-3
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from std_b200 import ops as _ops
+
+    assert torch.cuda.is_available()
+    return _ops
+
+
+def _bf16(x, dev="cuda"):
+    return torch.as_tensor(x).to(torch.bfloat16).to(dev).contiguous()
+
+
+def _check_attn(got, ref, what):
+    err = np.abs(got.astype(np.float64) - ref)
+    assert err.max() <= ATOL_MAX, f"{what}: max abs err {err.max()}"
+    assert err.mean() <= ATOL_MEAN, f"{what}: mean abs err {err.mean()}"
+
+
+def _no_device_error(ops):
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+
+
+# ------------------------------------------------------------------ draft
+@pytest.mark.parametrize("B,lens,cap", [(1, [1024], 1200), (3, [1, 700, 1301], 1408), (8, [1152] * 8, 1200)])
+def test_draft_attention_vs_oracle(ops, B, lens, cap):
+    g = torch.Generator().manual_seed(5 + B)
+    q = torch.randn(B, 28, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, 4, cap, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, 4, cap, 128, generator=g).to(torch.bfloat16)
+    lens_t = torch.tensor(lens, dtype=torch.int32)
+    lse = torch.empty(B, 28, dtype=torch.float32, device="cuda")
+    out = ops.draft_attention(q.cuda(), k.cuda(), v.cuda(), lens_t.cuda(), 0, lse=lse)
+    ref, ref_lse = oracle.draft_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), lens)
+    _check_attn(out.float().cpu().numpy(), ref, "draft")
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() < 1e-3
+    # second call reuses the workspace: split tickets must have been reset
+    out2 = ops.draft_attention(q.cuda(), k.cuda(), v.cuda(), lens_t.cuda(), 0)
+    assert torch.equal(out, out2)
+    _no_device_error(ops)
+
+
+def test_draft_attention_len_offset(ops):
+    g = torch.Generator().manual_seed(2)
+    q = torch.randn(2, 28, 128, generator=g).to(torch.bfloat16).cuda()
+    k = torch.randn(2, 4, 512, 128, generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn(2, 4, 512, 128, generator=g).to(torch.bfloat16).cuda()
+    a = ops.draft_attention(q, k, v, torch.tensor([100, 200], dtype=torch.int32, device="cuda"), 3)
+    b = ops.draft_attention(q, k, v, torch.tensor([103, 203], dtype=torch.int32, device="cuda"), 0)
+    assert torch.equal(a, b)
+
+
+def test_draft_attention_config0_matches_reference_sdpa(ops):
+    gl = np.load(os.path.join(GOLDEN, "attention_config0.npz"))
+    inp = make_layer_inputs(CONFIG0, 0)
+    idx = torch.from_numpy(gl["compact_index"])
+    kc = torch.stack([inp["k"][0, h, idx[h]] for h in range(4)])[None]
+    vc = torch.stack([inp["v"][0, h, idx[h]] for h in range(4)])[None]
+    q = inp["q_draft"][0, :, 0][None]
+    out = ops.draft_attention(_bf16(q), _bf16(kc), _bf16(vc), torch.tensor([1024], dtype=torch.int32, device="cuda"))
+    _check_attn(out[0].float().cpu().numpy(), gl["draft_out"].astype(np.float64), "draft config0")
+
+
+# ------------------------------------------------------------------ verify
+@pytest.mark.parametrize("B,nq,lens,cap", [(1, 10, [600], 1024), (2, 10, [1700, 513], 2048), (3, 1, [5, 129, 1000], 1024),
+                                           (1, 16, [4100], 4608)])
+def test_verify_attention_vs_oracle(ops, B, nq, lens, cap):
+    g = torch.Generator().manual_seed(11 + nq)
+    q = torch.randn(B, nq, 28, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, 4, cap, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, 4, cap, 128, generator=g).to(torch.bfloat16)
+    lens_t = torch.tensor(lens, dtype=torch.int32)
+    lse = torch.empty(B, nq, 28, dtype=torch.float32, device="cuda")
+    out = ops.verify_attention(q.cuda(), k.cuda(), v.cuda(), lens_t.cuda(), 0, lse=lse)
+    ref, ref_lse = oracle.verify_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), lens)
+    _check_attn(out.float().cpu().numpy(), ref, "verify")
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() < 1e-3
+    out2 = ops.verify_attention(q.cuda(), k.cuda(), v.cuda(), lens_t.cuda(), 0)
+    assert torch.equal(out, out2)
+    _no_device_error(ops)
+
+
+def test_verify_config0_matches_reference_sdpa(ops):
+    gl = np.load(os.path.join(GOLDEN, "attention_config0.npz"))
+    inp = make_layer_inputs(CONFIG0, 0)
+    q = inp["q_verify"][0].permute(1, 0, 2)[None]  # [1, 10, 28, 128]
+    out = ops.verify_attention(_bf16(q), _bf16(inp["k"]), _bf16(inp["v"]),
+                               torch.tensor([CONFIG0.P], dtype=torch.int32, device="cuda"), 0)
+    _check_attn(out[0].float().cpu().numpy(), gl["verify_out"].astype(np.float64), "verify config0")
+
+
+@pytest.mark.parametrize("L", [16384, 32768, 65536])
+def test_verify_config1_vs_math_sdpa(ops, L):
+    """bf16, 10 causal queries, seed 1, O and LSE vs math SDPA."""
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randn(1, 10, 28, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(1, 4, L, 128, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(1, 4, L, 128, generator=g, device="cuda").to(torch.bfloat16)
+    lse = torch.empty(1, 10, 28, dtype=torch.float32, device="cuda")
+    out = ops.verify_attention(q, k, v, torch.tensor([L], dtype=torch.int32, device="cuda"), 0, lse=lse)
+    qf = q.float().permute(0, 2, 1, 3)
+    kf = k.float().repeat_interleave(7, dim=1)
+    vf = v.float().repeat_interleave(7, dim=1)
+    s = (qf @ kf.transpose(-1, -2)) / np.sqrt(128.0)
+    mask = torch.arange(L, device="cuda")[None, :] > (L - 10 + torch.arange(10, device="cuda"))[:, None]
+    s = s.masked_fill(mask, float("-inf"))
+    ref_lse = torch.logsumexp(s, dim=-1)
+    ref = torch.softmax(s, dim=-1) @ vf
+    err = (out.float().permute(0, 2, 1, 3) - ref).abs()
+    assert err.max().item() <= ATOL_MAX and err.mean().item() <= ATOL_MEAN
+    assert (lse.permute(0, 2, 1) - ref_lse).abs().max().item() < 1e-3
+
+
+@pytest.mark.parametrize("L", [10, 127, 128, 129, 137, 511, 512, 513, 519, 520, 1030, 1535, 2049])
+def test_verify_rows_bit_identical_to_ar_rows(ops, L):
+    """A verify row equals the nq=1 (AR) call for the same token bit for bit."""
+    nq = 10
+    g = torch.Generator(device="cuda").manual_seed(L)
+    cap = 2176
+    q = torch.randn(2, nq, 28, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(2, 4, cap, 128, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(2, 4, cap, 128, generator=g, device="cuda").to(torch.bfloat16)
+    lens = torch.tensor([L, L + 3], dtype=torch.int32, device="cuda")
+    ver = ops.verify_attention(q, k, v, lens, 0)
+    for t in range(nq):
+        ar = ops.verify_attention(q[:, t:t + 1].contiguous(), k, v, lens, -(nq - 1 - t))
+        assert torch.equal(ar[:, 0], ver[:, t]), f"row {t} differs at L={L}"
+
+
+# ------------------------------------------------------------------ selection
+@pytest.mark.parametrize("case", [SMALL, CONFIG0], ids=lambda c: c.name)
+def test_select_scores_bit_exact_and_topk(ops, case):
+    inp = make_layer_inputs(case, 0)
+    qb = bf16_bits(inp["q_text"][0].permute(1, 0, 2).contiguous())
+    kb = bf16_bits(inp["k"][0])
+    ref_scores = oracle.select_scores(qb, kb, case.q_start, case.P)
+    q = torch.from_numpy(qb.view(np.int16)).view(torch.bfloat16).cuda()
+    k = torch.from_numpy(kb.view(np.int16)).view(torch.bfloat16).cuda()
+    scores = ops.select_scores(q, k, case.P, case.q_start)
+    got = scores.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref_scores.view(np.uint32)), \
+        f"{(got != ref_scores).sum()} scores differ"
+    vis = torch.arange(case.V, dtype=torch.int32, device="cuda")
+    topk = ops.topk_select(scores, vis, case.k).cpu().numpy()
+    ref_topk = oracle.topk_lowest(ref_scores, np.arange(case.V, dtype=np.int32), case.k)
+    assert np.array_equal(topk, ref_topk)
+    gl = np.load(os.path.join(GOLDEN, f"selection_{case.name}.npz"))
+    for h in range(4):
+        assert set(topk[h].tolist()) == set(gl["ref_topk"][h].tolist())
+    _no_device_error(ops)
+
+
+def test_select_probs_written(ops):
+    case = SMALL
+    inp = make_layer_inputs(case, 0)
+    qb = bf16_bits(inp["q_text"][0].permute(1, 0, 2).contiguous())
+    kb = bf16_bits(inp["k"][0])
+    _, logits, m, l = oracle.select_scores(qb, kb, case.q_start, case.P, return_logits=True)
+    q = torch.from_numpy(qb.view(np.int16)).view(torch.bfloat16).cuda()
+    k = torch.from_numpy(kb.view(np.int16)).view(torch.bfloat16).cuda()
+    _, probs = ops.select_scores(q, k, case.P, case.q_start, write_probs=True)
+    lf = logits.view(np.float16).astype(np.float32)
+    ex = oracle.std_exp((lf - m[..., None]).astype(np.float32))
+    ref_p = (ex / l[..., None].astype(np.float32)).astype(np.float32).astype(np.float16)
+    assert np.array_equal(probs.cpu().numpy().view(np.uint16), ref_p.view(np.uint16))
+
+
+def test_topk_ties_lowest_index(ops):
+    rng = np.random.default_rng(4)
+    P = 5000
+    sc = np.round(rng.random((6, P)) * 20).astype(np.float32)  # heavy ties
+    sc[3] = 1.0  # all equal
+    sc[4, :] = -0.0
+    sc[4, 100:200] = 0.0
+    vis = np.sort(rng.choice(P, 3000, replace=False)).astype(np.int32)
+    for k in (1, 7, 700, 2999, 3000):
+        got = ops.topk_select(torch.from_numpy(sc).cuda(), torch.from_numpy(vis).cuda(), k).cpu().numpy()
+        ref = oracle.topk_lowest(sc, vis, k)
+        assert np.array_equal(got, ref), k
+
+
+def test_compact_gather_set_and_tail(ops):
+    """Unique-valued caches (the reference's tests/test_sparse_cache_refresh.py:30-60 fixture idea)."""
+    layers, B, Hkv, capd, caps, D = 3, 2, 4, 64, 40, 8
+    n = layers * 2 * B * Hkv * capd * D
+    dense = (torch.arange(n, dtype=torch.float32) % 4093).to(torch.bfloat16).view(layers, 2, B, Hkv, capd, D).cuda()
+    sparse = torch.full((layers, 2, B, Hkv, caps, D), -7.0, dtype=torch.bfloat16, device="cuda")
+    rng = np.random.default_rng(0)
+    P, V = 50, 40
+    non_visual = np.array([0, 1] + list(range(V + 2, P)), dtype=np.int32)  # system tokens + text
+    visual = np.arange(2, V + 2)
+    K = 20
+    topk = np.stack([np.stack([np.sort(rng.choice(visual, K, replace=False)) for _ in range(Hkv)])
+                     for _ in range(layers)]).astype(np.int32)
+    b = 1
+    ops.compact_gather(dense, sparse, b, torch.from_numpy(non_visual).cuda(), torch.from_numpy(topk).cuda())
+    torch.cuda.synchronize()
+    cl = non_visual.size + K
+    sp = sparse.cpu()
+    dn = dense.cpu()
+    for l in range(layers):
+        idx = oracle.compact_indices(non_visual, topk[l])
+        for kv in range(2):
+            for h in range(Hkv):
+                assert torch.equal(sp[l, kv, b, h, :cl], dn[l, kv, b, h, torch.from_numpy(idx[h]).long()])
+                assert torch.all(sp[l, kv, b, h, cl:] == -7.0)
+                assert torch.all(sp[l, kv, 0] == -7.0)
+
+
+# ------------------------------------------------------------------ accept
+def test_accept_kernel_matches_oracle(ops):
+    from std_b200 import _lib
+
+    rng = np.random.default_rng(9)
+    B, gamma, max_new, eos = 16, 5, 12, 3
+    for trial in range(40):
+        pending = int(trial > 0 and rng.random() < 0.8)
+        ignore = int(rng.random() < 0.5)
+        nq = gamma + pending
+        tok = rng.integers(0, 6, size=(B, gamma + 1)).astype(np.int32)
+        vpred = rng.integers(0, 6, size=(B, nq)).astype(np.int32)
+        # make long accepted prefixes likely
+        for b in range(B):
+            cut = rng.integers(0, gamma + 1)
+            for i in range(cut):
+                if pending:
+                    vpred[b, i] = tok[b, 1 + i]
+                elif i > 0:
+                    vpred[b, i - 1] = tok[b, 1 + i]
+        dense_next = tok[:, 1].copy() if rng.random() < 0.7 else rng.integers(0, 6, B).astype(np.int32)
+        n_gen = rng.integers(0, max_new, B).astype(np.int32)
+        ctx = (100 + n_gen).astype(np.int32)
+        dlen = (ctx - pending).astype(np.int32)
+        slen = (40 + n_gen).astype(np.int32)
+        done = np.zeros(B, np.int32)
+        out = np.full((B, max_new), -1, np.int32)
+        stats = np.zeros((B, 4), np.int32)
+        dev = {k: torch.from_numpy(v.copy()).cuda() for k, v in dict(tok=tok, vpred=vpred, dn=dense_next, ctx=ctx,
+                                                                      dlen=dlen, slen=slen, ng=n_gen, done=done,
+                                                                      out=out, stats=stats).items()}
+        _lib.call("std_accept_commit", B, gamma, pending, dev["tok"].data_ptr(), gamma + 1, dev["vpred"].data_ptr(), nq,
+                  dev["dn"].data_ptr(), max_new, eos, ignore, dev["ctx"].data_ptr(), dev["dlen"].data_ptr(),
+                  dev["slen"].data_ptr(), dev["ng"].data_ptr(), dev["done"].data_ptr(), dev["out"].data_ptr(),
+                  dev["stats"].data_ptr(), None, 0, torch.cuda.current_stream().cuda_stream)
+        got = {k: v.cpu().numpy() for k, v in dev.items()}
+        for b in range(B):
+            remaining = max_new - int(n_gen[b])
+            propose = min(gamma, remaining)
+            acc, bonus, app, fin = oracle.accept_round(tok[b, 1:1 + propose].tolist(), vpred[b].tolist(),
+                                                       int(dense_next[b]), bool(pending), remaining, eos, bool(ignore))
+            assert got["stats"][b, 3] == acc
+            assert got["ng"][b] == n_gen[b] + len(app)
+            assert got["out"][b, n_gen[b]:n_gen[b] + len(app)].tolist() == app
+            assert got["done"][b] == int(fin)
+            if not fin:
+                nd, ns = oracle.rollback_lengths(int(dlen[b]), pending, int(slen[b]), acc)
+                assert got["dlen"][b] == nd and got["slen"][b] == ns + 1
+                assert got["tok"][b, 0] == bonus
+
+
+# ------------------------------------------------------------------ decoder ops
+def test_rmsnorm_rope_silu_argmax(ops):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    M, H = 7, 3584
+    x = (torch.randn(M, H, generator=g, device="cuda") * 3).to(torch.bfloat16)
+    w = (torch.rand(H, generator=g, device="cuda") + 0.5).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    ops.rmsnorm(x, w, 1e-6, out)
+    xf = x.float()
+    ref = w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    assert (out.float() - ref.float()).abs().max().item() <= 0.0625
+    # the row result does not depend on the row count
+    out1 = torch.empty_like(x[:1])
+    ops.rmsnorm(x[3:4].contiguous(), w, 1e-6, out1)
+    assert torch.equal(out1[0], out[3])
+
+    gu = torch.randn(5, 2 * 64, generator=g, device="cuda").to(torch.bfloat16)
+    so = torch.empty(5, 64, dtype=torch.bfloat16, device="cuda")
+    ops.silu_mul(gu, so)
+    refs = (torch.nn.functional.silu(gu[:, :64].float()).to(torch.bfloat16) * gu[:, 64:]).float()
+    assert (so.float() - refs).abs().max().item() <= 0.02
+
+    logits = torch.randn(4, 152064, generator=g, device="cuda").to(torch.bfloat16)
+    logits[2, 1000] = 50.0
+    logits[2, 500] = 50.0
+    am = torch.empty(4, dtype=torch.int32, device="cuda")
+    ops.argmax_rows(logits, am)
+    assert am.tolist() == torch.argmax(logits.float(), dim=-1).tolist()
+    assert am[2].item() == 500
+
+    # RoPE + append against the HF formula (bf16 arithmetic)
+    B, n, Hq, Hkv, D, cap = 2, 3, 28, 4, 128, 64
+    qkv = torch.randn(B * n, (Hq + 2 * Hkv) * D, generator=g, device="cuda").to(torch.bfloat16)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.int64).float() / D))
+    pos = torch.arange(256).float()[:, None] * inv[None, :]
+    cos_t = pos.cos().to(torch.bfloat16).cuda()
+    sin_t = pos.sin().to(torch.bfloat16).cuda()
+    pb = torch.tensor([10, 20], dtype=torch.int32, device="cuda")
+    sb = torch.tensor([5, 7], dtype=torch.int32, device="cuda")
+    q_out = torch.empty(B * n, Hq, D, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(B, Hkv, cap, D, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    ops.rope_append(qkv, B, n, Hq, Hkv, D, pb, 1, sb, 2, cos_t, sin_t, q_out, kc, vc)
+    for b in range(B):
+        for j in range(n):
+            r = b * n + j
+            p_ = int(pb[b]) + 1 + j
+            c = torch.cat([cos_t[p_], cos_t[p_]])
+            s = torch.cat([sin_t[p_], sin_t[p_]])
+            qh = qkv[r, : Hq * D].view(Hq, D)
+            rot = torch.cat([-qh[:, D // 2:], qh[:, : D // 2]], dim=-1)
+            ref_q = qh * c + rot * s
+            assert torch.equal(q_out[r], ref_q)
+            kh = qkv[r, Hq * D:(Hq + Hkv) * D].view(Hkv, D)
+            rotk = torch.cat([-kh[:, D // 2:], kh[:, : D // 2]], dim=-1)
+            slot = int(sb[b]) + 2 + j
+            assert torch.equal(kc[b, :, slot], kh * c + rotk * s)
+            assert torch.equal(vc[b, :, slot], qkv[r, (Hq + Hkv) * D:].view(Hkv, D))
+    _no_device_error(ops)
