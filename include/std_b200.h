@@ -152,11 +152,15 @@ int std_accept_commit(int B, int gamma, int pending, int32_t* tok, int tok_strid
                       int32_t* dense_len, int32_t* sparse_len, int32_t* n_gen, int32_t* done, int32_t* out_tokens,
                       int32_t* stats, int32_t* accept_hist, int hist_cap, void* stream);
 
-/* AR bookkeeping (std_qwen25vl.py:584-590): record tok[b][0] as generated. */
+/* AR bookkeeping (std_qwen25vl.py:584-590).  std_ar_commit records
+ * tok[b][0] as the next generated token of each running request and sets
+ * active[b]; the step's forward writes its argmax to next_tok[b];
+ * std_ar_advance then, for active requests, advances dense_len and ctx_len by
+ * one and moves next_tok[b] into tok[b][0].  Finished requests stay frozen. */
 int std_ar_commit(int B, int tok_stride, int max_new, int eos, int ignore_eos, const int32_t* tok, int32_t* n_gen,
-                  int32_t* done, int32_t* out_tokens, void* stream);
-/* AR bookkeeping: dense_len[b] += 1 after the step's forward. */
-int std_ar_advance(int B, int32_t* dense_len, void* stream);
+                  int32_t* done, int32_t* out_tokens, int32_t* active, void* stream);
+int std_ar_advance(int B, const int32_t* active, const int32_t* next_tok, int32_t* tok, int tok_stride,
+                   int32_t* dense_len, int32_t* ctx_len, void* stream);
 
 #ifdef __cplusplus
 }

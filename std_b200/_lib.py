@@ -47,8 +47,8 @@ SIGNATURES: Dict[str, tuple] = {
     "std_argmax_rows": (I, [P, I, I, I, I, I, PI32, P]),
     "std_accept_commit": (I, [I, I, I, PI32, I, PI32, I, PI32, I, I, I, PI32, PI32, PI32, PI32, PI32, PI32, PI32,
                               PI32, I, P]),
-    "std_ar_commit": (I, [I, I, I, I, I, PI32, PI32, PI32, PI32, P]),
-    "std_ar_advance": (I, [I, PI32, P]),
+    "std_ar_commit": (I, [I, I, I, I, I, PI32, PI32, PI32, PI32, PI32, P]),
+    "std_ar_advance": (I, [I, PI32, PI32, PI32, I, PI32, PI32, P]),
 }
 
 _STATUS = {1: "bad shape or argument", 2: "capacity exceeded", 3: "unsupported device or driver entry point",

@@ -258,13 +258,21 @@ __global__ void accept_commit_kernel(const AcceptParams p) {
   p.tok[static_cast<size_t>(b) * p.tok_stride] = bonus;
 }
 
-// AR step bookkeeping (std_qwen25vl.py:584-590): record cur (= tok[b][0]) as
-// generated; the following forward appends its KV at dense_len and writes the
-// next argmax into tok[b][0]; advance_ar then moves dense_len on.
+// AR step bookkeeping (std_qwen25vl.py:584-590).  ar_commit records cur =
+// tok[b][0] as generated (active[b] = request still running before this
+// step); the step's forward then appends cur's KV at dense_len and writes its
+// argmax into next_tok[b]; ar_advance moves dense_len on and makes next_tok
+// the new cur, for requests that were active.  A finished request's state is
+// frozen, so a batch can keep stepping until its last request finishes.
 __global__ void ar_commit_kernel(int B, int tok_stride, int max_new, int eos, int ignore_eos, const int32_t* tok,
-                                 int32_t* n_gen, int32_t* done, int32_t* out_tokens) {
+                                 int32_t* n_gen, int32_t* done, int32_t* out_tokens, int32_t* active) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B || done[b]) return;
+  if (b >= B) return;
+  if (done[b]) {
+    active[b] = 0;
+    return;
+  }
+  active[b] = 1;
   const int ng = n_gen[b];
   const int t = tok[static_cast<size_t>(b) * tok_stride];
   out_tokens[static_cast<size_t>(b) * max_new + ng] = t;
@@ -272,11 +280,13 @@ __global__ void ar_commit_kernel(int B, int tok_stride, int max_new, int eos, in
   if ((!ignore_eos && t == eos) || ng + 1 >= max_new) done[b] = 1;
 }
 
-__global__ void ar_advance_kernel(int B, const int32_t* done_before, int32_t* dense_len) {
+__global__ void ar_advance_kernel(int B, const int32_t* active, const int32_t* next_tok, int32_t* tok, int tok_stride,
+                                  int32_t* dense_len, int32_t* ctx_len) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
-  (void)done_before;
+  if (b >= B || !active[b]) return;
   dense_len[b] += 1;
+  ctx_len[b] += 1;
+  tok[static_cast<size_t>(b) * tok_stride] = next_tok[b];
 }
 
 }  // namespace stdb
@@ -383,14 +393,18 @@ extern "C" int std_accept_commit(int B, int gamma, int pending, int32_t* tok, in
 }
 
 extern "C" int std_ar_commit(int B, int tok_stride, int max_new, int eos, int ignore_eos, const int32_t* tok,
-                             int32_t* n_gen, int32_t* done, int32_t* out_tokens, void* stream) {
-  stdb::ar_commit_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(B, tok_stride, max_new, eos,
-                                                                                         ignore_eos, tok, n_gen, done,
-                                                                                         out_tokens);
+                             int32_t* n_gen, int32_t* done, int32_t* out_tokens, int32_t* active, void* stream) {
+  if (B <= 0 || tok_stride <= 0 || max_new <= 0) return 1;
+  stdb::ar_commit_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      B, tok_stride, max_new, eos, ignore_eos, tok, n_gen, done, out_tokens, active);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
 
-extern "C" int std_ar_advance(int B, int32_t* dense_len, void* stream) {
-  stdb::ar_advance_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(B, nullptr, dense_len);
+extern "C" int std_ar_advance(int B, const int32_t* active, const int32_t* next_tok, int32_t* tok, int tok_stride,
+                              int32_t* dense_len, int32_t* ctx_len, void* stream) {
+  if (B <= 0 || tok_stride <= 0) return 1;
+  stdb::ar_advance_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(B, active, next_tok, tok,
+                                                                                          tok_stride, dense_len,
+                                                                                          ctx_len);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

@@ -1,0 +1,501 @@
+"""Sparse-to-Dense (STD) and AR greedy decoding on B200 -- the public API.
+
+Keeps the reference's entry points and result types (std_qwen25vl.py):
+  ar_generate_qwen25vl   (:553-606)   vanilla greedy decoding, the oracle STD must equal
+  std_generate_qwen25vl  (:609-978)   STD: sparse drafting, parallel dense verify
+  build_sparse_selection (:175-231)   per-layer / per-KV-head top-K visual selection
+  compact_sparse_prompt_cache (:265-298)
+  SparseSelection (:41-50), GenerateResult (:53-89), generated_suffix / tokens_equal (:981-986)
+
+What changes is underneath: both caches live on the device with device-resident
+lengths ([layers, 2, B, Hkv, cap, D] bf16), selection/compaction/attention/
+acceptance run as libstd_b200.so kernels, and a whole STD round (gamma draft
+steps, the dense verify, the fused accept/rollback, the bonus sparse step) is
+one CUDA graph; the host reads one 4-byte "all done" flag per round instead of
+gamma+1 .item() syncs.  Requests are batched (the reference is batch 1): every
+request keeps its own lengths and finishes independently.
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import ops
+from .model import Qwen25VLDecoder, Workspace, decode_forward, prefill_request
+
+SPARSE_ATTN_MODES = ("b200",)
+VERIFY_MODES = ("parallel",)
+
+
+@dataclass
+class SparseSelection:
+    """Per-layer sparse visual KV choices (std_qwen25vl.py:41-50)."""
+
+    topk_positions: List[torch.Tensor]   # per layer [Hkv, k] int64 (CPU), ascending
+    non_visual_positions: torch.Tensor   # [NV] int64 (CPU)
+    prompt_len: int
+    visual_len: int
+    text_len: int
+    k: int
+
+
+@dataclass
+class GenerateResult:
+    """Same fields as the reference's GenerateResult (std_qwen25vl.py:53-89)."""
+
+    output_ids: torch.Tensor
+    decoding_time: float
+    inference_time: float
+    generate_len: int
+    accepted_draft_tokens: int = 0
+    proposed_draft_tokens: int = 0
+    mean_accept_length: float = 0.0
+    decode_rounds: int = 0
+    final_gamma: int = 0
+    fallback_count: int = 0
+    fallback_accepted_extra: int = 0
+    verify_margin_reruns: int = 0
+    min_verify_margin: float = 0.0
+    gamma_history: List[int] = field(default_factory=list)
+    proposed_lengths: List[int] = field(default_factory=list)
+    accept_lengths: List[int] = field(default_factory=list)
+    pending_lengths: List[int] = field(default_factory=list)
+    draft_time: float = 0.0
+    verify_time: float = 0.0
+    bonus_time: float = 0.0
+    cache_adjust_time: float = 0.0
+    cache_init_time: float = 0.0
+    prefill_time: float = 0.0
+    selection_prefill_time: float = 0.0
+    selection_time: float = 0.0
+    dense_prefill_time: float = 0.0
+    sparse_cache_time: float = 0.0
+
+    @property
+    def acceptance_rate(self) -> float:
+        if self.proposed_draft_tokens == 0:
+            return 0.0
+        return self.accepted_draft_tokens / self.proposed_draft_tokens
+
+
+def generated_suffix(output_ids: torch.Tensor, prompt_len: int) -> torch.Tensor:
+    return output_ids[:, prompt_len:]
+
+
+def tokens_equal(a: torch.Tensor, b: torch.Tensor) -> bool:
+    return a.shape == b.shape and bool(torch.equal(a.detach().cpu(), b.detach().cpu()))
+
+
+def get_last_video_idx(input_ids: Sequence[int], video_token_id: int) -> int:
+    """Last position of video_token_id, or -1 (utils.py:8-15)."""
+    for i in range(len(input_ids) - 1, -1, -1):
+        if int(input_ids[i]) == video_token_id:
+            return i
+    return -1
+
+
+def selection_budget(prompt_len: int, text_start: int, visual_len: int, target_k_plus_text: int,
+                     explicit_k: Optional[int]) -> int:
+    """k = K+text - text_len, clamped to [1, visual_len] (std_qwen25vl.py:190-195)."""
+    text_len = max(1, prompt_len - int(text_start))
+    k = int(explicit_k) if explicit_k is not None else max(1, int(target_k_plus_text) - text_len)
+    return min(k, int(visual_len))
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+@dataclass
+class PromptLayout:
+    prompt_len: int
+    text_start: int
+    visual_pos: torch.Tensor     # [V] int32 device, ascending
+    non_visual: torch.Tensor     # [NV] int32 device, ascending
+
+    @staticmethod
+    def from_ids(ids: torch.Tensor, video_token_id: int, device) -> "PromptLayout":
+        ids_cpu = ids.detach().cpu().view(-1)
+        last = get_last_video_idx(ids_cpu.tolist(), video_token_id)
+        if last < 0:
+            raise ValueError("No video token found in the prompt; STD visual KV selection requires video input.")
+        vis = torch.nonzero(ids_cpu == video_token_id).flatten().to(torch.int32)
+        nv = torch.nonzero(ids_cpu != video_token_id).flatten().to(torch.int32)
+        return PromptLayout(int(ids_cpu.numel()), last + 1, vis.to(device), nv.to(device))
+
+
+def initialize_past_key_values(model: Qwen25VLDecoder, batch_size: int, max_cache_len: int) -> torch.Tensor:
+    """One preallocated cache [layers, 2, B, Hkv, cap, D] (kv_cache.py:72-165)."""
+    c = model.config
+    return torch.zeros(c.num_hidden_layers, 2, batch_size, c.num_key_value_heads, max_cache_len, c.head_dim,
+                       device=model.device, dtype=model.dtype)
+
+
+def build_sparse_selection(scores: torch.Tensor, layout: PromptLayout, k: int) -> torch.Tensor:
+    """scores [layers, Hkv, P] fp32 -> top-k visual positions [layers, Hkv, k] int32 (device).
+
+    std_qwen25vl.py:204-222 on the device, ties to the lowest position."""
+    layers, Hkv, P = scores.shape
+    return ops.topk_select(scores.view(layers * Hkv, P), layout.visual_pos, k).view(layers, Hkv, k)
+
+
+def compact_sparse_prompt_cache(dense_cache: torch.Tensor, sparse_cache: torch.Tensor, b: int, layout: PromptLayout,
+                                topk: torch.Tensor) -> int:
+    """Gather sorted(non_visual U topk[layer, head]) rows of request b into the
+    sparse cache (std_qwen25vl.py:265-298); returns compact_len."""
+    ops.compact_gather(dense_cache, sparse_cache, b, layout.non_visual, topk)
+    return int(layout.non_visual.numel() + topk.shape[-1])
+
+
+class STDRunner:
+    """Device state, caches and CUDA graphs for one batch of same-length requests."""
+
+    def __init__(self, model: Qwen25VLDecoder, batch_size: int, layout: PromptLayout, max_new_tokens: int,
+                 gamma: int = 9, k: int = 896, eos_token_id: int = -1, ignore_eos: bool = False,
+                 use_graphs: bool = True):
+        c = model.config
+        if gamma < 1 or 7 * (gamma + 1) > 126:
+            raise ValueError("gamma must be in [1, 17]")
+        self.model, self.B, self.layout = model, batch_size, layout
+        self.gamma, self.k, self.max_new = gamma, k, max_new_tokens
+        self.eos, self.ignore_eos, self.use_graphs = eos_token_id, ignore_eos, use_graphs
+        P = layout.prompt_len
+        self.compact_len = int(layout.non_visual.numel()) + k
+        self.cap_d = _round_up(P + max_new_tokens + gamma + 2, 128)
+        self.cap_s = _round_up(self.compact_len + max_new_tokens + gamma + 2, 64)
+        dev = model.device
+        self.dense = initialize_past_key_values(model, batch_size, self.cap_d)
+        self.sparse = initialize_past_key_values(model, batch_size, self.cap_s)
+        model.rope_tables(self.cap_d + 2)
+        self.dense_rows = _round_up(batch_size * (gamma + 1), 16)
+        self.ws = Workspace(model, max(self.dense_rows, batch_size))
+        B = batch_size
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.tok_stride = gamma + 2
+        self.tok = torch.zeros(B, self.tok_stride, **i32)
+        self.vpred = torch.zeros(B, gamma + 1, **i32)
+        self.ctx_len = torch.zeros(B, **i32)
+        self.dense_len = torch.zeros(B, **i32)
+        self.sparse_len = torch.zeros(B, **i32)
+        self.n_gen = torch.zeros(B, **i32)
+        self.done = torch.zeros(B, **i32)
+        self.active = torch.zeros(B, **i32)
+        self.next_tok = torch.zeros(B, **i32)
+        self.dense_next = torch.zeros(B, **i32)
+        self.out_tokens = torch.zeros(B, max_new_tokens, **i32)
+        self.stats = torch.zeros(B, 4, **i32)
+        self.hist_cap = max_new_tokens + 1
+        self.accept_hist = torch.zeros(B, self.hist_cap, **i32)
+        self.all_done = torch.zeros(1, **i32)
+        self.all_done_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.topk = torch.zeros(c.num_hidden_layers, c.num_key_value_heads, k, **i32)
+        self.topk_per_request: List[torch.Tensor] = []
+        self._graphs: Dict[str, torch.cuda.CUDAGraph] = {}
+        self.prefill_done = False
+
+    # ------------------------------------------------------------------ prefill
+    def prefill(self, embeds: Sequence[torch.Tensor], with_selection: bool = True) -> Dict[str, float]:
+        """Prefill every request (embeds[b]: [P, H] bf16) and, for STD, select and compact."""
+        c = self.model.config
+        L, Hkv, P = c.num_hidden_layers, c.num_key_value_heads, self.layout.prompt_len
+        t = {"prefill_time": 0.0, "selection_time": 0.0, "sparse_cache_time": 0.0}
+        scores = torch.empty(L, Hkv, P, dtype=torch.float32, device=self.model.device) if with_selection else None
+        self.topk_per_request = []
+        dn = []
+        for b in range(self.B):
+            torch.cuda.synchronize()
+            t0 = time.time()
+            dn.append(prefill_request(self.model, self.dense, b, embeds[b], self.layout.text_start, scores))
+            torch.cuda.synchronize()
+            t1 = time.time()
+            t["prefill_time"] += t1 - t0
+            if with_selection:
+                topk = build_sparse_selection(scores, self.layout, self.k)
+                torch.cuda.synchronize()
+                t2 = time.time()
+                compact_sparse_prompt_cache(self.dense, self.sparse, b, self.layout, topk)
+                torch.cuda.synchronize()
+                t["selection_time"] += t2 - t1
+                t["sparse_cache_time"] += time.time() - t2
+                self.topk_per_request.append(topk.clone())
+        self.dense_next.copy_(torch.tensor(dn, dtype=torch.int32))
+        self.prefill_done = True
+        return t
+
+    # ------------------------------------------------------------------ state
+    def reset(self) -> None:
+        P = self.layout.prompt_len
+        self.ctx_len.fill_(P)
+        self.dense_len.fill_(P)
+        self.sparse_len.fill_(self.compact_len)
+        self.n_gen.zero_()
+        self.done.zero_()
+        self.active.zero_()
+        self.stats.zero_()
+        self.accept_hist.zero_()
+        self.out_tokens.zero_()
+        self.tok.zero_()
+        self.tok[:, 0] = self.dense_next   # AR: current token
+        self.tok[:, 1] = self.dense_next   # STD: sparse_next = dense_next (copy_sparse_prefill)
+        self.all_done.zero_()
+
+    # ------------------------------------------------------------------ steps
+    def _draft_step(self, i: int) -> None:
+        last = i == self.gamma - 1
+        decode_forward(self.model, self.ws, self.sparse, B=self.B, n=1, rows=self.B, tok=self.tok, tok_start=1 + i,
+                       pos_base=self.ctx_len, pos_off=i, slot_base=self.sparse_len, slot_off=i,
+                       lens=self.sparse_len, len_offset=i + 1, sparse=True,
+                       argmax_out=None if last else self.tok.view(-1), argmax_stride=self.tok_stride,
+                       argmax_start=2 + i)
+
+    def _verify(self, pending: int) -> None:
+        nq = self.gamma + pending
+        decode_forward(self.model, self.ws, self.dense, B=self.B, n=nq, rows=self.dense_rows, tok=self.tok,
+                       tok_start=1 - pending, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len,
+                       slot_off=0, lens=self.dense_len, len_offset=nq, sparse=False, argmax_out=self.vpred.view(-1),
+                       argmax_stride=self.gamma + 1, argmax_start=0)
+
+    def _accept(self, pending: int) -> None:
+        from . import _lib
+
+        _lib.call("std_accept_commit", self.B, self.gamma, pending, self.tok.data_ptr(), self.tok_stride,
+                  self.vpred.data_ptr(), self.gamma + 1, self.dense_next.data_ptr(), self.max_new, self.eos,
+                  1 if self.ignore_eos else 0, self.ctx_len.data_ptr(), self.dense_len.data_ptr(),
+                  self.sparse_len.data_ptr(), self.n_gen.data_ptr(), self.done.data_ptr(),
+                  self.out_tokens.data_ptr(), self.stats.data_ptr(), self.accept_hist.data_ptr(), self.hist_cap,
+                  torch.cuda.current_stream().cuda_stream)
+
+    def _bonus_step(self) -> None:
+        decode_forward(self.model, self.ws, self.sparse, B=self.B, n=1, rows=self.B, tok=self.tok, tok_start=0,
+                       pos_base=self.ctx_len, pos_off=-1, slot_base=self.sparse_len, slot_off=-1,
+                       lens=self.sparse_len, len_offset=0, sparse=True, argmax_out=self.tok.view(-1),
+                       argmax_stride=self.tok_stride, argmax_start=1)
+
+    def std_round(self, first: bool) -> None:
+        pending = 0 if first else 1
+        for i in range(self.gamma):
+            self._draft_step(i)
+        self._verify(pending)
+        self._accept(pending)
+        self._bonus_step()
+        torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
+
+    def ar_step(self) -> None:
+        from . import _lib
+
+        s = torch.cuda.current_stream().cuda_stream
+        _lib.call("std_ar_commit", self.B, self.tok_stride, self.max_new, self.eos, 1 if self.ignore_eos else 0,
+                  self.tok.data_ptr(), self.n_gen.data_ptr(), self.done.data_ptr(), self.out_tokens.data_ptr(),
+                  self.active.data_ptr(), s)
+        decode_forward(self.model, self.ws, self.dense, B=self.B, n=1, rows=self.dense_rows, tok=self.tok,
+                       tok_start=0, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len, slot_off=0,
+                       lens=self.dense_len, len_offset=1, sparse=False, argmax_out=self.next_tok)
+        _lib.call("std_ar_advance", self.B, self.active.data_ptr(), self.next_tok.data_ptr(), self.tok.data_ptr(),
+                  self.tok_stride, self.dense_len.data_ptr(), self.ctx_len.data_ptr(), s)
+        torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
+
+    # ------------------------------------------------------------------ graphs
+    def capture(self) -> None:
+        """Capture the round-1, steady-state and AR-step graphs.
+
+        Each step runs once eagerly first (allocating workspaces and setting
+        kernel attributes outside capture); state is reset afterwards."""
+        if not self.use_graphs:
+            return
+        steps = (("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False)),
+                 ("ar", self.ar_step))
+        for name, fn in steps:
+            if name in self._graphs:
+                continue
+            self.reset()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            self.reset()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            self._graphs[name] = g
+        self.reset()
+        torch.cuda.synchronize()
+
+    def _all_done(self) -> bool:
+        self.all_done_host.copy_(self.all_done, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return bool(self.all_done_host.item())
+
+    # ------------------------------------------------------------------ loops
+    def run_std(self) -> float:
+        """STD decode of every request from the post-prefill state; returns seconds (device time)."""
+        self.capture()
+        self.reset()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        self._replay_or_run("std_first", lambda: self.std_round(True))
+        rounds = 1
+        while not self._all_done():
+            if rounds > self.max_new + 1:
+                raise RuntimeError("STD decode did not terminate")
+            self._replay_or_run("std", lambda: self.std_round(False))
+            rounds += 1
+        end.record()
+        end.synchronize()
+        return start.elapsed_time(end) / 1000.0
+
+    def run_ar(self) -> float:
+        self.capture()
+        self.reset()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        steps = 0
+        while True:
+            self._replay_or_run("ar", self.ar_step)
+            steps += 1
+            if steps >= self.max_new:
+                if self._all_done():
+                    break
+            elif steps % 16 == 0 and self._all_done():
+                break
+        end.record()
+        end.synchronize()
+        return start.elapsed_time(end) / 1000.0
+
+    def _replay_or_run(self, name: str, fn) -> None:
+        g = self._graphs.get(name)
+        if g is not None:
+            g.replay()
+        else:
+            fn()
+
+    # ------------------------------------------------------------------ results
+    def generated(self) -> torch.Tensor:
+        return self.out_tokens[:, : int(self.n_gen.max().item())].to(torch.int64).cpu()
+
+    def std_stats(self) -> Dict[str, object]:
+        st = self.stats.cpu()
+        hist = self.accept_hist.cpu()
+        rounds = st[:, 0].tolist()
+        return {
+            "rounds": rounds,
+            "accepted": st[:, 1].tolist(),
+            "proposed": st[:, 2].tolist(),
+            "accept_lengths": [hist[b, : rounds[b]].tolist() for b in range(self.B)],
+        }
+
+
+# ----------------------------------------------------------------------------
+# reference-shaped entry points
+# ----------------------------------------------------------------------------
+
+def _prepare(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor], video_token_id: int):
+    ids = inputs["input_ids"]
+    if ids.dim() == 1:
+        ids = ids.view(1, -1)
+    B, P = ids.shape
+    layout = PromptLayout.from_ids(ids[0], video_token_id, model.device)
+    for b in range(1, B):
+        if not torch.equal((ids[b] == video_token_id).cpu(), (ids[0] == video_token_id).cpu()):
+            raise ValueError("all requests of a batch must share the video/text layout")
+    vis = inputs["visual_embeds"]
+    if vis.dim() == 2:
+        vis = vis.unsqueeze(0)
+    ids_dev = ids.to(model.device, non_blocking=True)
+    vis_dev = vis.to(model.device, non_blocking=True)
+    embeds = []
+    vpos = layout.visual_pos.long()
+    for b in range(B):
+        e = model.embed[ids_dev[b].clamp(0, model.config.vocab_size - 1)]
+        e[vpos] = vis_dev[b].to(model.dtype)
+        embeds.append(e)
+    return ids, layout, embeds
+
+
+@torch.inference_mode()
+def ar_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor], video_token_id: int,
+                         eos_token_id: int, max_new_tokens: int = 256, output_attentions: bool = False,
+                         profile_prefill: bool = False, ignore_eos: bool = False,
+                         runner: Optional[STDRunner] = None) -> GenerateResult:
+    """Vanilla greedy decoding with the same two-stage prefill as STD (std_qwen25vl.py:553-606).
+
+    inputs: {"input_ids": [B, P], "visual_embeds": [B, V, H]} -- the visual
+    rows replace the embeddings of the video-token positions (the vision tower
+    is outside this path)."""
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ids, layout, embeds = _prepare(model, inputs, video_token_id)
+    if runner is None:
+        runner = STDRunner(model, ids.shape[0], layout, max_new_tokens, gamma=9, k=1, eos_token_id=eos_token_id,
+                           ignore_eos=ignore_eos)
+    tp = runner.prefill(embeds, with_selection=False)
+    dec = runner.run_ar()
+    torch.cuda.synchronize()
+    gen = runner.generated()
+    out = torch.cat([ids.cpu().long(), gen], dim=1) if ids.shape[0] == gen.shape[0] else gen
+    return GenerateResult(out, dec, time.time() - t0, int(runner.n_gen.sum().item()),
+                          prefill_time=tp["prefill_time"])
+
+
+@torch.inference_mode()
+def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor], video_token_id: int,
+                          eos_token_id: int, max_new_tokens: int = 256, gamma: int = 9,
+                          target_k_plus_text: int = 1024, explicit_k: Optional[int] = None,
+                          verify_mode: str = "parallel", verify_fallback: str = "none",
+                          sequential_fallback_max_accept: int = 1, profile_decode: bool = False,
+                          sparse_attn_mode: str = "b200", adaptive_gamma_min: Optional[int] = None,
+                          adaptive_gamma_mode: str = "accept_len", copy_sparse_prefill: bool = True,
+                          profile_prefill: bool = False, verify_attn_backend: str = "default",
+                          verify_margin_threshold: Optional[float] = None, use_compile: bool = False,
+                          ignore_eos: bool = False,
+                          runner: Optional[STDRunner] = None) -> Tuple[GenerateResult, SparseSelection]:
+    """Sparse-to-Dense greedy decoding (std_qwen25vl.py:609-978).
+
+    Implemented: verify_mode="parallel", verify_fallback="none",
+    sparse_attn_mode="b200", copy_sparse_prefill=True, fixed gamma.  Other
+    values of the reference's research flags raise ValueError (there is no
+    alternative backend to dispatch to)."""
+    if verify_mode not in VERIFY_MODES:
+        raise ValueError(f"Unsupported verify_mode={verify_mode!r}; this build implements 'parallel'.")
+    if verify_fallback != "none":
+        raise ValueError("verify_fallback other than 'none' is not part of the B200 path.")
+    if sparse_attn_mode not in SPARSE_ATTN_MODES:
+        raise ValueError(f"Unsupported sparse_attn_mode={sparse_attn_mode!r}; expected 'b200'.")
+    if adaptive_gamma_min is not None or use_compile or not copy_sparse_prefill:
+        raise ValueError("adaptive gamma, torch.compile and a separate sparse prefill are not part of the B200 path.")
+    if verify_attn_backend != "default":
+        raise ValueError("verify_attn_backend must be 'default' (the verify kernel is the only backend).")
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ids, layout, embeds = _prepare(model, inputs, video_token_id)
+    k = selection_budget(layout.prompt_len, layout.text_start, int(layout.visual_pos.numel()), target_k_plus_text,
+                         explicit_k)
+    if runner is None:
+        runner = STDRunner(model, ids.shape[0], layout, max_new_tokens, gamma=gamma, k=k, eos_token_id=eos_token_id,
+                           ignore_eos=ignore_eos)
+    tp = runner.prefill(embeds, with_selection=True)
+    dec = runner.run_std()
+    torch.cuda.synchronize()
+    gen = runner.generated()
+    out = torch.cat([ids.cpu().long(), gen], dim=1) if ids.shape[0] == gen.shape[0] else gen
+    st = runner.std_stats()
+    acc = st["accept_lengths"][0]
+    result = GenerateResult(
+        output_ids=out, decoding_time=dec, inference_time=time.time() - t0, generate_len=int(runner.n_gen.sum().item()),
+        accepted_draft_tokens=int(sum(st["accepted"])), proposed_draft_tokens=int(sum(st["proposed"])),
+        mean_accept_length=(sum(acc) / len(acc)) if acc else 0.0, decode_rounds=int(max(st["rounds"])),
+        final_gamma=gamma, accept_lengths=acc, prefill_time=tp["prefill_time"], selection_time=tp["selection_time"],
+        sparse_cache_time=tp["sparse_cache_time"])
+    topk0 = runner.topk_per_request[0].cpu().long()
+    selection = SparseSelection(topk_positions=[topk0[l] for l in range(topk0.shape[0])],
+                                non_visual_positions=layout.non_visual.cpu().long(), prompt_len=layout.prompt_len,
+                                visual_len=int(layout.visual_pos.numel()),
+                                text_len=max(1, layout.prompt_len - layout.text_start), k=k)
+    return result, selection

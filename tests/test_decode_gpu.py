@@ -1,0 +1,76 @@
+"""GPU end to end: STD greedy output == AR greedy output, token for token.
+
+A tiny decoder with the 7B's head geometry (7 query heads per KV head,
+head_dim 128) runs the full path: two-stage prefill with the selection branch,
+device top-K, compaction, CUDA-graph STD rounds and AR steps.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+VIDEO = 7
+
+
+def _inputs(B, V, T, vocab, H, seed):
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(10, vocab, (B, V + T), generator=g)
+    ids[:, :V] = VIDEO
+    vis = torch.randn(B, V, H, generator=g).to(torch.bfloat16)
+    return {"input_ids": ids, "visual_embeds": vis}
+
+
+@pytest.mark.parametrize("B,gamma,kpt,max_new,ignore_eos", [(1, 4, 100, 40, True), (3, 9, 80, 33, True),
+                                                            (2, 5, 120, 30, False)])
+def test_std_equals_ar(B, gamma, kpt, max_new, ignore_eos):
+    from std_b200 import ops
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import PromptLayout, STDRunner, selection_budget
+
+    model = Qwen25VLDecoder(TINY, seed=2)
+    V, T = 600, 40
+    inp = _inputs(B, V, T, TINY.vocab_size, TINY.hidden_size, seed=B)
+    from std_b200.std_qwen25vl import _prepare
+
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    k = selection_budget(layout.prompt_len, layout.text_start, V, kpt, None)
+    eos = int(ids[0, -1]) if not ignore_eos else -1
+    runner = STDRunner(model, B, layout, max_new, gamma=gamma, k=k, eos_token_id=eos, ignore_eos=ignore_eos)
+    runner.prefill(embeds, with_selection=True)
+    t_std = runner.run_std()
+    std_tokens = runner.out_tokens.cpu().clone()
+    std_n = runner.n_gen.cpu().clone()
+    st = runner.std_stats()
+    t_ar = runner.run_ar()
+    ar_tokens = runner.out_tokens.cpu().clone()
+    ar_n = runner.n_gen.cpu().clone()
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert torch.equal(std_n, ar_n)
+    for b in range(B):
+        n = int(std_n[b])
+        assert std_tokens[b, :n].tolist() == ar_tokens[b, :n].tolist(), f"request {b}"
+        if ignore_eos:
+            assert n == max_new
+        assert sum(st["accept_lengths"][b]) == st["accepted"][b]
+    assert t_std > 0 and t_ar > 0
+
+
+def test_public_api_and_selection():
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import ar_generate_qwen25vl, std_generate_qwen25vl, tokens_equal
+
+    model = Qwen25VLDecoder(TINY, seed=3)
+    inp = _inputs(1, 500, 24, TINY.vocab_size, TINY.hidden_size, seed=9)
+    std, sel = std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, max_new_tokens=24, gamma=9,
+                                     target_k_plus_text=88, ignore_eos=True)
+    ar = ar_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, max_new_tokens=24, ignore_eos=True)
+    assert tokens_equal(std.output_ids, ar.output_ids)
+    assert sel.k == 88 - 24 and len(sel.topk_positions) == TINY.num_hidden_layers
+    for tk in sel.topk_positions:
+        assert tk.shape == (1, sel.k)
+        assert torch.all(tk[:, 1:] > tk[:, :-1]) and int(tk.max()) < 500
+    assert std.generate_len == 24 and std.decode_rounds >= 1
+    with pytest.raises(ValueError):
+        std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, verify_mode="sequential")
