@@ -1,0 +1,391 @@
+#!/usr/bin/env python
+"""bench.py -- STD (sparse-to-dense) decode throughput on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference] [--workload config4|config2|config3]
+
+One step = STD greedy decoding of `max_new_tokens` new tokens for every request
+of this GPU's group, from the post-prefill state (the metric counts decode
+time only, like the reference's decoding_time, std_qwen25vl.py:762-763, :942).
+The prefill, selection and compaction run once before timing; each step
+resets the device-resident lengths (the cached prompt rows are never written
+by decoding), so every step repeats the same work.
+
+Default workload = BASELINE configs[4]: random-init Qwen2.5-VL-7B-shaped
+decoder (bf16, weights seed 2), 8 requests per GPU, each 32768 visual tokens
+(64 frames x 512, embeddings N(0,1)) + 128 text ids U[0,151643) (request seeds
+100 + global index), K+text = 1024, gamma = 9, 128 new tokens, ignore_eos.
+Requests are data-parallel: rank r decodes requests 8r..8r+7 with no
+collective on the hot path (weak scaling).
+
+Rank 0 prints one JSON line.  --impl reference times the reference's decode
+algorithm restated on the host cores (oracle/decoder.py, numpy fp32) -- the
+reference itself is Python and cannot travel to the GPU box.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+METRIC = "STD generated tokens/sec per GPU & per box (1/2/4/8 B200); draft-attn HBM GB/s"
+VIDEO_TOKEN_ID = 151656
+
+WORKLOADS = {
+    "config4": dict(batch=8, visual=32768, text=128, k_plus_text=1024, gamma=9, max_new=128,
+                    desc="configs[4]: 8 requests/GPU x (32768 visual (64x512) + 128 text), K+text=1024, gamma=9, "
+                         "128 new tokens, request groups data-parallel"),
+    "config2": dict(batch=1, visual=16384, text=128, k_plus_text=1024, gamma=9, max_new=128,
+                    desc="configs[2]: 1 request x (16384 visual (32x512) + 128 text), K+text=1024, gamma=9, "
+                         "128 new tokens"),
+    "config3": dict(batch=1, visual=131072, text=128, k_plus_text=4096, gamma=9, max_new=128,
+                    desc="configs[3]: 1 request x (131072 visual (256x512) + 128 text), K+text=4096, gamma=9, "
+                         "128 new tokens, unsharded"),
+}
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config4")
+    ap.add_argument("--gamma", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=None, help="requests per GPU")
+    ap.add_argument("--max-new", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ar", action="store_true")
+    return ap.parse_args()
+
+
+def _workload(a):
+    w = dict(WORKLOADS[a.workload])
+    if a.gamma is not None:
+        w["gamma"] = a.gamma
+    if a.batch is not None:
+        w["batch"] = a.batch
+    if a.max_new is not None:
+        w["max_new"] = a.max_new
+    w["prompt"] = w["visual"] + w["text"]
+    w["k"] = min(max(1, w["k_plus_text"] - w["text"]), w["visual"])
+    w["compact"] = w["text"] + w["k"]
+    return w
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_id: str):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", device_id,
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- reference arm
+def reference_arm(a, w, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    from oracle.decoder import run_cpu_std
+
+    r = run_cpu_std(rounds=a.steps, warmup=a.warmup, L_dense=w["prompt"], L_sparse=w["compact"],
+                    max_new=w["max_new"], gamma=w["gamma"])
+    value = r["tokens"] / r["seconds"]
+    sample = (f"{a.steps} STD rounds (gamma={w['gamma']}) of one request at the workload's shapes "
+              f"(dense cache {w['prompt']}, sparse cache {w['compact']}), numpy fp32, 28 layers sharing one "
+              f"weight set, synthetic cache state")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1000.0 * r["seconds"] / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w["desc"], "requests_per_gpu": w["batch"]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["cores"], "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "accept_lengths": r["accepts"],
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- B200 arm
+def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
+    import torch
+
+    from std_b200 import ops
+    from std_b200.model import QWEN25_VL_7B, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import PromptLayout, STDRunner, std_generate_qwen25vl
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+
+    def allreduce(x: float, op: str) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+        return float(t.item())
+
+    B, P, V, T = w["batch"], w["prompt"], w["visual"], w["text"]
+    c = QWEN25_VL_7B
+    t_setup = time.time()
+    model = Qwen25VLDecoder(c, seed=2, device=str(dev))
+    ids = torch.full((B, P), VIDEO_TOKEN_ID, dtype=torch.int64)
+    vis = torch.empty(B, V, c.hidden_size, dtype=torch.bfloat16, device=dev)
+    for b in range(B):
+        g = torch.Generator(device=dev).manual_seed(100 + rank * B + b)
+        vis[b] = torch.randn(V, c.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+        gc = torch.Generator().manual_seed(100 + rank * B + b)
+        ids[b, V:] = torch.randint(0, 151643, (T,), generator=gc)
+    layout = PromptLayout.from_ids(ids[0], VIDEO_TOKEN_ID, dev)
+    embeds = []
+    for b in range(B):
+        e = model.embed[ids[b].to(dev)]
+        e[:V] = vis[b]
+        embeds.append(e)
+    runner = STDRunner(model, B, layout, w["max_new"], gamma=w["gamma"], k=w["k"], eos_token_id=-1, ignore_eos=True)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    runner.prefill(embeds, with_selection=True)
+    torch.cuda.synchronize()
+    prefill_s = time.time() - t0
+    del embeds
+    runner.capture()
+
+    # ---- warmup + timed STD decode ----
+    for _ in range(a.warmup):
+        runner.run_std()
+    rounds_per_step = int(runner.stats[:, 0].max().item())
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid or str(local_rank))
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        runner.run_std()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    t_local = ev0.elapsed_time(ev1) / 1000.0
+    tokens_local = a.steps * int(runner.n_gen.sum().item())
+    t_max = allreduce(t_local, "max")
+    tokens_all = allreduce(float(tokens_local), "sum")
+    value = tokens_all / t_max
+    st = runner.std_stats()
+    std_tokens = runner.out_tokens.clone()
+    acc_all = sum(st["accepted"])
+    prop_all = sum(st["proposed"])
+    rounds_all = [len(x) for x in st["accept_lengths"]]
+    mean_accept = acc_all / max(1, sum(rounds_all))
+
+    # ---- AR on the same prefilled state: tokens/s and token-exactness ----
+    ar_tps, token_exact = None, None
+    if not a.no_ar:
+        runner.run_ar()  # warm
+        t_ar = runner.run_ar()
+        ar_tps = allreduce(float(runner.n_gen.sum().item()), "sum") / allreduce(t_ar, "max")
+        token_exact = bool(torch.equal(std_tokens, runner.out_tokens))
+        token_exact = bool(allreduce(0.0 if token_exact else 1.0, "sum") == 0.0)
+
+    # ---- roofline: verify kernel (dominant of ours) and draft kernel, timed alone ----
+    runner.reset()
+    nq = w["gamma"] + 1
+    qv = torch.randn(B, nq, c.num_attention_heads, c.head_dim, device=dev).to(torch.bfloat16)
+    ov = torch.empty_like(qv)
+    lens_v = runner.dense_len  # = P for every request after reset
+    for li in range(c.num_hidden_layers):  # warm (workspaces, tensor maps)
+        ops.verify_attention(qv, runner.dense[li, 0], runner.dense[li, 1], lens_v, nq, out=ov)
+    reps = 4
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        for li in range(c.num_hidden_layers):  # 28 distinct caches, > L2 in total
+            ops.verify_attention(qv, runner.dense[li, 0], runner.dense[li, 1], lens_v, nq, out=ov)
+    e1.record()
+    torch.cuda.synchronize()
+    t_verify = e0.elapsed_time(e1) / 1000.0 / (reps * c.num_hidden_layers)
+    L = P + nq
+    verify_bytes = B * (2048 * L + 143360)
+    verify_flops = B * 14336 * (10 * L - 45)
+    qd = torch.randn(B, c.num_attention_heads, c.head_dim, device=dev).to(torch.bfloat16)
+    od = torch.empty_like(qd)
+    lens_s = runner.sparse_len
+    for li in range(c.num_hidden_layers):
+        ops.draft_attention(qd, runner.sparse[li, 0], runner.sparse[li, 1], lens_s, 1, out=od)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        for li in range(c.num_hidden_layers):
+            ops.draft_attention(qd, runner.sparse[li, 0], runner.sparse[li, 1], lens_s, 1, out=od)
+    e1.record()
+    torch.cuda.synchronize()
+    t_draft = e0.elapsed_time(e1) / 1000.0 / (reps * c.num_hidden_layers)
+    Ls = w["compact"] + 1
+    draft_bytes = B * (2048 * Ls + 14336)
+    peaks = {}
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    achieved = verify_bytes / t_verify / 1e9
+    draft_gbs = draft_bytes / t_draft / 1e9
+    assert ops.device_error() == 0
+
+    # ---- launches of our kernels in the timed region ----
+    Lyr = c.num_hidden_layers
+    fwd = 1 + 7 * Lyr           # embed + per layer (2 rmsnorm, rope_append, attention, 2 add, silu_mul)
+    head = 2                    # final rmsnorm + argmax
+    g_ = w["gamma"]
+    per_round = g_ * fwd + (g_ - 1) * head + (fwd + head) + (fwd + head) + 1  # drafts, verify, bonus, accept
+    gpu_launches = a.steps * rounds_per_step * per_round
+
+    # ---- e2e through the public API, host buffers ----
+    e2e = None
+    if not a.no_e2e:
+        ids_h = ids.pin_memory()
+        vis_h = vis.cpu().pin_memory()
+        h2d = ids_h.numel() * ids_h.element_size() + vis_h.numel() * vis_h.element_size()
+        d2h = B * w["max_new"] * 8
+        torch.cuda.synchronize()
+        barrier()
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record()
+        res, _ = std_generate_qwen25vl(model, {"input_ids": ids_h, "visual_embeds": vis_h}, VIDEO_TOKEN_ID, -1,
+                                       max_new_tokens=w["max_new"], gamma=w["gamma"],
+                                       target_k_plus_text=w["k_plus_text"], ignore_eos=True, runner=runner)
+        gen_host = res.output_ids  # host tensor (device -> host read inside the call)
+        x1.record()
+        torch.cuda.synchronize()
+        barrier()
+        te = allreduce(x0.elapsed_time(x1) / 1000.0, "max")
+        toks = allreduce(float(res.generate_len), "sum")
+        e2e = {"value": toks / te, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "seconds": te, "includes": "H2D of ids+visual embeddings, two-stage prefill, selection, compaction, "
+                                         "STD decode, D2H of tokens",
+               "token_exact_vs_timed_run": bool(torch.equal(gen_host[:, P:].to(torch.int32),
+                                                             std_tokens.cpu()[:, : gen_host.shape[1] - P]))}
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        from oracle.decoder import run_cpu_std
+
+        r = run_cpu_std(rounds=2, warmup=0, L_dense=P, L_sparse=w["compact"], max_new=w["max_new"], gamma=g_)
+        cpu_baseline = {"value": r["tokens"] / r["seconds"], "unit": "tokens/s", "cores": r["cores"], "kind": "port",
+                        "sample": f"2 STD rounds (gamma={g_}) of one request at the workload's shapes, numpy fp32 "
+                                  f"restatement (oracle/decoder.py), 28 layers sharing one weight set, synthetic "
+                                  f"cache state; {r['seconds']:.1f} s"}
+
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": 1000.0 * t_max / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: random-init Qwen2.5-VL-7B-shaped decoder (std 0.02, seed 2); visual embeddings N(0,1), "
+                "text ids U[0,151643), request seeds 100+i",
+        "config": {"workload": w["desc"], "requests_per_gpu": B, "prompt_len": P, "k": w["k"], "gamma": g_,
+                   "max_new_tokens": w["max_new"], "parallelism": f"dp{world} (independent request groups)",
+                   "l2": "inputs larger than L2 (15.2 GB weights + KV caches read per step)"},
+        "e2e": e2e,
+        "roofline": {"bound": "hbm", "kernel": "verify_attn_kernel (tcgen05)", "achieved": achieved,
+                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, burst)",
+                     "algorithmic_bytes_per_launch": verify_bytes, "launch_us": t_verify * 1e6,
+                     "tensor_tflops": verify_flops / t_verify / 1e12,
+                     "tensor_frac": verify_flops / t_verify / 1e12 / tc_peak},
+        "draft_attn": {"achieved": draft_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": draft_gbs / hbm_peak,
+                       "algorithmic_bytes_per_launch": draft_bytes, "launch_us": t_draft * 1e6},
+        "cpu_baseline": cpu_baseline,
+        "clocks": clocks,
+        "gpu_launches": gpu_launches,
+        "token_exact_vs_ar": token_exact,
+        "ar_tokens_per_s": ar_tps,
+        "std_over_ar": (value / ar_tps) if ar_tps else None,
+        "acceptance_rate": acc_all / max(1, prop_all),
+        "mean_accept_length": mean_accept,
+        "rounds_per_step": rounds_per_step,
+        "per_gpu_tokens_per_s": value / world,
+        "prefill_s": prefill_s,
+        "setup_s": time.time() - t_setup,
+    }
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    a = _args()
+    w = _workload(a)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(a.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if "WORLD_SIZE" not in os.environ and a.gpus != 1:
+        print("for --gpus > 1 launch with torch.distributed.run (one process per GPU)", file=sys.stderr)
+        sys.exit(2)
+    if a.impl == "reference":
+        reference_arm(a, w, rank, world)
+        return
+    b200_arm(a, w, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

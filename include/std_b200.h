@@ -12,10 +12,9 @@
  *   - lengths are device-resident int32 arrays (one entry per request), so a
  *     decode round never reads them on the host;
  *   - kernels never allocate; scratch memory is a caller-provided workspace
- *     whose size is given by the matching *_workspace_bytes() function.  A
- *     workspace must be zero-filled once before its first use (the kernels
- *     leave their split counters at zero on exit) and must not be shared by
- *     launches that can run concurrently;
+ *     whose size is given by the matching *_workspace_bytes() function.  It
+ *     needs no initialisation and must not be shared by launches that can
+ *     run concurrently;
  *   - device-side faults are never raised: a wait that exceeds its ~1 s limit
  *     or an out-of-range index is recorded in a device error word that
  *     std_get_device_error() reads and clears.

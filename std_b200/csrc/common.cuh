@@ -170,6 +170,19 @@ STD_DEV void tmem_ld32(uint32_t taddr, uint32_t* r) {
       : "memory");
 }
 STD_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+STD_DEV void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+STD_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128B-swizzled tile
 // whose rows are 128 bytes (the layout TMA SWIZZLE_128B produces).
@@ -203,6 +216,17 @@ STD_DEV float std_exp(float x) {
   }
   return __fmul_rn(p, __uint_as_float(static_cast<uint32_t>(ni + 127) << 23));
 }
+
+
+// 2^x on the SFU (approximate, denormal results flushed to zero).
+STD_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Named barrier over the first `nthreads` threads of the block (id 1..15).
+STD_DEV void named_bar_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 
 STD_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 

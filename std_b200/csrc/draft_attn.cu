@@ -6,23 +6,31 @@
 // over the compacted sparse cache (no mask: the draft query sees every cached
 // key, std_qwen25vl.py:400-417).
 //
-// Design (HBM-bound, ~7 flop/B): split-KV flash-decoding.
-//   grid = (max_splits, Hkv, B); one CTA = one chunk of CHUNK keys of one
-//   (request, KV head) and all G = 7 query heads of that group, so every K/V
-//   byte is read from HBM exactly once (the Triton kernel re-reads each KV head
-//   for each of its 7 query heads).  The chunk's K and V rows are contiguous
-//   in the cache ([B, Hkv, cap, D]) and arrive by two cp.async.bulk copies.
-//   The number of live splits comes from the device-resident length, so the
-//   launch is graph-capturable while lengths change between replays.
-//   Each CTA writes (m, l, O) partials; the last CTA of a (request, head)
-//   (atomic ticket) merges the splits in split order and writes out / lse.
+// Design (HBM-bound, ~7 flop/B, and at batch 1 latency-bound): split-KV
+// flash-decoding inside one thread-block cluster per (request, KV head).
+//   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1).  CTA rank i
+//   streams keys [i*per, (i+1)*per) of the request's live length through a
+//   two-stage cp.async.bulk ring (K and V rows are contiguous in the
+//   [B, Hkv, cap, D] cache), computing all G = 7 query heads of the group with
+//   an online softmax, so every K/V byte is read from HBM once (the Triton
+//   kernel re-reads each KV head for each of its 7 query heads).  The CTAs of
+//   the cluster then combine their (m, l, O) partials through distributed
+//   shared memory -- rank 0 reads the others' smem -- so there is one launch,
+//   no global scratch and no second kernel.  Lengths come from device memory,
+//   so the launch is graph-capturable while they change between replays.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace stdb {
 
 constexpr int DR_D = 128;
 constexpr int DR_G = 7;
-constexpr int DR_THREADS = 128;
+constexpr int DR_THREADS = 256;
+constexpr int DR_SUB = 64;      // keys per pipeline stage
+constexpr int DR_CLUSTER = 8;   // CTAs per (request, KV head)
+constexpr uint32_t DR_STAGE_BYTES = DR_SUB * DR_D * 2;  // one K (or V) stage
+constexpr uint32_t DR_SMEM = 4 * DR_STAGE_BYTES + 128;  // 2 stages x (K, V) + alignment
 
 struct DraftParams {
   const __nv_bfloat16* q;   // [B, Hq, D]
@@ -35,76 +43,96 @@ struct DraftParams {
   float scale_log2;         // (1/sqrt(D)) * log2(e)
   __nv_bfloat16* out;       // [B, Hq, D]
   float* lse;               // [B, Hq] natural-log LSE, may be null
-  int* counters;            // [B, Hkv] zero-initialised tickets
-  float* ws_ml;             // [B, Hkv, max_splits, G, 2]
-  float* ws_o;              // [B, Hkv, max_splits, G, D]
-  int max_splits;
 };
 
-template <int CHUNK>
-__global__ void __launch_bounds__(DR_THREADS) draft_attn_kernel(const DraftParams p) {
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
+    draft_attn_kernel(const DraftParams p) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  extern __shared__ uint8_t dsmem_raw[];
+  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 127) & ~uintptr_t(127));
+  __nv_bfloat16* sK[2] = {reinterpret_cast<__nv_bfloat16*>(sbase),
+                          reinterpret_cast<__nv_bfloat16*>(sbase + DR_STAGE_BYTES)};
+  __nv_bfloat16* sV[2] = {reinterpret_cast<__nv_bfloat16*>(sbase + 2 * DR_STAGE_BYTES),
+                          reinterpret_cast<__nv_bfloat16*>(sbase + 3 * DR_STAGE_BYTES)};
+  __shared__ float sQ[DR_G][DR_D];
+  __shared__ float sS[DR_G][DR_SUB];
+  __shared__ float sAlpha[DR_G];
+  // partials published to the cluster
+  __shared__ float pm[DR_G], pl[DR_G];
+  __shared__ __align__(16) float po[DR_G][DR_D];
+  __shared__ __align__(8) uint64_t bar[2];
+
   int L = p.lens[b] + p.len_offset;
   if (L > p.cap || L < 0) {
-    if (split == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
+    if (rank == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
     L = L < 0 ? 0 : p.cap;
   }
-  const int n_splits = (L + CHUNK - 1) / CHUNK;
-  if (split >= n_splits || split >= p.max_splits) return;
-  const int k0 = split * CHUNK;
-  const int nk = min(CHUNK, L - k0);
-
-  __shared__ __align__(128) __nv_bfloat16 sK[CHUNK * DR_D];
-  __shared__ __align__(128) __nv_bfloat16 sV[CHUNK * DR_D];
-  __shared__ float sQ[DR_G][DR_D];
-  __shared__ float sP[DR_G][CHUNK];
-  __shared__ float sM[DR_G], sL[DR_G];
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ int s_ticket;
-
+  int per = (L + DR_CLUSTER - 1) / DR_CLUSTER;
+  per = (per + 15) & ~15;
+  const int k0 = min(L, rank * per);
+  const int k1 = min(L, k0 + per);
+  const int nsub = (k1 - k0 + DR_SUB - 1) / DR_SUB;
   const size_t head_off = (static_cast<size_t>(b) * p.Hkv + kvh) * p.cap;
+
   if (tid == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_barrier_init();
   }
   __syncthreads();
+  auto issue = [&](int i) {
+    const int st = i & 1;
+    const int a = k0 + i * DR_SUB;
+    const uint32_t bytes = static_cast<uint32_t>(min(DR_SUB, k1 - a)) * DR_D * 2;
+    mbar_arrive_expect_tx(&bar[st], 2 * bytes);
+    bulk_load(sK[st], p.k + (head_off + a) * DR_D, bytes, &bar[st]);
+    bulk_load(sV[st], p.v + (head_off + a) * DR_D, bytes, &bar[st]);
+  };
   if (tid == 0) {
-    const uint32_t bytes = static_cast<uint32_t>(nk) * DR_D * 2;
-    mbar_arrive_expect_tx(&bar, 2 * bytes);
-    bulk_load(sK, p.k + (head_off + k0) * DR_D, bytes, &bar);
-    bulk_load(sV, p.v + (head_off + k0) * DR_D, bytes, &bar);
+    if (nsub > 0) issue(0);
+    if (nsub > 1) issue(1);
   }
-  // q for the G heads of this group (fp32 in smem)
   for (int i = tid; i < DR_G * DR_D; i += DR_THREADS) {
     const int g = i / DR_D, d = i % DR_D;
     sQ[g][d] = __bfloat162float(p.q[(static_cast<size_t>(b) * p.Hq + kvh * DR_G + g) * DR_D + d]);
   }
   __syncthreads();
-  const bool loaded = mbar_wait(&bar, 0);
 
-  // ---- scores: 8 lanes per key, 16 d-elements per lane ----
-  {
-    const int sub = lane >> 3;   // key slot within the warp (0..3)
-    const int part = lane & 7;   // d segment [16*part, 16*part+16)
-    float qr[DR_G][16];
+  // per-thread running state
+  const int sub = lane >> 3, part = lane & 7;  // scores: 8 lanes per key
+  float qr[DR_G][16];
 #pragma unroll
-    for (int g = 0; g < DR_G; ++g)
+  for (int g = 0; g < DR_G; ++g)
 #pragma unroll
-      for (int j = 0; j < 16; ++j) qr[g][j] = sQ[g][part * 16 + j];
-    for (int kb = warp * 4 + sub; kb < CHUNK; kb += 16) {
+    for (int j = 0; j < 16; ++j) qr[g][j] = sQ[g][part * 16 + j];
+  const int od = tid & (DR_D - 1), hs = tid >> 7;  // PV: dim od, heads hs, hs+2, ...
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  float m_run = -INFINITY, l_run = 0.f;  // meaningful in warp g's lanes (softmax of head g)
+  bool ok = true;
+
+  for (int i = 0; i < nsub; ++i) {
+    const int st = i & 1;
+    const int nk = min(DR_SUB, k1 - (k0 + i * DR_SUB));
+    if (ok) ok = mbar_wait(&bar[st], (i >> 1) & 1);
+    // scores
+    for (int kb = warp * 4 + sub; kb < DR_SUB; kb += 32) {
       float acc[DR_G];
 #pragma unroll
       for (int g = 0; g < DR_G; ++g) acc[g] = 0.f;
       if (kb < nk) {
-        const uint4* kr = reinterpret_cast<const uint4*>(sK + kb * DR_D + part * 16);
+        const uint4* kr = reinterpret_cast<const uint4*>(sK[st] + kb * DR_D + part * 16);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint4 u = kr[h];
           const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            float2 f = __bfloat1622float2(e[j]);
+            const float2 f = __bfloat1622float2(e[j]);
 #pragma unroll
             for (int g = 0; g < DR_G; ++g) {
               acc[g] = fmaf(qr[g][h * 8 + 2 * j], f.x, acc[g]);
@@ -115,105 +143,84 @@ __global__ void __launch_bounds__(DR_THREADS) draft_attn_kernel(const DraftParam
       }
 #pragma unroll
       for (int g = 0; g < DR_G; ++g) {
-        float v = acc[g];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if (part == 0) sP[g][kb] = (kb < nk && loaded) ? v * p.scale_log2 : -INFINITY;
+        float x = acc[g];
+        x += __shfl_xor_sync(0xffffffffu, x, 1);
+        x += __shfl_xor_sync(0xffffffffu, x, 2);
+        x += __shfl_xor_sync(0xffffffffu, x, 4);
+        if (part == 0) sS[g][kb] = (kb < nk && ok) ? x * p.scale_log2 : -INFINITY;
       }
     }
-  }
-  __syncthreads();
-
-  // ---- per-head softmax over the chunk (log2 domain) ----
-  for (int g = warp; g < DR_G; g += 4) {
-    float m = -INFINITY;
-    for (int j = lane; j < CHUNK; j += 32) m = fmaxf(m, sP[g][j]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int j = lane; j < CHUNK; j += 32) {
-      const float e = (m == -INFINITY) ? 0.f : exp2f(sP[g][j] - m);
-      sP[g][j] = e;
-      l += e;
+    __syncthreads();
+    // online softmax, warp g owns head g
+    if (warp < DR_G) {
+      const int g = warp;
+      const float a0 = sS[g][lane], a1 = sS[g][lane + 32];
+      const float mc = warp_max(fmaxf(a0, a1));
+      const float mn = fmaxf(m_run, mc);
+      const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mn);
+      const float e0 = (mn == -INFINITY) ? 0.f : exp2f(a0 - mn);
+      const float e1 = (mn == -INFINITY) ? 0.f : exp2f(a1 - mn);
+      sS[g][lane] = e0;
+      sS[g][lane + 32] = e1;
+      l_run = l_run * alpha + warp_sum(e0 + e1);
+      m_run = mn;
+      if (lane == 0) sAlpha[g] = alpha;
     }
-    l = warp_sum(l);
-    if (lane == 0) {
-      sM[g] = m;
-      sL[g] = l;
-    }
-  }
-  __syncthreads();
-
-  // ---- O = P V : thread = d ----
-  float o[DR_G];
+    __syncthreads();
+    // O = O * alpha + P V
 #pragma unroll
-  for (int g = 0; g < DR_G; ++g) o[g] = 0.f;
-  {
-    const int d = tid;
+    for (int hh = 0; hh < 4; ++hh) {
+      const int g = hs + 2 * hh;
+      if (g < DR_G) o[hh] *= sAlpha[g];
+    }
     for (int j = 0; j < nk; ++j) {
-      const float vv = __bfloat162float(sV[j * DR_D + d]);
+      const float vv = __bfloat162float(sV[st][j * DR_D + od]);
 #pragma unroll
-      for (int g = 0; g < DR_G; ++g) o[g] = fmaf(sP[g][j], vv, o[g]);
-    }
-  }
-
-  const int Hq = p.Hq;
-  if (n_splits == 1) {
-#pragma unroll
-    for (int g = 0; g < DR_G; ++g) {
-      const float l = sL[g];
-      p.out[(static_cast<size_t>(b) * Hq + kvh * DR_G + g) * DR_D + tid] =
-          __float2bfloat16_rn(l > 0.f ? o[g] / l : 0.f);
-    }
-    if (p.lse != nullptr && tid < DR_G) {
-      const float l = sL[tid];
-      p.lse[static_cast<size_t>(b) * Hq + kvh * DR_G + tid] =
-          l > 0.f ? (sM[tid] + log2f(l)) * 0.69314718055994530942f : -INFINITY;
-    }
-    return;
-  }
-
-  // ---- multi-split: publish partials, last CTA merges ----
-  const size_t slot = (static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits;
-#pragma unroll
-  for (int g = 0; g < DR_G; ++g) p.ws_o[((slot + split) * DR_G + g) * DR_D + tid] = o[g];
-  if (tid < DR_G) {
-    p.ws_ml[((slot + split) * DR_G + tid) * 2 + 0] = sM[tid];
-    p.ws_ml[((slot + split) * DR_G + tid) * 2 + 1] = sL[tid];
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_ticket = atomicAdd(&p.counters[b * p.Hkv + kvh], 1);
-  __syncthreads();
-  if (s_ticket != n_splits - 1) return;
-  __threadfence();
-  const int d = tid;
-#pragma unroll 1
-  for (int g = 0; g < DR_G; ++g) {
-    float m = -INFINITY, l = 0.f, acc = 0.f;
-    for (int s = 0; s < n_splits; ++s) {
-      const float ms = __ldcg(&p.ws_ml[((slot + s) * DR_G + g) * 2 + 0]);
-      const float ls = __ldcg(&p.ws_ml[((slot + s) * DR_G + g) * 2 + 1]);
-      const float os = __ldcg(&p.ws_o[((slot + s) * DR_G + g) * DR_D + d]);
-      if (ms == -INFINITY) continue;
-      if (m == -INFINITY) {
-        m = ms;
-        l = ls;
-        acc = os;
-        continue;
+      for (int hh = 0; hh < 4; ++hh) {
+        const int g = hs + 2 * hh;
+        if (g < DR_G) o[hh] = fmaf(sS[g][j], vv, o[hh]);
       }
-      const float mn = fmaxf(m, ms);
-      const float a = exp2f(m - mn), c = exp2f(ms - mn);
-      acc = acc * a + os * c;
-      l = l * a + ls * c;
-      m = mn;
     }
-    p.out[(static_cast<size_t>(b) * Hq + kvh * DR_G + g) * DR_D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
-    if (p.lse != nullptr && d == 0)
-      p.lse[static_cast<size_t>(b) * Hq + kvh * DR_G + g] =
-          l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
+    __syncthreads();  // stage st and sS free
+    if (tid == 0 && i + 2 < nsub) issue(i + 2);
   }
-  if (tid == 0) p.counters[b * p.Hkv + kvh] = 0;
+
+  // publish this CTA's partial to the cluster
+#pragma unroll
+  for (int hh = 0; hh < 4; ++hh) {
+    const int g = hs + 2 * hh;
+    if (g < DR_G) po[g][od] = o[hh];
+  }
+  if (warp < DR_G && lane == 0) {
+    pm[warp] = (l_run > 0.f) ? m_run : -INFINITY;
+    pl[warp] = l_run;
+  }
+  cluster.sync();
+  if (rank == 0) {
+    for (int idx = tid; idx < DR_G * DR_D; idx += DR_THREADS) {
+      const int g = idx / DR_D, d = idx % DR_D;
+      float mr[DR_CLUSTER];
+      float m = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < DR_CLUSTER; ++r) {
+        mr[r] = *cluster.map_shared_rank(&pm[g], r);
+        m = fmaxf(m, mr[r]);
+      }
+      float l = 0.f, acc = 0.f;
+#pragma unroll
+      for (int r = 0; r < DR_CLUSTER; ++r) {
+        if (mr[r] == -INFINITY) continue;
+        const float w = exp2f(mr[r] - m);
+        l += w * *cluster.map_shared_rank(&pl[g], r);
+        acc += w * *cluster.map_shared_rank(&po[g][d], r);
+      }
+      p.out[(static_cast<size_t>(b) * p.Hq + kvh * DR_G + g) * DR_D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+      if (d == 0 && p.lse != nullptr)
+        p.lse[static_cast<size_t>(b) * p.Hq + kvh * DR_G + g] =
+            l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
+    }
+  }
+  cluster.sync();  // keep every CTA's smem alive until rank 0 has read it
 }
 
 }  // namespace stdb
@@ -221,32 +228,30 @@ __global__ void __launch_bounds__(DR_THREADS) draft_attn_kernel(const DraftParam
 // ---------------------------------------------------------------------------
 // C ABI
 // ---------------------------------------------------------------------------
-static int draft_chunk_for(int B, int Hkv, int cap) {
-  const long ctas64 = static_cast<long>(B) * Hkv * ((cap + 63) / 64);
-  return ctas64 >= 2 * 148 ? 64 : 32;
-}
-
 extern "C" size_t std_draft_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int cap) {
+  (void)B;
   (void)Hq;
+  (void)Hkv;
   (void)D;
-  const int chunk = draft_chunk_for(B, Hkv, cap);
-  const size_t max_splits = (cap + chunk - 1) / chunk;
-  const size_t n = static_cast<size_t>(B) * Hkv;
-  size_t bytes = ((n * 4 + 255) / 256) * 256;
-  bytes += n * max_splits * stdb::DR_G * 2 * 4;
-  bytes = ((bytes + 255) / 256) * 256;
-  bytes += n * max_splits * stdb::DR_G * stdb::DR_D * 4;
-  return bytes;
+  (void)cap;
+  return 0;  // partials are combined in distributed shared memory
 }
 
 extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
                               int len_offset, int B, int Hq, int Hkv, int D, int cap, void* out, float* lse,
                               void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
   if (D != stdb::DR_D || Hq != Hkv * stdb::DR_G || B <= 0 || cap <= 0) return 1;
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || lens == nullptr || out == nullptr) return 1;
-  if (workspace == nullptr || workspace_bytes < std_draft_attn_workspace_bytes(B, Hq, Hkv, D, cap)) return 5;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) return 1;
-  const int chunk = draft_chunk_for(B, Hkv, cap);
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(stdb::draft_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, stdb::DR_SMEM) !=
+        cudaSuccess)
+      return 3;
+    attr_set = true;
+  }
   stdb::DraftParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k_cache);
@@ -259,20 +264,7 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
-  p.max_splits = (cap + chunk - 1) / chunk;
-  const size_t n = static_cast<size_t>(B) * Hkv;
-  char* ws = static_cast<char*>(workspace);
-  p.counters = reinterpret_cast<int*>(ws);
-  size_t off = ((n * 4 + 255) / 256) * 256;
-  p.ws_ml = reinterpret_cast<float*>(ws + off);
-  off += n * p.max_splits * stdb::DR_G * 2 * 4;
-  off = ((off + 255) / 256) * 256;
-  p.ws_o = reinterpret_cast<float*>(ws + off);
-  dim3 grid(p.max_splits, Hkv, B);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (chunk == 64)
-    stdb::draft_attn_kernel<64><<<grid, stdb::DR_THREADS, 0, s>>>(p);
-  else
-    stdb::draft_attn_kernel<32><<<grid, stdb::DR_THREADS, 0, s>>>(p);
+  dim3 grid(stdb::DR_CLUSTER, Hkv, B);
+  stdb::draft_attn_kernel<<<grid, stdb::DR_THREADS, stdb::DR_SMEM, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

@@ -7,35 +7,42 @@
 // and, with nq = 1, the dense attention of AR decoding
 //   std_qwen25vl.py:584-590          ar_generate_qwen25vl loop.
 //
-// One CTA = one (request, KV head, split of 512 keys).  The 7 query heads of
-// the group times nq tokens form the rows of a 128-row tile (row = t*7 + g,
-// zero-padded), so each K/V byte is read once for all 7 heads:
-//   S_c  = Q K_c^T   tcgen05.mma M=128 N=128 K=128 (8 x K16), fp32 in TMEM
-//   P_c  = exp2(S_c*scale*log2e - rowmax_c), bf16, written to smem (SW128)
-//   O_c  = P_c V_c   tcgen05.mma M=128 N=128 K=128, V as an MN-major operand
-// Warp roles: warps 0-3 own TMEM lanes 0-127 (one row per thread: softmax,
-// chunk merge, epilogue); warp 4 lane 0 issues TMA (K/V chunks, 2 stages);
-// warp 5 allocates TMEM and lane 0 issues the MMAs.
+// One CTA = one (request, KV head, split of split_keys keys).  The 7 query
+// heads of the group times nq tokens form the rows of a 128-row tile
+// (row = t*7 + g, zero-padded), so each K/V byte is read once for all 7 heads:
+//   S_c  = Q K_c^T    tcgen05.mma M=128 N=128 K=128 (8 x K16), fp32 in TMEM
+//   P_c  = exp2(S_c*scale*log2e - m_row), bf16, written to smem (SW128, 2 buffers)
+//   O   += P_c V_c    tcgen05.mma into one TMEM accumulator, V MN-major
+// m_row is a running row max; O is rescaled in TMEM only when a chunk raises
+// the max by more than 2^8 (lazy rescale), so the softmax threads normally
+// touch TMEM once per chunk.  Warp roles: warps 0-3 own TMEM lanes 0-127 (one
+// row per thread); warp 4 lane 0 issues TMA (2 K/V stages); warp 5 allocates
+// TMEM and lane 0 issues the MMAs.  Splits write (O, m, l) partials that a
+// second kernel combines; a request whose keys fit one split writes its output
+// directly.
 //
-// Canonical reduction tree.  Chunk boundaries (128 keys) and split boundaries
-// (512 keys) sit at fixed absolute key positions; each chunk is normalised to
-// its own max and chunk partials are merged in key order, fully masked chunks
-// are skipped, and splits are merged in split order the same way.  A row's
-// result therefore depends only on its query, its visible keys and these
-// boundaries -- not on nq or on the other rows.  AR (nq = 1) and verify rows
-// (nq = gamma+1) through this kernel are bit-identical, which STD's
+// Row invariance.  Chunk boundaries (128 keys) and split boundaries
+// (split_keys, a function of the cache shape only) sit at fixed absolute key
+// positions, and every per-row decision (running max, rescale, masking) uses
+// only that row's scores; fully masked chunks and splits contribute exact
+// zeros.  A row's result therefore depends only on its query, its visible
+// keys and these boundaries -- not on nq or on the other rows.  AR (nq = 1)
+// and verify rows (nq = gamma+1) are bit-identical, which STD's
 // token-exactness against AR relies on.
 #include "common.cuh"
 
 namespace stdb {
 
 constexpr int VF_D = 128;
-constexpr int VF_CHUNK = 128;
-constexpr int VF_SPLIT = 512;
-constexpr int VF_THREADS = 192;
+constexpr int VF_CHUNK = 64;       // keys per chunk (MMA N of S, K of P V)
+constexpr int VF_STAGES = 4;       // K/V ring depth
+constexpr int VF_THREADS = 320;    // 2 softmax warpgroups + TMA warp + MMA warp
 constexpr int VF_G = 7;
-constexpr uint32_t VF_TILE = 32768;  // 128 rows x 256 B
-constexpr uint32_t VF_SMEM = 6 * VF_TILE + 1024;
+constexpr uint32_t VF_QTILE = 32768;  // 128 rows x 256 B (two 64-d K-blocks)
+constexpr uint32_t VF_KV = 16384;     // one K or V chunk: 64 keys x 256 B (two 8 KB d-blocks)
+constexpr uint32_t VF_PTILE = 16384;  // 128 rows x 64 keys bf16 (one K-block)
+constexpr uint32_t VF_SMEM = VF_QTILE + 2 * VF_STAGES * VF_KV + 2 * VF_PTILE + 1024;
+constexpr float VF_RESCALE = 8.0f;    // log2 units
 
 struct VerifyParams {
   const __nv_bfloat16* q;  // [B, nq, Hq, D]
@@ -46,79 +53,63 @@ struct VerifyParams {
   float scale_log2;
   __nv_bfloat16* out;      // [B, nq, Hq, D]
   float* lse;              // [B, nq, Hq] natural log, may be null
-  int* counters;           // [B, Hkv]
   float* ws_ml;            // [B, Hkv, max_splits, 128, 2]
   float* ws_o;             // [B, Hkv, max_splits, 128, D]
   int max_splits;
+  int split_keys;          // keys per split: a multiple of VF_CHUNK fixed by (B, Hkv, cap)
 };
 
-STD_DEV void merge_chunk(float* acc, float& m_run, float& l_run, const uint32_t* oc, int base, float m_c,
-                         float l_c, float& a_out, float& b_out) {
-  (void)acc;
-  (void)oc;
-  (void)base;
-  if (m_c == -INFINITY) {
-    a_out = 1.f;
-    b_out = 0.f;
-    return;
-  }
-  if (m_run == -INFINITY) {
-    a_out = 0.f;
-    b_out = 1.f;
-    m_run = m_c;
-    l_run = l_c;
-    return;
-  }
-  const float mn = fmaxf(m_run, m_c);
-  a_out = exp2f(m_run - mn);
-  b_out = exp2f(m_c - mn);
-  l_run = l_run * a_out + l_c * b_out;
-  m_run = mn;
+STD_DEV int verify_len(const VerifyParams& p, int b) {
+  int L = p.lens[b] + p.len_offset;
+  if (L > p.cap) L = p.cap;
+  if (L < p.nq) L = p.nq;
+  return L;
 }
 
+// Chunk c of a split goes to softmax warpgroup / TMEM accumulator (c & 1);
+// S buffer (c & 1), P buffer (c & 1), K/V stage (c % 4).
 __global__ void __launch_bounds__(VF_THREADS, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const VerifyParams p) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int L = p.lens[b] + p.len_offset;
-  if (L > p.cap || L < p.nq) {
-    if (split == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
-    L = L > p.cap ? p.cap : p.nq;
-  }
-  const int n_splits = (L + VF_SPLIT - 1) / VF_SPLIT;
+  const int Lraw = p.lens[b] + p.len_offset;
+  if ((Lraw > p.cap || Lraw < p.nq) && split == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
+  const int L = verify_len(p, b);
+  const int n_splits = (L + p.split_keys - 1) / p.split_keys;
   if (split >= n_splits || split >= p.max_splits) return;
-  const int k0 = split * VF_SPLIT;
-  const int k1 = min(k0 + VF_SPLIT, L);
+  const int k0 = split * p.split_keys;
+  const int k1 = min(k0 + p.split_keys, L);
   const int nchunks = (k1 - k0 + VF_CHUNK - 1) / VF_CHUNK;
   const int nrows = VF_G * p.nq;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK[2] = {smem + VF_TILE, smem + 2 * VF_TILE};
-  uint8_t* sV[2] = {smem + 3 * VF_TILE, smem + 4 * VF_TILE};
-  uint8_t* sP = smem + 5 * VF_TILE;
+  uint8_t* sK = smem + VF_QTILE;                       // [VF_STAGES][VF_KV]
+  uint8_t* sV = sK + VF_STAGES * VF_KV;                // [VF_STAGES][VF_KV]
+  uint8_t* sP = sV + VF_STAGES * VF_KV;                // [2][VF_PTILE]
 
-  __shared__ __align__(8) uint64_t bar_q, bar_kv_full[2], bar_kv_empty[2], bar_s_full[2], bar_s_free[2], bar_p_full,
-      bar_o_full, bar_mma_done;
+  __shared__ __align__(8) uint64_t bar_q, bar_kv_full[VF_STAGES], bar_kv_empty[VF_STAGES], bar_s_full[2],
+      bar_s_free[2], bar_p_full[2], bar_mma_done;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_ticket;
+  __shared__ float s_mB[128], s_lB[128];
 
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(&s_tmem, 512);
     tmem_relinquish();
   }
-  if (tid == 128) {
+  if (tid == 256) {
     mbar_init(&bar_q, 128);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < VF_STAGES; ++i) {
       mbar_init(&bar_kv_full[i], 1);
       mbar_init(&bar_kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_s_full[i], 1);
       mbar_init(&bar_s_free[i], 128);
+      mbar_init(&bar_p_full[i], 128);
     }
-    mbar_init(&bar_p_full, 128);
-    mbar_init(&bar_o_full, 1);
     mbar_init(&bar_mma_done, 1);
     fence_barrier_init();
     prefetch_tensormap(&tmK);
@@ -127,80 +118,84 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = s_tmem;
+  const uint32_t tmem = s_tmem;  // S[w]: cols 64w .. 64w+63; O[w]: cols 128 + 128w
   const int row0 = (b * p.Hkv + kvh) * p.cap;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
-        const int st = c & 1;
-        if (c >= 2 && !mbar_wait(&bar_kv_empty[st], ((c >> 1) - 1) & 1)) break;
-        mbar_arrive_expect_tx(&bar_kv_full[st], 4 * 16384);
+        const int st = c % VF_STAGES;
+        if (c >= VF_STAGES && !mbar_wait(&bar_kv_empty[st], ((c / VF_STAGES) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&bar_kv_full[st], 2 * VF_KV);
         const int y = row0 + k0 + c * VF_CHUNK;
-        tma_load_2d(sK[st], &tmK, &bar_kv_full[st], 0, y);
-        tma_load_2d(sK[st] + 16384, &tmK, &bar_kv_full[st], 64, y);
-        tma_load_2d(sV[st], &tmV, &bar_kv_full[st], 0, y);
-        tma_load_2d(sV[st] + 16384, &tmV, &bar_kv_full[st], 64, y);
+        uint8_t* kd = sK + st * VF_KV;
+        uint8_t* vd = sV + st * VF_KV;
+        tma_load_2d(kd, &tmK, &bar_kv_full[st], 0, y);
+        tma_load_2d(kd + VF_KV / 2, &tmK, &bar_kv_full[st], 64, y);
+        tma_load_2d(vd, &tmV, &bar_kv_full[st], 0, y);
+        tma_load_2d(vd + VF_KV / 2, &tmV, &bar_kv_full[st], 64, y);
         issued = c + 1;
       }
       // never leave a copy in flight: wait for the last load of each stage
-      for (int c = issued - 2 < 0 ? 0 : issued - 2; c < issued; ++c) mbar_wait(&bar_kv_full[c & 1], (c >> 1) & 1);
+      for (int c = issued - VF_STAGES < 0 ? 0 : issued - VF_STAGES; c < issued; ++c)
+        mbar_wait(&bar_kv_full[c % VF_STAGES], (c / VF_STAGES) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);
-      const uint32_t idO = idesc_bf16_f32(128, 128, 0, 1);
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      const uint32_t idS = idesc_bf16_f32(128, VF_CHUNK, 0, 0);
+      const uint32_t idO = idesc_bf16_f32(128, VF_D, 0, 1);
+      const uint32_t aQ = smem_u32(sQ);
       bool ok = mbar_wait(&bar_q, 0);
       tc_fence_after();
       auto issue_S = [&](int c) -> bool {
-        const int st = c & 1;
-        if (!mbar_wait(&bar_kv_full[st], (c >> 1) & 1)) return false;
-        if (c >= 2 && !mbar_wait(&bar_s_free[st], ((c >> 1) - 1) & 1)) return false;
+        const int st = c % VF_STAGES, w = c & 1;
+        if (!mbar_wait(&bar_kv_full[st], (c / VF_STAGES) & 1)) return false;
+        if (c >= 2 && !mbar_wait(&bar_s_free[w], ((c >> 1) - 1) & 1)) return false;
         tc_fence_after();
-        const uint32_t aK = smem_u32(sK[st]);
+        const uint32_t aK = smem_u32(sK + st * VF_KV);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t off = (ks >> 2) * 16384u + (ks & 3) * 32u;
-          umma_bf16(tmem + st * 128, sdesc_sw128(aQ + off, 16, 1024), sdesc_sw128(aK + off, 16, 1024), idS,
+          const uint32_t offQ = (ks >> 2) * 16384u + (ks & 3) * 32u;
+          const uint32_t offK = (ks >> 2) * (VF_KV / 2) + (ks & 3) * 32u;
+          umma_bf16(tmem + w * VF_CHUNK, sdesc_sw128(aQ + offQ, 16, 1024), sdesc_sw128(aK + offK, 16, 1024), idS,
                     ks > 0 ? 1u : 0u);
         }
-        umma_commit(&bar_s_full[st]);
+        umma_commit(&bar_s_full[w]);
         return true;
       };
       if (ok) ok = issue_S(0);
+      if (ok && nchunks > 1) ok = issue_S(1);
       for (int c = 0; ok && c < nchunks; ++c) {
-        if (c + 1 < nchunks && !issue_S(c + 1)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(&bar_p_full, c & 1)) {
+        const int w = c & 1, st = c % VF_STAGES;
+        if (!mbar_wait(&bar_p_full[w], (c >> 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t aV = smem_u32(sV[c & 1]);
+        const uint32_t aV = smem_u32(sV + st * VF_KV), aP = smem_u32(sP + w * VF_PTILE);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t offP = (ks >> 2) * 16384u + (ks & 3) * 32u;
-          umma_bf16(tmem + 256, sdesc_sw128(aP + offP, 16, 1024), sdesc_sw128(aV + ks * 2048u, 16384, 1024), idO,
-                    ks > 0 ? 1u : 0u);
+        for (int ks = 0; ks < VF_CHUNK / 16; ++ks) {
+          umma_bf16(tmem + 128 + 128 * w, sdesc_sw128(aP + ks * 32u, 16, 1024),
+                    sdesc_sw128(aV + ks * 2048u, VF_KV / 2, 1024), idO, (c >= 2 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(&bar_o_full);
-        umma_commit(&bar_kv_empty[c & 1]);
+        umma_commit(&bar_kv_empty[st]);
+        if (c + 2 < nchunks && !issue_S(c + 2)) {
+          ok = false;
+          break;
+        }
       }
       umma_commit(&bar_mma_done);
-      mbar_wait(&bar_mma_done, 0);
     }
   } else {
-    // ---------------- softmax / merge / epilogue: thread = row ----------------
-    const int r = tid;
+    // ---------------- softmax warpgroups: thread = row ----------------
+    const int wg = warp >> 2;          // 0 or 1
+    const int r = tid & 127;
     const int t = r / VF_G, g = r % VF_G;
     const bool valid_row = r < nrows;
-    {
+    if (wg == 0) {
       const uint4* src = reinterpret_cast<const uint4*>(
           p.q + ((static_cast<size_t>(b) * p.nq + (valid_row ? t : 0)) * p.Hq + kvh * VF_G + g) * VF_D);
 #pragma unroll
@@ -208,172 +203,190 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         uint4 v = valid_row ? src[c] : make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(sQ + (c >> 3) * 16384u + sw128_offset(r, c & 7)) = v;
       }
+      fence_async_smem();
+      mbar_arrive(&bar_q);
     }
-    fence_async_smem();
-    mbar_arrive(&bar_q);
-
-    const int limit = p.causal ? (L - p.nq + t) : (L - 1);  // last visible key
-    const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    float acc[VF_D];
-#pragma unroll
-    for (int d = 0; d < VF_D; ++d) acc[d] = 0.f;
+    const int limit = min(p.causal ? (L - p.nq + t) : (L - 1), k1 - 1);  // last visible key
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t tO = trow + 128 + 128 * wg;
+    const float sc = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
-    float m_prev = -INFINITY, l_prev = 0.f;
     bool ok = true;
-    uint32_t v[32];
+    uint32_t s[VF_CHUNK];
+    uint8_t* P = sP + wg * VF_PTILE;
 
-    auto merge_o = [&](float m_c, float l_c) {
-      float a, bb;
-      merge_chunk(acc, m_run, l_run, nullptr, 0, m_c, l_c, a, bb);
-#pragma unroll
-      for (int piece = 0; piece < 4; ++piece) {
-        tmem_ld32(trow + 256 + piece * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float oc = __uint_as_float(v[j]);
-          float& x = acc[piece * 32 + j];
-          if (bb == 1.f && a == 0.f)
-            x = oc;
-          else if (bb != 0.f)
-            x = x * a + oc * bb;
-        }
-      }
-    };
-
-    for (int c = 0; c < nchunks; ++c) {
-      const int sb = c & 1;
-      if (ok) ok = mbar_wait(&bar_s_full[sb], (c >> 1) & 1);
+    for (int c = wg; c < nchunks; c += 2) {
+      const int kk = c >> 1;
+      if (ok) ok = mbar_wait(&bar_s_full[wg], kk & 1);  // also: O[wg] and P[wg] no longer in use
+      __syncwarp();
       tc_fence_after();
-      const int key0 = k0 + c * VF_CHUNK;
-      float m_c = -INFINITY;
+      tmem_ld32(trow + wg * VF_CHUNK, s);
+      tmem_ld32(trow + wg * VF_CHUNK + 32, s + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bar_s_free[wg]);
+      const int nvis = limit - (k0 + c * VF_CHUNK) + 1;  // visible keys of this chunk
+      float mraw = -INFINITY;
+      if (nvis >= VF_CHUNK) {
 #pragma unroll
-      for (int piece = 0; piece < 4; ++piece) {
-        tmem_ld32(trow + sb * 128 + piece * 32, v);
-        tmem_wait_ld();
+        for (int j = 0; j < VF_CHUNK; ++j) mraw = fmaxf(mraw, __uint_as_float(s[j]));
+      } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int key = key0 + piece * 32 + j;
-          if (key <= limit && key < k1) m_c = fmaxf(m_c, __uint_as_float(v[j]) * p.scale_log2);
+        for (int j = 0; j < VF_CHUNK; ++j)
+          if (j < nvis) mraw = fmaxf(mraw, __uint_as_float(s[j]));
+      }
+      const float m_c = mraw * sc;  // scale > 0: max commutes with the scaling
+      const bool need = (m_run != -INFINITY) && (m_c > m_run + VF_RESCALE);
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? exp2f(m_run - m_c) : 1.0f;
+        uint32_t o[32];
+#pragma unroll
+        for (int piece = 0; piece < 4; ++piece) {
+          tmem_ld32(tO + piece * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          tmem_st32(tO + piece * 32, o);
+        }
+        tmem_wait_st();
+        if (need) {
+          l_run *= alpha;
+          m_run = m_c;
         }
       }
-      if (c > 0) {
-        if (ok) ok = mbar_wait(&bar_o_full, (c - 1) & 1);
-        tc_fence_after();
-        merge_o(m_prev, l_prev);
-      }
-      float l_c = 0.f;
+      if (m_run == -INFINITY) m_run = m_c;
+      const float nm = -m_run;
+      const bool any = m_run != -INFINITY;
 #pragma unroll
-      for (int piece = 0; piece < 4; ++piece) {
-        tmem_ld32(trow + sb * 128 + piece * 32, v);
-        tmem_wait_ld();
-        uint32_t pk[16];
+      for (int piece = 0; piece < VF_CHUNK / 16; ++piece) {  // 16 keys = 2 x 16 B
+        uint32_t pk[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float e[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int jj = 2 * j + h;
-            const int key = key0 + piece * 32 + jj;
-            float pe = 0.f;
-            if (m_c != -INFINITY && key <= limit && key < k1)
-              pe = bf16_round(exp2f(__uint_as_float(v[jj]) * p.scale_log2 - m_c));
-            e[h] = pe;
-            l_c += pe;
-          }
-          pk[j] = pack_bf16x2(e[0], e[1]);
+        for (int q2 = 0; q2 < 8; ++q2) {
+          const int j = piece * 16 + 2 * q2;
+          float e0 = (any && j < nvis) ? ex2_approx(fmaf(__uint_as_float(s[j]), sc, nm)) : 0.f;
+          float e1 = (any && j + 1 < nvis) ? ex2_approx(fmaf(__uint_as_float(s[j + 1]), sc, nm)) : 0.f;
+          l_run += e0 + e1;
+          pk[q2] = pack_bf16x2(e0, e1);
         }
-        // keys piece*32 .. +31 -> K-block piece/2, 16-B chunks (piece%2)*4 .. +3
-        uint8_t* base = sP + (piece >> 1) * 16384u;
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          *reinterpret_cast<uint4*>(base + sw128_offset(r, (piece & 1) * 4 + q4)) =
-              make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
-        }
+        *reinterpret_cast<uint4*>(P + sw128_offset(r, 2 * piece)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(P + sw128_offset(r, 2 * piece + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
       tc_fence_before();
-      mbar_arrive(&bar_s_free[sb]);
       fence_async_smem();
-      mbar_arrive(&bar_p_full);
-      m_prev = m_c;
-      l_prev = l_c;
+      mbar_arrive(&bar_p_full[wg]);
     }
-    if (ok) ok = mbar_wait(&bar_o_full, (nchunks - 1) & 1);
+    // ---- combine the two accumulators (row-local), write output or partial ----
+    if (ok) ok = mbar_wait(&bar_mma_done, 0);
+    __syncwarp();
     tc_fence_after();
-    merge_o(m_prev, l_prev);
-
-    if (valid_row) {
-      if (n_splits == 1) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(
-            p.out + ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D);
+    if (wg == 1) {
+      s_mB[r] = m_run;
+      s_lB[r] = l_run;
+    }
+    named_bar_sync(1, 256);
+    if (wg == 0) {
+      const float mB = s_mB[r], lB = s_lB[r];
+      const bool hasA = m_run != -INFINITY && l_run > 0.f, hasB = mB != -INFINITY && lB > 0.f;
+      const float m = hasA ? (hasB ? fmaxf(m_run, mB) : m_run) : (hasB ? mB : -INFINITY);
+      const float wa = hasA ? exp2f(m_run - m) : 0.f, wb = hasB ? exp2f(mB - m) : 0.f;
+      const float l = (hasA ? l_run * wa : 0.f) + (hasB ? lB * wb : 0.f);
+      const bool single = n_splits == 1;
+      const float inv = (single && l > 0.f) ? 1.f / l : 1.f;
+      uint32_t oa[32], ob[32];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          uint4 w;
-          w.x = pack_bf16x2(acc[8 * c + 0] * inv, acc[8 * c + 1] * inv);
-          w.y = pack_bf16x2(acc[8 * c + 2] * inv, acc[8 * c + 3] * inv);
-          w.z = pack_bf16x2(acc[8 * c + 4] * inv, acc[8 * c + 5] * inv);
-          w.w = pack_bf16x2(acc[8 * c + 6] * inv, acc[8 * c + 7] * inv);
-          dst[c] = w;
+      for (int piece = 0; piece < 4; ++piece) {
+        tmem_ld32(trow + 128 + piece * 32, oa);
+        tmem_ld32(trow + 256 + piece * 32, ob);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = hasA ? __uint_as_float(oa[j]) * wa : 0.f;
+          if (hasB) x += __uint_as_float(ob[j]) * wb;
+          v[j] = x * inv;
         }
-        if (p.lse != nullptr)
-          p.lse[(static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g] =
-              l_run > 0.f ? (m_run + log2f(l_run)) * 0.69314718055994530942f : -INFINITY;
-      } else {
-        const size_t slot = ((static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits + split) * 128 + r;
-        float4* dst = reinterpret_cast<float4*>(p.ws_o + slot * VF_D);
+        if (valid_row) {
+          if (single) {
+            uint4* dst = reinterpret_cast<uint4*>(
+                p.out + ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + piece * 32);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) dst[c] = make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
-        p.ws_ml[slot * 2 + 0] = m_run;
-        p.ws_ml[slot * 2 + 1] = l_run;
+            for (int c4 = 0; c4 < 4; ++c4)
+              dst[c4] = make_uint4(pack_bf16x2(v[8 * c4], v[8 * c4 + 1]), pack_bf16x2(v[8 * c4 + 2], v[8 * c4 + 3]),
+                                   pack_bf16x2(v[8 * c4 + 4], v[8 * c4 + 5]), pack_bf16x2(v[8 * c4 + 6], v[8 * c4 + 7]));
+          } else {
+            const size_t slot = ((static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits + split) * 128 + r;
+            float4* dst = reinterpret_cast<float4*>(p.ws_o + slot * VF_D + piece * 32);
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) dst[c4] = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+          }
+        }
+      }
+      if (valid_row) {
+        if (single) {
+          if (p.lse != nullptr)
+            p.lse[(static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g] =
+                l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
+        } else {
+          const size_t slot = ((static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits + split) * 128 + r;
+          p.ws_ml[slot * 2 + 0] = l > 0.f ? m : -INFINITY;
+          p.ws_ml[slot * 2 + 1] = l;
+        }
       }
     }
   }
 
-  // ---------------- teardown + cross-split merge ----------------
+  // ---------------- teardown ----------------
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-  if (n_splits == 1) return;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_ticket = atomicAdd(&p.counters[b * p.Hkv + kvh], 1);
-  __syncthreads();
-  if (s_ticket != n_splits - 1) return;
-  __threadfence();
-  const size_t slot0 = (static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits * 128;
-  for (int idx = tid; idx < nrows * VF_D; idx += VF_THREADS) {
-    const int r = idx / VF_D, d = idx % VF_D;
-    float m = -INFINITY, l = 0.f, a = 0.f;
-    for (int s = 0; s < n_splits; ++s) {
-      const size_t sl = slot0 + static_cast<size_t>(s) * 128 + r;
-      const float ms = __ldcg(&p.ws_ml[sl * 2]);
-      const float ls = __ldcg(&p.ws_ml[sl * 2 + 1]);
-      const float os = __ldcg(&p.ws_o[sl * VF_D + d]);
-      if (ms == -INFINITY) continue;
-      if (m == -INFINITY) {
-        m = ms;
-        l = ls;
-        a = os;
-        continue;
-      }
-      const float mn = fmaxf(m, ms);
-      const float x = exp2f(m - mn), y = exp2f(ms - mn);
-      a = a * x + os * y;
-      l = l * x + ls * y;
-      m = mn;
-    }
-    const int t = r / VF_G, g = r % VF_G;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    p.out[((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + d] = __float2bfloat16_rn(a * inv);
-    if (d == 0 && p.lse != nullptr)
-      p.lse[(static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g] =
-          l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
+}
+
+// Combine split partials: m = max_s m_s, w_s = exp2(m_s - m) (0 for splits a
+// row cannot see), out = (sum_s w_s o_s) / (sum_s w_s l_s), split order.
+// One thread per (row, 4 dims); requests whose keys fit one split are skipped
+// (the split kernel wrote them).
+__global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p) {
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int L = verify_len(p, b);
+  const int n_splits = (L + p.split_keys - 1) / p.split_keys;
+  if (n_splits <= 1) return;
+  const int nrows = VF_G * p.nq;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = idx / (VF_D / 4), d4 = idx % (VF_D / 4);
+  if (r >= nrows) return;
+  const size_t slot0 = (static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits * 128 + r;
+  float m = -INFINITY;
+#pragma unroll 8
+  for (int s = 0; s < n_splits; ++s) m = fmaxf(m, __ldcg(&p.ws_ml[(slot0 + static_cast<size_t>(s) * 128) * 2]));
+  float l = 0.f;
+  float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int s = 0; s < n_splits; ++s) {
+    const size_t sl = slot0 + static_cast<size_t>(s) * 128;
+    const float ms = __ldcg(&p.ws_ml[sl * 2]);
+    if (ms == -INFINITY) continue;
+    const float w = exp2f(ms - m);
+    l += w * __ldcg(&p.ws_ml[sl * 2 + 1]);
+    const float4 o = __ldcg(reinterpret_cast<const float4*>(p.ws_o + sl * VF_D) + d4);
+    a.x += w * o.x;
+    a.y += w * o.y;
+    a.z += w * o.z;
+    a.w += w * o.w;
   }
-  if (tid == 0) p.counters[b * p.Hkv + kvh] = 0;
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  const int t = r / VF_G, g = r % VF_G;
+  uint2 pk;
+  pk.x = pack_bf16x2(a.x * inv, a.y * inv);
+  pk.y = pack_bf16x2(a.z * inv, a.w * inv);
+  *reinterpret_cast<uint2*>(p.out + ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + 4 * d4) =
+      pk;
+  if (d4 == 0 && p.lse != nullptr)
+    p.lse[(static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g] =
+        l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
 }
 
 }  // namespace stdb
@@ -398,7 +411,7 @@ static PFN_tmapEncodeTiled tmap_encoder() {
   return fn;
 }
 
-// 2-D bf16 tensor [rows, cols] (row pitch = cols*2 bytes), box = box_cols x box_rows,
+// 2-D bf16 tensor [rows, cols] (row pitch in bytes), box = box_cols x box_rows,
 // 128-byte swizzle.  box_cols*2 must be 128.
 static int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t row_pitch_bytes,
                              uint32_t box_cols, uint32_t box_rows) {
@@ -414,11 +427,37 @@ static int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t rows, ui
   return r == CUDA_SUCCESS ? 0 : 4;
 }
 
+// Keys per split, fixed by the cache shape alone (so two calls on the same
+// cache -- an AR step and a verify block -- use the same split boundaries).
+// The split count per (request, head) is chosen so the CTAs fill whole waves of
+// the 148 SMs (one CTA per SM) as evenly as possible, preferring fewer waves.
+static int verify_split_keys(int B, int Hkv, int cap) {
+  const long heads = static_cast<long>(B) * Hkv;
+  const long max_ns = (cap + 2 * stdb::VF_CHUNK - 1) / (2 * stdb::VF_CHUNK);  // >= 2 chunks per split
+  long best_ns = 1;
+  double best_eff = -1.0;
+  for (long waves = 1; waves <= 4; ++waves) {
+    long ns = waves * 148 / heads;
+    if (ns < 1) ns = 1;
+    if (ns > max_ns) ns = max_ns;
+    const long ctas = heads * ns;
+    const double eff = static_cast<double>(ctas) / (static_cast<double>((ctas + 147) / 148) * 148.0);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best_ns = ns;
+    }
+  }
+  long keys = (cap + best_ns - 1) / best_ns;
+  keys = ((keys + stdb::VF_CHUNK - 1) / stdb::VF_CHUNK) * stdb::VF_CHUNK;
+  if (keys < stdb::VF_CHUNK) keys = stdb::VF_CHUNK;
+  return static_cast<int>(keys);
+}
+
 extern "C" size_t std_verify_attn_workspace_bytes(int B, int Hkv, int cap) {
-  const size_t max_splits = (cap + stdb::VF_SPLIT - 1) / stdb::VF_SPLIT;
+  const int split_keys = verify_split_keys(B, Hkv, cap);
+  const size_t max_splits = (cap + split_keys - 1) / split_keys;
   const size_t n = static_cast<size_t>(B) * Hkv;
-  size_t bytes = ((n * 4 + 255) / 256) * 256;
-  bytes += n * max_splits * 128 * 2 * 4;
+  size_t bytes = n * max_splits * 128 * 2 * 4;
   bytes = ((bytes + 255) / 256) * 256;
   bytes += n * max_splits * 128 * stdb::VF_D * 4;
   return bytes;
@@ -442,8 +481,8 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
   }
   CUtensorMap tk, tv;
   const uint64_t rows = static_cast<uint64_t>(B) * Hkv * cap;
-  int rc = make_tmap_bf16_2d(&tk, k_cache, rows, 128, 256, 64, 128);
-  if (rc == 0) rc = make_tmap_bf16_2d(&tv, v_cache, rows, 128, 256, 64, 128);
+  int rc = make_tmap_bf16_2d(&tk, k_cache, rows, 128, 256, 64, stdb::VF_CHUNK);
+  if (rc == 0) rc = make_tmap_bf16_2d(&tv, v_cache, rows, 128, 256, 64, stdb::VF_CHUNK);
   if (rc != 0) return rc;
   stdb::VerifyParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -457,16 +496,20 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
-  p.max_splits = (cap + stdb::VF_SPLIT - 1) / stdb::VF_SPLIT;
+  p.split_keys = verify_split_keys(B, Hkv, cap);
+  p.max_splits = (cap + p.split_keys - 1) / p.split_keys;
   const size_t n = static_cast<size_t>(B) * Hkv;
   char* ws = static_cast<char*>(workspace);
-  p.counters = reinterpret_cast<int*>(ws);
-  size_t off = ((n * 4 + 255) / 256) * 256;
-  p.ws_ml = reinterpret_cast<float*>(ws + off);
-  off += n * p.max_splits * 128 * 2 * 4;
+  p.ws_ml = reinterpret_cast<float*>(ws);
+  size_t off = n * p.max_splits * 128 * 2 * 4;
   off = ((off + 255) / 256) * 256;
   p.ws_o = reinterpret_cast<float*>(ws + off);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(p.max_splits, Hkv, B);
-  stdb::verify_attn_kernel<<<grid, stdb::VF_THREADS, stdb::VF_SMEM, static_cast<cudaStream_t>(stream)>>>(tk, tv, p);
+  stdb::verify_attn_kernel<<<grid, stdb::VF_THREADS, stdb::VF_SMEM, s>>>(tk, tv, p);
+  if (p.max_splits > 1) {
+    dim3 mgrid((stdb::VF_G * nq * (stdb::VF_D / 4) + 127) / 128, Hkv, B);
+    stdb::verify_merge_kernel<<<mgrid, 128, 0, s>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

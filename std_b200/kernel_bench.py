@@ -1,0 +1,77 @@
+"""Kernel microbenchmark: one STD kernel alone, timed with CUDA events.
+
+    python -m std_b200.kernel_bench --kernel verify --B 8 --L 32906 --nq 10
+    python -m std_b200.kernel_bench --kernel draft  --B 8 --L 1025
+
+Each repetition cycles through `--caches` distinct K/V caches (default: as
+many as keep the total above 256 MB, i.e. larger than the 126 MB L2), so the
+number measures HBM, not L2.  Prints achieved algorithmic GB/s:
+  verify: B * (2048*L + 143360) bytes per launch  (K/V rows + q/out)
+  draft:  B * (2048*L + 14336)  bytes per launch
+This is also the target command of the ncu captures summarised in profiles/.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import ops
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", choices=["verify", "draft"], default="verify")
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--L", type=int, default=32906, help="keys per request (including the nq new ones)")
+    ap.add_argument("--nq", type=int, default=10)
+    ap.add_argument("--caches", type=int, default=0)
+    ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=2)
+    a = ap.parse_args()
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, L = a.B, a.L
+    cap = (L + 255) // 256 * 256
+    per_cache = 2 * B * 4 * cap * 128 * 2
+    n_caches = a.caches or max(1, min(28, (256 << 20) // per_cache + 1))
+    g = torch.Generator(device=dev).manual_seed(0)
+    ks = [torch.randn(B, 4, cap, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(n_caches)]
+    vs = [torch.randn(B, 4, cap, 128, generator=g, device=dev).to(torch.bfloat16) for _ in range(n_caches)]
+    if a.kernel == "verify":
+        q = torch.randn(B, a.nq, 28, 128, generator=g, device=dev).to(torch.bfloat16)
+        lens = torch.full((B,), L - a.nq, dtype=torch.int32, device=dev)
+
+        def run(i):
+            ops.verify_attention(q, ks[i], vs[i], lens, a.nq)
+
+        nbytes = B * (2048 * L + 143360)
+    else:
+        q = torch.randn(B, 28, 128, generator=g, device=dev).to(torch.bfloat16)
+        lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+
+        def run(i):
+            ops.draft_attention(q, ks[i], vs[i], lens, 0)
+
+        nbytes = B * (2048 * L + 14336)
+    for i in range(a.warmup):
+        run(i % n_caches)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.reps):
+        run(i % n_caches)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / a.reps
+    assert ops.device_error() == 0
+    print(json.dumps({"kernel": a.kernel, "B": B, "L": L, "nq": a.nq if a.kernel == "verify" else 1,
+                      "caches": n_caches, "launch_us": us, "algorithmic_bytes": nbytes,
+                      "achieved_gbs": nbytes / us / 1e3}))
+
+
+if __name__ == "__main__":
+    main()

@@ -35,11 +35,10 @@ def _check(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
 
 
 def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
-    """Zero-initialised scratch buffer, grown on demand, one per (kind, device).
+    """Scratch buffer, grown on demand, one per (kind, device).
 
-    The kernels leave their split counters at zero, so a buffer is zeroed only
-    when it is (re)allocated.  Allocation happens outside graph capture: call
-    each op once eagerly before capturing it.
+    Allocation happens outside graph capture: call each op once eagerly before
+    capturing it.
     """
     key = (kind, device.index if device.index is not None else torch.cuda.current_device())
     buf = _WS.get(key)

@@ -74,3 +74,25 @@ def test_public_api_and_selection():
     assert std.generate_len == 24 and std.decode_rounds >= 1
     with pytest.raises(ValueError):
         std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, verify_mode="sequential")
+
+
+def test_full_selection_accepts_nearly_everything():
+    """With every visual token kept, the sparse cache is the dense cache: drafts
+    differ from the dense model only by attention-kernel rounding, so nearly all
+    are accepted (separates a workload effect from a draft-path bug)."""
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import STDRunner, _prepare
+
+    model = Qwen25VLDecoder(TINY, seed=5)
+    V, T = 400, 16
+    inp = _inputs(2, V, T, TINY.vocab_size, TINY.hidden_size, seed=11)
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    runner = STDRunner(model, 2, layout, 48, gamma=6, k=V, ignore_eos=True)
+    runner.prefill(embeds)
+    runner.run_std()
+    st = runner.std_stats()
+    rate = sum(st["accepted"]) / sum(st["proposed"])
+    assert rate > 0.75, rate  # a broken draft path accepts ~nothing
+    std_tokens = runner.out_tokens.clone()
+    runner.run_ar()
+    assert torch.equal(std_tokens, runner.out_tokens)
