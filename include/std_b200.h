@@ -73,6 +73,25 @@ int std_verify_attn(const void* q, const void* k_cache, const void* v_cache, con
                     int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out, float* lse,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same computation as std_verify_attn, for callers that cannot allocate device
+ * memory (a serving process that keeps the whole GPU in its own pool and does
+ * not let plugins allocate; an FFI caller with no device allocator; a loop
+ * that cannot afford an allocation's device synchronisation).  It has no
+ * counterpart in the reference.  Its scratch is a fixed array of
+ * STD_VERIFY_NOALLOC_SCRATCH_BYTES inside this library, held on every GPU
+ * that loads the library until the process exits; the call allocates
+ * nothing.  Shapes whose scratch (std_verify_attn_workspace_bytes) exceeds
+ * that size are rejected with status 2.  The first call on a device looks up
+ * the array's device address with that device current; make that first call
+ * before any stream capture.  All calls share the one array: calls that can
+ * overlap on the GPU (other streams, other host threads on the same device)
+ * race and must be serialised by the caller.  Nothing in the array needs to
+ * start at zero. */
+#define STD_VERIFY_NOALLOC_SCRATCH_BYTES (32u << 20)
+int std_verify_attn_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
+                            int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out,
+                            float* lse, void* stream);
+
 /* Exact (O, LSE) merge of attention partials computed over disjoint key
  * ranges (sequence shards).  Replaces nothing in the reference (it has no
  * sequence parallelism); it is the exchange step of sharded verify.

@@ -513,3 +513,57 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
   }
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
+
+// ---------------------------------------------------------------------------
+// std_verify_attn_noalloc: the verify entry point for callers that cannot
+// allocate device memory.
+//
+// Some callers of this path are not allowed to call cudaMalloc at all: a
+// serving process that reserves the whole GPU for its own memory pool and
+// does not let plugins allocate outside it; a foreign-language host (an FFI
+// or ctypes caller without torch) that has no device allocator of its own; a
+// latency-critical loop where an allocation, which may synchronise the
+// device, is not acceptable.  For them the split-partial scratch of the
+// verify kernel lives in a fixed file-scope __device__ array instead of a
+// caller workspace.  Every GPU that loads this library holds that array
+// (STD_VERIFY_NOALLOC_SCRATCH_BYTES) until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(32) << 20;  // == STD_VERIFY_NOALLOC_SCRATCH_BYTES
+__device__ __align__(256) unsigned char g_verify_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[128] = {};  // device address of the array, per device ordinal
+
+// On the host, g_verify_noalloc_scratch only stands in for the symbol; its
+// device address is looked up once per device, with that device current.
+int noalloc_scratch_for_current_device(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 4;
+  if (dev < 0 || dev >= 128) return 3;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_verify_noalloc_scratch) != cudaSuccess || p == nullptr) return 4;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+}  // namespace
+
+extern "C" int std_verify_attn_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
+                                       int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap,
+                                       void* out, float* lse, void* stream) {
+  if (B <= 0 || Hkv <= 0 || cap <= 0) return 1;
+  if (std_verify_attn_workspace_bytes(B, Hkv, cap) > kNoAllocScratchBytes) return 2;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_for_current_device(&scratch);
+  if (rc != 0) return rc;
+  // Nothing in the scratch has to start at zero: every partial the merge
+  // reads was written by the split kernel of the same call.
+  return std_verify_attn(q, k_cache, v_cache, lens, len_offset, nq, causal, B, Hq, Hkv, D, cap, out, lse, scratch,
+                         kNoAllocScratchBytes, stream);
+}
