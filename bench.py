@@ -214,8 +214,10 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
+    torch.cuda.nvtx.range_push("std_timed")
     for _ in range(a.steps):
         runner.run_std()
+    torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize()
     barrier()
@@ -292,10 +294,11 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
 
     # ---- launches of our kernels in the timed region ----
     Lyr = c.num_hidden_layers
-    fwd = 1 + 7 * Lyr           # embed + per layer (2 rmsnorm, rope_append, attention, 2 add, silu_mul)
-    head = 2                    # final rmsnorm + argmax
+    fwd = 2 + 5 * Lyr           # embed, first rmsnorm; per layer rope_append, attention, 2 add_rmsnorm, silu_mul
+    head = 1                    # argmax (the final norm is fused into the last add_rmsnorm)
     g_ = w["gamma"]
-    per_round = g_ * fwd + (g_ - 1) * head + (fwd + head) + (fwd + head) + 1  # drafts, verify, bonus, accept
+    # drafts, verify (+1 split-merge launch per layer), bonus, accept
+    per_round = g_ * fwd + (g_ - 1) * head + (fwd + Lyr + head) + (fwd + head) + 1
     gpu_launches = a.steps * rounds_per_step * per_round
 
     # ---- e2e through the public API, host buffers ----

@@ -138,6 +138,9 @@ int std_embed(const void* table, int vocab, int H, const int32_t* tok, int tok_s
               void* out, void* stream);
 /* modeling_qwen2_5_vl.py:183-197 (Qwen2RMSNorm). */
 int std_rmsnorm(const void* x, const void* w, float eps, int M, int H, void* out, void* stream);
+/* modeling_qwen2_5_vl.py:1200-1221 + :183-197 (residual add, then the next
+ * RMSNorm): x <- bf16(x + delta) in place, out = rmsnorm(x) * w. */
+int std_add_rmsnorm(void* x, const void* delta, const void* w, float eps, int M, int H, void* out, void* stream);
 /* modeling_qwen2_5_vl.py:690-732 (RoPE, 1-D positions) + kv_cache.py:54-69
  * (KVCache.cat): rotates q and k of qkv [B*n, (Hq+2Hkv)*D], writes q_out and
  * appends k, v at cache slot slot_base[b]+slot_off+j, position

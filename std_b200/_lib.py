@@ -42,6 +42,7 @@ SIGNATURES: Dict[str, tuple] = {
     "std_compact_gather": (I, [P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
     "std_rmsnorm": (I, [P, P, F, I, I, P, P]),
+    "std_add_rmsnorm": (I, [P, P, P, F, I, I, P, P]),
     "std_rope_append": (I, [P, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I, P]),
     "std_silu_mul": (I, [P, I, I, P, P]),
     "std_add": (I, [P, P, SZ, P, P]),

@@ -39,30 +39,75 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int vocab, int H, const
 }
 
 // ------------------------------- RMSNorm -----------------------------------
-// y = bf16( w * bf16( x * rsqrt(mean(x^2) + eps) ) ), per-thread strided sums
-// then a fixed xor tree: the same order for every row count.
-template <int NT>
-__global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w, float eps, int H,
-                                                     __nv_bfloat16* out) {
-  const size_t row = blockIdx.x;
-  const __nv_bfloat16* xr = x + row * H;
-  __shared__ float s_part[NT / 32];
-  float s = 0.f;
-  for (int i = threadIdx.x; i < H; i += NT) {
-    const float v = __bfloat162float(xr[i]);
-    s = __fmaf_rn(v, v, s);
-  }
+// One block per row, one thread per 8 consecutive elements (H % 8 == 0,
+// H/8 <= 1024): every input is loaded once into registers before any store.
+// Sum of squares: per-thread sequential over its 8 values, xor tree inside
+// each warp, then warps in order -- the same order for every row count.
+STD_DEV float block_sum_ordered(float s, float* s_part) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
   if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = s;
   __syncthreads();
   float tot = 0.f;
+  const int nw = (blockDim.x + 31) >> 5;
+  for (int i = 0; i < nw; ++i) tot = __fadd_rn(tot, s_part[i]);
+  return tot;
+}
+
+STD_DEV void load8(const __nv_bfloat16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-  for (int i = 0; i < NT / 32; ++i) tot = __fadd_rn(tot, s_part[i]);
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+STD_DEV void store8(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// y = bf16( w * bf16( x * rsqrt(mean(x^2) + eps) ) );  with delta != null,
+// first x <- bf16(x + delta) (the residual add), written back in place.
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(__nv_bfloat16* __restrict__ x,
+                                                       const __nv_bfloat16* __restrict__ delta,
+                                                       const __nv_bfloat16* __restrict__ w, float eps, int H,
+                                                       __nv_bfloat16* __restrict__ out) {
+  __shared__ float s_part[32];
+  const size_t row = blockIdx.x;
+  const int c = threadIdx.x * 8;
+  const bool act = c < H;
+  float v[8], wv[8];
+  if (act) {
+    load8(x + row * H + c, v);
+    load8(w + c, wv);
+    if (delta != nullptr) {
+      float dv[8];
+      load8(delta + row * H + c, dv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = bf16_round(__fadd_rn(v[j], dv[j]));
+      store8(x + row * H + c, v);
+    }
+  }
+  float s = 0.f;
+  if (act) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s = __fmaf_rn(v[j], v[j], s);
+  }
+  const float tot = block_sum_ordered(s, s_part);
   const float inv = rsqrtf(__fadd_rn(__fdiv_rn(tot, static_cast<float>(H)), eps));
-  for (int i = threadIdx.x; i < H; i += NT) {
-    const float v = bf16_round(__fmul_rn(__bfloat162float(xr[i]), inv));
-    out[row * H + i] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(w[i]), v));
+  if (act) {
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(wv[j], bf16_round(__fmul_rn(v[j], inv)));
+    store8(out + row * H + c, y);
   }
 }
 
@@ -70,6 +115,8 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const __nv_bfloat16* x, con
 // qkv rows (b, j): [Hq*D | Hkv*D | Hkv*D].  q -> q_out [b*n+j, Hq, D];
 // k, v -> cache slot slot_base[b] + slot_off + j of [B, Hkv, cap, D].
 // position = pos_base[b] + pos_off + j; cos/sin tables [max_pos, D/2] bf16.
+// One block per token row; a thread owns 8 dims of the first half of one head
+// and the matching 8 of the second half (rotate_half pairs d and d + D/2).
 struct RopeParams {
   const __nv_bfloat16* qkv;
   int n, Hq, Hkv, D, cap, max_pos;
@@ -84,54 +131,70 @@ struct RopeParams {
   __nv_bfloat16* v_cache;
 };
 
-__global__ void rope_append_kernel(const RopeParams p) {
+__global__ void __launch_bounds__(512) rope_append_kernel(const RopeParams p) {
   const int row = blockIdx.x;
   const int b = row / p.n, j = row % p.n;
   const int heads = p.Hq + 2 * p.Hkv;
   const int half = p.D / 2;
+  const int per_head = half / 8;
+  const int h = threadIdx.x / per_head, c = (threadIdx.x % per_head) * 8;
   int pos = p.pos_base[b] + p.pos_off + j;
-  int slot = p.slot_base[b] + p.slot_off + j;
+  const int slot = p.slot_base[b] + p.slot_off + j;
   const bool slot_ok = slot >= 0 && slot < p.cap;
   if (pos < 0 || pos >= p.max_pos) {
     if (threadIdx.x == 0) std_set_error(STD_DEVERR_BOUNDS);
     pos = pos < 0 ? 0 : p.max_pos - 1;
   }
   if (!slot_ok && threadIdx.x == 0) std_set_error(STD_DEVERR_LENGTH);
-  const __nv_bfloat16* src = p.qkv + static_cast<size_t>(row) * heads * p.D;
-  const __nv_bfloat16* cr = p.cos_t + static_cast<size_t>(pos) * half;
-  const __nv_bfloat16* sr = p.sin_t + static_cast<size_t>(pos) * half;
-  for (int idx = threadIdx.x; idx < heads * p.D; idx += blockDim.x) {
-    const int h = idx / p.D, d = idx % p.D;
-    const float x = __bfloat162float(src[idx]);
-    if (h < p.Hq + p.Hkv) {
-      const float c = __bfloat162float(cr[d % half]);
-      const float s = __bfloat162float(sr[d % half]);
-      const float partner = __bfloat162float(src[h * p.D + (d < half ? d + half : d - half)]);
-      const float rot = d < half ? -partner : partner;
-      const float y = bf16_round(__fadd_rn(bf16_round(__fmul_rn(x, c)), bf16_round(__fmul_rn(rot, s))));
-      if (h < p.Hq) {
-        p.q_out[(static_cast<size_t>(row) * p.Hq + h) * p.D + d] = __float2bfloat16_rn(y);
-      } else if (slot_ok) {
-        const int kh = h - p.Hq;
-        p.k_cache[((static_cast<size_t>(b) * p.Hkv + kh) * p.cap + slot) * p.D + d] = __float2bfloat16_rn(y);
-      }
-    } else if (slot_ok) {
-      const int vh = h - p.Hq - p.Hkv;
-      p.v_cache[((static_cast<size_t>(b) * p.Hkv + vh) * p.cap + slot) * p.D + d] = src[idx];
-    }
+  if (h >= heads) return;
+  const __nv_bfloat16* src = p.qkv + (static_cast<size_t>(row) * heads + h) * p.D;
+  float lo[8], hi[8];
+  load8(src + c, lo);
+  load8(src + half + c, hi);
+  __nv_bfloat16* dst;
+  if (h < p.Hq) {
+    dst = p.q_out + (static_cast<size_t>(row) * p.Hq + h) * p.D;
+  } else if (h < p.Hq + p.Hkv) {
+    if (!slot_ok) return;
+    dst = p.k_cache + ((static_cast<size_t>(b) * p.Hkv + (h - p.Hq)) * p.cap + slot) * p.D;
+  } else {
+    if (!slot_ok) return;
+    dst = p.v_cache + ((static_cast<size_t>(b) * p.Hkv + (h - p.Hq - p.Hkv)) * p.cap + slot) * p.D;
+    store8(dst + c, lo);
+    store8(dst + half + c, hi);
+    return;
   }
+  float cs[8], sn[8];
+  load8(p.cos_t + static_cast<size_t>(pos) * half + c, cs);
+  load8(p.sin_t + static_cast<size_t>(pos) * half + c, sn);
+  float ylo[8], yhi[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    // q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16
+    ylo[k] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(lo[k], cs[k])), bf16_round(__fmul_rn(-hi[k], sn[k]))));
+    yhi[k] = bf16_round(__fadd_rn(bf16_round(__fmul_rn(hi[k], cs[k])), bf16_round(__fmul_rn(lo[k], sn[k]))));
+  }
+  store8(dst + c, ylo);
+  store8(dst + half + c, yhi);
 }
 
 // ------------------------------- SiLU * up ---------------------------------
-// gu rows: [gate (I) | up (I)]; out = bf16( bf16(silu(gate)) * up )
-__global__ void silu_mul_kernel(const __nv_bfloat16* gu, int I, size_t total, __nv_bfloat16* out) {
-  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+// gu rows: [gate (I) | up (I)]; out = bf16( bf16(silu(gate)) * up ), 8 per thread
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, size_t total8,
+                                __nv_bfloat16* __restrict__ out) {
+  const int I8 = I / 8;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total8;
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t row = idx / I, c = idx % I;
-    const float g = __bfloat162float(gu[row * 2 * I + c]);
-    const float u = __bfloat162float(gu[row * 2 * I + I + c]);
-    const float sg = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, __expf(-g))));
-    out[idx] = __float2bfloat16_rn(__fmul_rn(sg, u));
+    const size_t row = idx / I8, c = (idx % I8) * 8;
+    float g[8], u[8], y[8];
+    load8(gu + row * 2 * I + c, g);
+    load8(gu + row * 2 * I + I + c, u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float sg = bf16_round(__fdiv_rn(g[k], __fadd_rn(1.0f, __expf(-g[k]))));
+      y[k] = __fmul_rn(sg, u[k]);
+    }
+    store8(out + row * I + c, y);
   }
 }
 
@@ -305,9 +368,22 @@ extern "C" int std_embed(const void* table, int vocab, int H, const int32_t* tok
 
 extern "C" int std_rmsnorm(const void* x, const void* w, float eps, int M, int H, void* out, void* stream) {
   if (M <= 0 || H <= 0) return 1;
-  stdb::rmsnorm_kernel<256><<<M, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), eps, H,
-      static_cast<__nv_bfloat16*>(out));
+  if (H % 8 != 0 || H / 8 > 1024) return 1;
+  const int nt = ((H / 8 + 31) / 32) * 32;
+  stdb::rmsnorm_kernel<<<M, nt, 0, static_cast<cudaStream_t>(stream)>>>(
+      const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)), nullptr,
+      static_cast<const __nv_bfloat16*>(w), eps, H, static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+}
+
+extern "C" int std_add_rmsnorm(void* x, const void* delta, const void* w, float eps, int M, int H, void* out,
+                               void* stream) {
+  if (M <= 0 || H <= 0) return 1;
+  if (H % 8 != 0 || H / 8 > 1024 || delta == nullptr) return 1;
+  const int nt = ((H / 8 + 31) / 32) * 32;
+  stdb::rmsnorm_kernel<<<M, nt, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(delta), static_cast<const __nv_bfloat16*>(w),
+      eps, H, static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
 
@@ -315,7 +391,7 @@ extern "C" int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, i
                                int pos_off, const int32_t* slot_base, int slot_off, const void* cos_t,
                                const void* sin_t, int max_pos, void* q_out, void* k_cache, void* v_cache, int cap,
                                void* stream) {
-  if (B <= 0 || n <= 0 || D % 2 != 0 || cap <= 0) return 1;
+  if (B <= 0 || n <= 0 || D % 16 != 0 || cap <= 0 || (Hq + 2 * Hkv) * (D / 16) > 512) return 1;
   stdb::RopeParams p;
   p.qkv = static_cast<const __nv_bfloat16*>(qkv);
   p.n = n;
@@ -333,16 +409,17 @@ extern "C" int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, i
   p.q_out = static_cast<__nv_bfloat16*>(q_out);
   p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
   p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
-  stdb::rope_append_kernel<<<B * n, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const int nt = (((Hq + 2 * Hkv) * (D / 16) + 31) / 32) * 32;
+  stdb::rope_append_kernel<<<B * n, nt, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
 
 extern "C" int std_silu_mul(const void* gu, int M, int I, void* out, void* stream) {
-  if (M <= 0 || I <= 0) return 1;
-  const size_t total = static_cast<size_t>(M) * I;
-  const int blocks = static_cast<int>((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+  if (M <= 0 || I <= 0 || I % 8 != 0) return 1;
+  const size_t total8 = static_cast<size_t>(M) * I / 8;
+  const int blocks = static_cast<int>((total8 + 255) / 256 < 148 * 8 ? (total8 + 255) / 256 : 148 * 8);
   stdb::silu_mul_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gu), I, total, static_cast<__nv_bfloat16*>(out));
+      static_cast<const __nv_bfloat16*>(gu), I, total8, static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
 

@@ -15,7 +15,8 @@
 //   an online softmax, so every K/V byte is read from HBM once (the Triton
 //   kernel re-reads each KV head for each of its 7 query heads).  The CTAs of
 //   the cluster then combine their (m, l, O) partials through distributed
-//   shared memory -- rank 0 reads the others' smem -- so there is one launch,
+//   shared memory -- four ranks each read a quarter of the outputs from all
+//   eight ranks' smem -- so there is one launch,
 //   no global scratch and no second kernel.  Lengths come from device memory,
 //   so the launch is graph-capturable while they change between replays.
 #include <cooperative_groups.h>
@@ -45,7 +46,7 @@ struct DraftParams {
   float* lse;               // [B, Hq] natural-log LSE, may be null
 };
 
-__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
+__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS, 2)
     draft_attn_kernel(const DraftParams p) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
@@ -103,15 +104,17 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
   }
   __syncthreads();
 
-  // per-thread running state
-  const int sub = lane >> 3, part = lane & 7;  // scores: 8 lanes per key
-  float qr[DR_G][16];
+  // scores: 16 lanes per key, lane part owns dims [8*part, 8*part+8) (16 B of
+  // the 256-B key row: a half-warp reads one row without bank conflicts)
+  const int slot = lane >> 4, part = lane & 15;
+  float qr[DR_G][8];
 #pragma unroll
   for (int g = 0; g < DR_G; ++g)
 #pragma unroll
-    for (int j = 0; j < 16; ++j) qr[g][j] = sQ[g][part * 16 + j];
-  const int od = tid & (DR_D - 1), hs = tid >> 7;  // PV: dim od, heads hs, hs+2, ...
-  float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < 8; ++j) qr[g][j] = sQ[g][part * 8 + j];
+  // PV: thread owns dims (2*dp, 2*dp+1) of heads hg and hg+4
+  const int dp = tid & 63, hg = tid >> 6;
+  float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
   float m_run = -INFINITY, l_run = 0.f;  // meaningful in warp g's lanes (softmax of head g)
   bool ok = true;
 
@@ -119,25 +122,21 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
     const int st = i & 1;
     const int nk = min(DR_SUB, k1 - (k0 + i * DR_SUB));
     if (ok) ok = mbar_wait(&bar[st], (i >> 1) & 1);
-    // scores
-    for (int kb = warp * 4 + sub; kb < DR_SUB; kb += 32) {
+#pragma unroll 1
+    for (int kb = warp * 2 + slot; kb < DR_SUB; kb += 16) {
       float acc[DR_G];
 #pragma unroll
       for (int g = 0; g < DR_G; ++g) acc[g] = 0.f;
       if (kb < nk) {
-        const uint4* kr = reinterpret_cast<const uint4*>(sK[st] + kb * DR_D + part * 16);
+        const uint4 u = *reinterpret_cast<const uint4*>(sK[st] + kb * DR_D + part * 8);
+        const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint4 u = kr[h];
-          const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&u);
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __bfloat1622float2(e[j]);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(e[j]);
-#pragma unroll
-            for (int g = 0; g < DR_G; ++g) {
-              acc[g] = fmaf(qr[g][h * 8 + 2 * j], f.x, acc[g]);
-              acc[g] = fmaf(qr[g][h * 8 + 2 * j + 1], f.y, acc[g]);
-            }
+          for (int g = 0; g < DR_G; ++g) {
+            acc[g] = fmaf(qr[g][2 * j], f.x, acc[g]);
+            acc[g] = fmaf(qr[g][2 * j + 1], f.y, acc[g]);
           }
         }
       }
@@ -147,6 +146,7 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
         x += __shfl_xor_sync(0xffffffffu, x, 1);
         x += __shfl_xor_sync(0xffffffffu, x, 2);
         x += __shfl_xor_sync(0xffffffffu, x, 4);
+        x += __shfl_xor_sync(0xffffffffu, x, 8);
         if (part == 0) sS[g][kb] = (kb < nk && ok) ? x * p.scale_log2 : -INFINITY;
       }
     }
@@ -168,17 +168,24 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
     }
     __syncthreads();
     // O = O * alpha + P V
-#pragma unroll
-    for (int hh = 0; hh < 4; ++hh) {
-      const int g = hs + 2 * hh;
-      if (g < DR_G) o[hh] *= sAlpha[g];
-    }
-    for (int j = 0; j < nk; ++j) {
-      const float vv = __bfloat162float(sV[st][j * DR_D + od]);
-#pragma unroll
-      for (int hh = 0; hh < 4; ++hh) {
-        const int g = hs + 2 * hh;
-        if (g < DR_G) o[hh] = fmaf(sS[g][j], vv, o[hh]);
+    {
+      const bool h1 = hg + 4 < DR_G;
+      const float a0 = sAlpha[hg], a1 = h1 ? sAlpha[hg + 4] : 0.f;
+      o[0][0] *= a0;
+      o[0][1] *= a0;
+      o[1][0] *= a1;
+      o[1][1] *= a1;
+      const __nv_bfloat162* vcol = reinterpret_cast<const __nv_bfloat162*>(sV[st]) + dp;
+      const float* p0 = sS[hg];
+      const float* p1 = sS[h1 ? hg + 4 : hg];
+#pragma unroll 4
+      for (int j = 0; j < nk; ++j) {
+        const float2 vv = __bfloat1622float2(vcol[j * (DR_D / 2)]);
+        const float w0 = p0[j], w1 = p1[j];
+        o[0][0] = fmaf(w0, vv.x, o[0][0]);
+        o[0][1] = fmaf(w0, vv.y, o[0][1]);
+        o[1][0] = fmaf(w1, vv.x, o[1][0]);
+        o[1][1] = fmaf(w1, vv.y, o[1][1]);
       }
     }
     __syncthreads();  // stage st and sS free
@@ -186,33 +193,40 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
   }
 
   // publish this CTA's partial to the cluster
-#pragma unroll
-  for (int hh = 0; hh < 4; ++hh) {
-    const int g = hs + 2 * hh;
-    if (g < DR_G) po[g][od] = o[hh];
+  po[hg][2 * dp] = o[0][0];
+  po[hg][2 * dp + 1] = o[0][1];
+  if (hg + 4 < DR_G) {
+    po[hg + 4][2 * dp] = o[1][0];
+    po[hg + 4][2 * dp + 1] = o[1][1];
   }
   if (warp < DR_G && lane == 0) {
     pm[warp] = (l_run > 0.f) ? m_run : -INFINITY;
     pl[warp] = l_run;
   }
   cluster.sync();
-  if (rank == 0) {
-    for (int idx = tid; idx < DR_G * DR_D; idx += DR_THREADS) {
+  // Combine: output element idx = rank * DR_THREADS + tid (ranks 0..3 cover the
+  // 7 x 128 outputs); the 8 ranks' partials are read over DSMEM, loads unrolled.
+  {
+    const int idx = rank * DR_THREADS + tid;
+    if (idx < DR_G * DR_D) {
       const int g = idx / DR_D, d = idx % DR_D;
-      float mr[DR_CLUSTER];
-      float m = -INFINITY;
+      float mr[DR_CLUSTER], lr[DR_CLUSTER], orr[DR_CLUSTER];
 #pragma unroll
       for (int r = 0; r < DR_CLUSTER; ++r) {
         mr[r] = *cluster.map_shared_rank(&pm[g], r);
-        m = fmaxf(m, mr[r]);
+        lr[r] = *cluster.map_shared_rank(&pl[g], r);
+        orr[r] = *cluster.map_shared_rank(&po[g][d], r);
       }
+      float m = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < DR_CLUSTER; ++r) m = fmaxf(m, mr[r]);
       float l = 0.f, acc = 0.f;
 #pragma unroll
       for (int r = 0; r < DR_CLUSTER; ++r) {
         if (mr[r] == -INFINITY) continue;
         const float w = exp2f(mr[r] - m);
-        l += w * *cluster.map_shared_rank(&pl[g], r);
-        acc += w * *cluster.map_shared_rank(&po[g][d], r);
+        l += w * lr[r];
+        acc += w * orr[r];
       }
       p.out[(static_cast<size_t>(b) * p.Hq + kvh * DR_G + g) * DR_D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
       if (d == 0 && p.lse != nullptr)
@@ -220,7 +234,7 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS)
             l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
     }
   }
-  cluster.sync();  // keep every CTA's smem alive until rank 0 has read it
+  cluster.sync();  // keep every CTA's smem alive until the others have read it
 }
 
 }  // namespace stdb
@@ -248,7 +262,9 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(stdb::draft_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, stdb::DR_SMEM) !=
-        cudaSuccess)
+            cudaSuccess ||
+        cudaFuncSetAttribute(stdb::draft_attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return 3;
     attr_set = true;
   }

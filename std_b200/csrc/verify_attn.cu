@@ -454,6 +454,7 @@ static int verify_split_keys(int B, int Hkv, int cap) {
 }
 
 extern "C" size_t std_verify_attn_workspace_bytes(int B, int Hkv, int cap) {
+  if (B <= 0 || Hkv <= 0 || cap <= 0) return 0;
   const int split_keys = verify_split_keys(B, Hkv, cap);
   const size_t max_splits = (cap + split_keys - 1) / split_keys;
   const size_t n = static_cast<size_t>(B) * Hkv;

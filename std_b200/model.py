@@ -167,9 +167,10 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     cos_t, sin_t = model.cos_t, model.sin_t
     x, h = ws.x[:rows], ws.h[:rows]
     ops.embed(model.embed, tok, tok_start, n, ws.x[:M])
+    ops.rmsnorm(x, model.layers[0].w_in, c.rms_norm_eps, h)
+    n_layers = len(model.layers)
     for li, lw in enumerate(model.layers):
         kc, vc = cache[li, 0], cache[li, 1]
-        ops.rmsnorm(x, lw.w_in, c.rms_norm_eps, h)
         _mm(h, lw.w_qkv, ws.qkv[:rows], lw.b_qkv)
         ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
                         ws.q[:M], kc, vc)
@@ -179,15 +180,18 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
             ops.verify_attention(ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset,
                                  out=ws.attn[:M].view(B, n, Hq, D))
         _mm(ws.attn[:rows], lw.w_o, ws.o[:rows])
-        ops.add(x, ws.o[:rows], x)
-        ops.rmsnorm(x, lw.w_post, c.rms_norm_eps, h)
+        ops.add_rmsnorm(x, ws.o[:rows], lw.w_post, c.rms_norm_eps, h)
         _mm(h, lw.w_gu, ws.gu[:rows])
         ops.silu_mul(ws.gu[:rows], ws.act[:rows])
         _mm(ws.act[:rows], lw.w_down, ws.o[:rows])
-        ops.add(x, ws.o[:rows], x)
+        if li + 1 < n_layers:
+            ops.add_rmsnorm(x, ws.o[:rows], model.layers[li + 1].w_in, c.rms_norm_eps, h)
+        elif argmax_out is not None:
+            ops.add_rmsnorm(x, ws.o[:rows], model.norm, c.rms_norm_eps, h)
+        else:
+            ops.add(x, ws.o[:rows], x)
     if argmax_out is None:
         return
-    ops.rmsnorm(x, model.norm, c.rms_norm_eps, h)
     _mm(h, model.lm_head, ws.logits[:rows])
     ops.argmax_rows(ws.logits[:M], argmax_out, n=n, out_stride=argmax_stride, out_start=argmax_start)
 

@@ -176,6 +176,15 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor):
     return out
 
 
+def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor):
+    """x <- x + delta (bf16, in place); out = rmsnorm(x) * w."""
+    H = x.shape[-1]
+    M = x.numel() // H
+    _lib.call("std_add_rmsnorm", x.data_ptr(), delta.data_ptr(), w.data_ptr(), float(eps), M, H, out.data_ptr(),
+              _stream())
+    return out
+
+
 def rope_append(qkv: torch.Tensor, B: int, n: int, Hq: int, Hkv: int, D: int, pos_base: torch.Tensor, pos_off: int,
                 slot_base: torch.Tensor, slot_off: int, cos_t: torch.Tensor, sin_t: torch.Tensor,
                 q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor):
