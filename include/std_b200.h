@@ -157,6 +157,16 @@ int std_add(const void* a, const void* b, size_t n, void* out, void* stream);
 int std_argmax_rows(const void* logits, int rows, int V, int n, int out_stride, int out_start, int32_t* out,
                     void* stream);
 
+/* Decode-time linear layer: y[M, N] = x[M, K] . w[N, K]^T (+ bias[N]), bf16,
+ * fp32 accumulation, tcgen05 weight streaming; replaces the cuBLAS GEMMs of
+ * the decode forwards (modeling_qwen2_5_vl.py:778-781 q/k/v/o projections,
+ * :674-687 Qwen2MLP, :1749 lm_head).  M <= 256, K % 64 == 0, N % 4 == 0.
+ * A row's result does not depend on the other rows for a fixed M.  The
+ * workspace holds split-K partials (0 bytes when the shape needs none). */
+size_t std_gemm_workspace_bytes(int M, int N, int K);
+int std_gemm_bf16(const void* x, const void* w, const void* bias, void* y, int M, int N, int K, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* ---- (d) fused greedy acceptance + rollback ---------------------------- */
 
 /* Replaces: std_qwen25vl.py:806-815 (argmax compare, accepted prefix, bonus),

@@ -40,6 +40,8 @@ SIGNATURES: Dict[str, tuple] = {
     "std_select_probs_view": (I, [I, I, I, P]),
     "std_topk_select": (I, [PF, I64, I, PI32, I, I, PI32, P]),
     "std_compact_gather": (I, [P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P]),
+    "std_gemm_workspace_bytes": (SZ, [I, I, I]),
+    "std_gemm_bf16": (I, [P, P, P, P, I, I, I, P, SZ, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
     "std_rmsnorm": (I, [P, P, F, I, I, P, P]),
     "std_add_rmsnorm": (I, [P, P, P, F, I, I, P, P]),

@@ -225,6 +225,12 @@ STD_DEV float ex2_approx(float x) {
   return y;
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue (launch_dependents), and wait for the previous kernel's completion
+// and memory (wait; a no-op when the launch had no programmatic dependency).
+STD_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+STD_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier over the first `nthreads` threads of the block (id 1..15).
 STD_DEV void named_bar_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory"); }
 

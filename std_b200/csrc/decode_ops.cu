@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(__nv_bfloat16* __restrict
                                                        const __nv_bfloat16* __restrict__ w, float eps, int H,
                                                        __nv_bfloat16* __restrict__ out) {
   __shared__ float s_part[32];
+  pdl_launch_dependents();  // the following GEMM may start streaming its weights
   const size_t row = blockIdx.x;
   const int c = threadIdx.x * 8;
   const bool act = c < H;
@@ -182,6 +183,7 @@ __global__ void __launch_bounds__(512) rope_append_kernel(const RopeParams p) {
 // gu rows: [gate (I) | up (I)]; out = bf16( bf16(silu(gate)) * up ), 8 per thread
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, size_t total8,
                                 __nv_bfloat16* __restrict__ out) {
+  pdl_launch_dependents();
   const int I8 = I / 8;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total8;
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {

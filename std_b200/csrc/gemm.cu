@@ -1,0 +1,284 @@
+// gemm.cu -- weight-streaming skinny GEMM on tcgen05 for the decode forwards.
+//
+//   Y[M, N] = X[M, K] . W[N, K]^T (+ bias[N]),  bf16 in, fp32 accumulate, bf16 out
+//
+// Replaces the cuBLAS calls behind the decoder's nn.Linear layers during decode
+// (modeling_qwen2_5_vl.py: q/k/v/o projections :778-781, Qwen2MLP :674-687,
+// lm_head :1749) for M <= 256 tokens, where the op streams the weights once
+// and is HBM-bound (a 7B forward reads 14.1 GB of weights).
+//
+// The weights are the MMA's M=128 operand (128 output features per CTA) and
+// the tokens its N operand (padded to a multiple of 16), so the tensor-core
+// work scales with the token count, not with a 128-row tile.  A TMA warp
+// streams 128x64 weight tiles and nmma x 64 token tiles (128-B swizzle)
+// through a ring of 2..8 stages (as many as fit two CTAs per SM); one thread issues tcgen05.mma (M128, N=nmma,
+// K16) into a TMEM accumulator; then all four warps drain TMEM (one output
+// feature per thread, tokens along the columns) with coalesced bf16 stores.
+// K is split into `splits` contiguous ranges chosen from (N, K) alone; split
+// partials (fp32) are summed by gemm_reduce_kernel in split order.
+//
+// Row invariance: a token's output depends only on its own X row, the weights,
+// the (N, K)-fixed split and the MMA N (the padded token count) -- not on the
+// other rows -- so callers that keep the padded count fixed (the dense decode
+// forwards) get bit-identical rows for AR steps and verify blocks.
+#include "common.cuh"
+
+namespace stdb {
+
+constexpr int GM_BM = 128;         // output features per CTA (MMA M)
+constexpr int GM_BK = 64;          // K per stage (one 128-B swizzle row)
+constexpr int GM_MAX_STAGES = 8;
+constexpr uint32_t GM_SMEM_BUDGET = 104 * 1024;  // per CTA: two CTAs per SM
+constexpr int GM_THREADS = 128;
+constexpr uint32_t GM_WTILE = GM_BM * GM_BK * 2;  // 16 KB
+
+struct GemmParams {
+  int M, N, K, nmma, splits, kblocks, stages;
+  const __nv_bfloat16* bias;  // [N] or null
+  __nv_bfloat16* y;           // [M, N]
+  float* partial;             // [splits, M, N] (splits > 1)
+};
+
+__global__ void __launch_bounds__(GM_THREADS)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                const GemmParams p) {
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb0 = static_cast<int>((static_cast<long>(split) * p.kblocks) / p.splits);
+  const int kb1 = static_cast<int>((static_cast<long>(split + 1) * p.kblocks) / p.splits);
+  const int nkb = kb1 - kb0;
+  const int n0 = tile * GM_BM;
+  const uint32_t xtile = static_cast<uint32_t>(p.nmma) * GM_BK * 2;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint8_t* sW = smem;                 // [S][16 KB]
+  uint8_t* sX = smem + S * GM_WTILE;  // [S][xtile]
+  __shared__ __align__(8) uint64_t bar_full[GM_MAX_STAGES], bar_empty[GM_MAX_STAGES], bar_done;
+  __shared__ uint32_t s_tmem;
+
+  uint32_t ncols = 32;
+  while (ncols < static_cast<uint32_t>(p.nmma)) ncols <<= 1;
+  if (warp == 1) {
+    tmem_alloc(&s_tmem, ncols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&bar_full[i], 1);
+      mbar_init(&bar_empty[i], 1);
+    }
+    mbar_init(&bar_done, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tmW);
+    prefetch_tensormap(&tmX);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    // The weights do not depend on the previous kernel: the first stages'
+    // weight tiles are requested before waiting for it (programmatic
+    // dependent launch), the token tiles only after.
+    const int pre = nkb < S ? nkb : S;
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&bar_full[i], GM_WTILE + xtile);
+      tma_load_2d(sW + i * GM_WTILE, &tmW, &bar_full[i], (kb0 + i) * GM_BK, n0);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * xtile, &tmX, &bar_full[i], (kb0 + i) * GM_BK, 0);
+    int issued = pre;
+    for (int i = pre; i < nkb; ++i) {
+      const int st = i % S;
+      if (!mbar_wait(&bar_empty[st], ((i / S) - 1) & 1)) break;
+      mbar_arrive_expect_tx(&bar_full[st], GM_WTILE + xtile);
+      const int kx = (kb0 + i) * GM_BK;
+      tma_load_2d(sW + st * GM_WTILE, &tmW, &bar_full[st], kx, n0);
+      tma_load_2d(sX + st * xtile, &tmX, &bar_full[st], kx, 0);
+      issued = i + 1;
+    }
+    for (int i = issued - S < 0 ? 0 : issued - S; i < issued; ++i) mbar_wait(&bar_full[i % S], (i / S) & 1);
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    const uint32_t idesc = idesc_bf16_f32(GM_BM, p.nmma, 0, 0);
+    for (int i = 0; i < nkb; ++i) {
+      const int st = i % S;
+      if (!mbar_wait(&bar_full[st], (i / S) & 1)) break;
+      tc_fence_after();
+      const uint32_t aW = smem_u32(sW + st * GM_WTILE), aX = smem_u32(sX + st * xtile);
+#pragma unroll
+      for (int ks = 0; ks < GM_BK / 16; ++ks)
+        umma_bf16(tmem, sdesc_sw128(aW + ks * 32u, 16, 1024), sdesc_sw128(aX + ks * 32u, 16, 1024), idesc,
+                  (i > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(&bar_empty[st]);
+    }
+    umma_commit(&bar_done);
+  }
+
+  // ---- epilogue: thread = output feature, columns = tokens ----
+  mbar_wait(&bar_done, 0);
+  pdl_wait();                 // every thread: the previous kernel is complete before any store
+  pdl_launch_dependents();    // the next kernel may start its prologue
+  __syncwarp();
+  tc_fence_after();
+  const int f = n0 + warp * 32 + lane;
+  const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const float bias = (p.splits == 1 && p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
+  // ncols is a power of two >= max(nmma, 32), so 32-column loads stay inside it
+  for (int t0 = 0; t0 < p.nmma; t0 += 32) {
+    uint32_t v[32];
+    tmem_ld32(trow + t0, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = t0 + j;
+      if (t >= p.M || f >= p.N) continue;
+      const float acc = __uint_as_float(v[j]);
+      if (p.splits == 1)
+        p.y[static_cast<size_t>(t) * p.N + f] = __float2bfloat16_rn(acc + bias);
+      else
+        p.partial[(static_cast<size_t>(split) * p.M + t) * p.N + f] = acc;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+// y[t, f] = bf16( sum_s partial[s, t, f] + bias[f] ), splits in order
+__global__ void gemm_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
+                                   const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t total = static_cast<size_t>(M) * N / 4;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float4 a = reinterpret_cast<const float4*>(partial)[i];
+    for (int s = 1; s < splits; ++s) {
+      const float4 b = reinterpret_cast<const float4*>(partial + static_cast<size_t>(s) * M * N)[i];
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    const int f = static_cast<int>((i * 4) % N);
+    if (bias != nullptr) {
+      a.x += __bfloat162float(bias[f]);
+      a.y += __bfloat162float(bias[f + 1]);
+      a.z += __bfloat162float(bias[f + 2]);
+      a.w += __bfloat162float(bias[f + 3]);
+    }
+    uint2 u;
+    u.x = pack_bf16x2(a.x, a.y);
+    u.y = pack_bf16x2(a.z, a.w);
+    reinterpret_cast<uint2*>(y)[i] = u;
+  }
+}
+
+}  // namespace stdb
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+// K splits from (N, K) only: fill whole waves of two resident CTAs per SM.
+static int gemm_splits(int N, int K) {
+  const long tiles = (N + stdb::GM_BM - 1) / stdb::GM_BM;
+  const long kblocks = K / stdb::GM_BK;
+  const long slots = 2L * 148;
+  if (tiles >= slots / 2) return 1;  // enough tiles to stream the weights without splitting K
+  long best = 1;
+  double best_eff = -1.0;
+  for (long s = 1; s <= kblocks / 2 && s <= 16; ++s) {
+    const long ctas = tiles * s;
+    const double eff = static_cast<double>(ctas) / (static_cast<double>((ctas + slots - 1) / slots) * slots);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return static_cast<int>(best);
+}
+
+static int gemm_nmma(int M) { return ((M + 15) / 16) * 16; }
+
+extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const int s = gemm_splits(N, K);
+  return s > 1 ? static_cast<size_t>(s) * M * N * 4 : 0;
+}
+
+extern "C" int std_gemm_bf16(const void* x, const void* w, const void* bias, void* y, int M, int N, int K,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % stdb::GM_BK != 0 || N % 4 != 0) return 1;
+  if (x == nullptr || w == nullptr || y == nullptr) return 1;
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) != 0) return 1;
+  const int splits = gemm_splits(N, K);
+  const size_t need = std_gemm_workspace_bytes(M, N, K);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return 5;
+  const int nmma = gemm_nmma(M);
+  const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
+  int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
+  stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
+  const size_t smem = static_cast<size_t>(stages) * stage_bytes + 1024;
+  static size_t attr_smem = 0;
+  if (smem > attr_smem) {
+    if (cudaFuncSetAttribute(stdb::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return 3;
+    attr_smem = smem;
+  }
+  CUtensorMap tw, tx;
+  int rc = make_tmap_bf16_2d(&tw, w, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
+                             static_cast<uint64_t>(K) * 2, stdb::GM_BK, stdb::GM_BM);
+  if (rc == 0)
+    rc = make_tmap_bf16_2d(&tx, x, static_cast<uint64_t>(M), static_cast<uint64_t>(K), static_cast<uint64_t>(K) * 2,
+                           stdb::GM_BK, static_cast<uint32_t>(nmma));
+  if (rc != 0) return rc;
+  stdb::GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.nmma = nmma;
+  p.splits = splits;
+  p.kblocks = K / stdb::GM_BK;
+  p.stages = stages;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.partial = static_cast<float*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // both launches may begin while the previous kernel in the stream finishes
+  // (programmatic dependent launch); the kernels wait before touching its data
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits);
+  cfg.blockDim = dim3(stdb::GM_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, stdb::gemm_kernel, tw, tx, p) != cudaSuccess) return 4;
+  if (splits > 1) {
+    const size_t total4 = static_cast<size_t>(M) * N / 4;
+    const int blocks = static_cast<int>((total4 + 255) / 256 < 1184 ? (total4 + 255) / 256 : 1184);
+    cudaLaunchConfig_t rc2 = {};
+    rc2.gridDim = dim3(blocks);
+    rc2.blockDim = dim3(256);
+    rc2.stream = s;
+    rc2.attrs = attr;
+    rc2.numAttrs = 1;
+    if (cudaLaunchKernelEx(&rc2, stdb::gemm_reduce_kernel, static_cast<const float*>(p.partial), splits, M, N,
+                           p.bias, p.y) != cudaSuccess)
+      return 4;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+}

@@ -2,12 +2,14 @@
 
     python -m std_b200.kernel_bench --kernel verify --B 8 --L 32906 --nq 10
     python -m std_b200.kernel_bench --kernel draft  --B 8 --L 1025
+    python -m std_b200.kernel_bench --kernel gemm   --M 8 --N 4608 --K 3584 [--cublas]
 
 Each repetition cycles through `--caches` distinct K/V caches (default: as
 many as keep the total above 256 MB, i.e. larger than the 126 MB L2), so the
 number measures HBM, not L2.  Prints achieved algorithmic GB/s:
   verify: B * (2048*L + 143360) bytes per launch  (K/V rows + q/out)
   draft:  B * (2048*L + 14336)  bytes per launch
+  gemm:   2*N*K (weights) + 2*M*K + 2*M*N bytes per launch
 This is also the target command of the ncu captures summarised in profiles/.
 """
 
@@ -23,7 +25,11 @@ from . import ops
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["verify", "draft"], default="verify")
+    ap.add_argument("--kernel", choices=["verify", "draft", "gemm"], default="verify")
+    ap.add_argument("--M", type=int, default=8)
+    ap.add_argument("--N", type=int, default=4608)
+    ap.add_argument("--K", type=int, default=3584)
+    ap.add_argument("--cublas", action="store_true", help="time torch.mm (cuBLAS) on the same shapes instead")
     ap.add_argument("--B", type=int, default=8)
     ap.add_argument("--L", type=int, default=32906, help="keys per request (including the nq new ones)")
     ap.add_argument("--nq", type=int, default=10)
@@ -34,6 +40,8 @@ def main() -> None:
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if a.kernel == "gemm":
+        return gemm_bench(a, dev)
     B, L = a.B, a.L
     cap = (L + 255) // 256 * 256
     per_cache = 2 * B * 4 * cap * 128 * 2
@@ -71,6 +79,37 @@ def main() -> None:
     print(json.dumps({"kernel": a.kernel, "B": B, "L": L, "nq": a.nq if a.kernel == "verify" else 1,
                       "caches": n_caches, "launch_us": us, "algorithmic_bytes": nbytes,
                       "achieved_gbs": nbytes / us / 1e3}))
+
+
+def gemm_bench(a, dev) -> None:
+    M, N, K = a.M, a.N, a.K
+    per = N * K * 2
+    n_w = a.caches or max(2, min(64, (512 << 20) // per + 1))
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = [(torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(n_w)]
+    x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+
+    def run(i):
+        if a.cublas:
+            torch.mm(x, ws[i].t(), out=y)
+        else:
+            ops.gemm(x, ws[i], y)
+
+    for i in range(max(a.warmup, 2)):
+        run(i % n_w)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(a.reps, n_w)
+    e0.record()
+    for i in range(reps):
+        run(i % n_w)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / reps
+    nbytes = 2 * N * K + 2 * M * K + 2 * M * N
+    print(json.dumps({"kernel": "cublas" if a.cublas else "gemm", "M": M, "N": N, "K": K, "weights": n_w,
+                      "launch_us": us, "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / us / 1e3}))
 
 
 if __name__ == "__main__":

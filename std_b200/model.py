@@ -8,13 +8,12 @@ Positions are 1-D (the fork disables get_rope_index, :2074-2105), so M-RoPE
 reduces to ordinary RoPE with theta = 1e6.
 
 Compute split:
-  * projections, MLP and lm_head: cuBLAS GEMMs through torch (torch.addmm/mm
-    with preallocated outputs);
-  * everything else on the decode path: libstd_b200.so kernels (RMSNorm,
-    RoPE + KV append, draft / verify attention, SiLU*up, residual add,
-    argmax);
-  * prefill attention: torch SDPA (a library flash/efficient kernel), as the
-    reference does.
+  * decode forwards: every kernel is from libstd_b200.so -- the tcgen05
+    weight-streaming GEMM for projections, MLP and lm_head, RMSNorm (fused
+    with the residual add), RoPE + KV append, draft / verify attention,
+    SiLU*up, argmax;
+  * prefill (thousands of rows): cuBLAS GEMMs through torch and torch SDPA
+    attention (library flash/efficient kernels), as the reference does.
 Dense decode forwards (AR steps and verify) always run their GEMMs on the same
 padded row count, and every other kernel on the decode path is row
 independent, so a token gets bit-identical logits whether it is verified in a
@@ -141,11 +140,8 @@ class Workspace:
 
 
 def _mm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[torch.Tensor] = None):
-    if bias is None:
-        torch.mm(x, w.t(), out=out)
-    else:
-        torch.addmm(bias, x, w.t(), out=out)
-    return out
+    """Decode-forward linear layer: the tcgen05 weight-streaming GEMM (ops.gemm)."""
+    return ops.gemm(x, w, out, bias)
 
 
 def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *, B: int, n: int, rows: int,

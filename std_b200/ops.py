@@ -176,6 +176,20 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor):
     return out
 
 
+def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[torch.Tensor] = None):
+    """out[M, N] = x[M, K] @ w[N, K]^T (+ bias) on the tcgen05 weight-streaming GEMM (M <= 256)."""
+    M, K = x.shape
+    N = w.shape[0]
+    _check(x, torch.bfloat16, "x")
+    _check(w, torch.bfloat16, "w")
+    _check(out, torch.bfloat16, "out")
+    nb = _lib.query("std_gemm_workspace_bytes", M, N, K)
+    ws = workspace("gemm", nb, x.device) if nb > 0 else None
+    _lib.call("std_gemm_bf16", x.data_ptr(), w.data_ptr(), _p(bias), out.data_ptr(), M, N, K, _p(ws),
+              0 if ws is None else ws.numel(), _stream())
+    return out
+
+
 def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor):
     """x <- x + delta (bf16, in place); out = rmsnorm(x) * w."""
     H = x.shape[-1]

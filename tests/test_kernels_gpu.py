@@ -337,3 +337,39 @@ def test_rmsnorm_rope_silu_argmax(ops):
             assert torch.equal(kc[b, :, slot], kh * c + rotk * s)
             assert torch.equal(vc[b, :, slot], qkv[r, (Hq + Hkv) * D:].view(Hkv, D))
     _no_device_error(ops)
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("M", [1, 8, 16, 80, 128, 200])
+@pytest.mark.parametrize("N,K,bias", [(4608, 3584, True), (3584, 18944, False), (37888, 3584, False),
+                                      (1152, 896, True)])
+def test_gemm_vs_fp32(ops, M, N, K, bias):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g, device="cuda") * 0.1).to(torch.bfloat16) if bias else None
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, w, y, b)
+    ref = x.float() @ w.float().t()
+    if b is not None:
+        ref = ref + b.float()
+    err = (y.float() - ref).abs()
+    scale = ref.abs().max().item()
+    assert err.max().item() <= 0.01 * scale + 1e-3, err.max().item()
+    assert err.mean().item() <= 0.002 * scale
+    _no_device_error(ops)
+
+
+def test_gemm_rows_independent_of_other_rows(ops):
+    """Fixed padded row count: a row's output does not depend on the other rows."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    M, N, K = 80, 3584, 18944
+    x1 = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    x2 = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    for j in (0, 9, 47, 79):
+        x2[j] = x1[j]
+    y1 = ops.gemm(x1, w, torch.empty(M, N, dtype=torch.bfloat16, device="cuda"))
+    y2 = ops.gemm(x2, w, torch.empty(M, N, dtype=torch.bfloat16, device="cuda"))
+    for j in (0, 9, 47, 79):
+        assert torch.equal(y1[j], y2[j])
