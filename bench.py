@@ -152,6 +152,7 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     from std_b200 import ops
     from std_b200.model import QWEN25_VL_7B, Qwen25VLDecoder
     from std_b200.std_qwen25vl import PromptLayout, STDRunner, std_generate_qwen25vl
+    from std_b200.timing import graph_time_us
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -249,34 +250,19 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     qv = torch.randn(B, nq, c.num_attention_heads, c.head_dim, device=dev).to(torch.bfloat16)
     ov = torch.empty_like(qv)
     lens_v = runner.dense_len  # = P for every request after reset
-    for li in range(c.num_hidden_layers):  # warm (workspaces, tensor maps)
-        ops.verify_attention(qv, runner.dense[li, 0], runner.dense[li, 1], lens_v, nq, out=ov)
-    reps = 4
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps):
-        for li in range(c.num_hidden_layers):  # 28 distinct caches, > L2 in total
-            ops.verify_attention(qv, runner.dense[li, 0], runner.dense[li, 1], lens_v, nq, out=ov)
-    e1.record()
-    torch.cuda.synchronize()
-    t_verify = e0.elapsed_time(e1) / 1000.0 / (reps * c.num_hidden_layers)
+    # 28 distinct per-layer caches (> L2 in total), launched from one CUDA graph as in the decode loop
+    t_verify = graph_time_us([lambda li=li: ops.verify_attention(qv, runner.dense[li, 0], runner.dense[li, 1],
+                                                                 lens_v, nq, out=ov)
+                              for li in range(c.num_hidden_layers)], rounds=4) / 1e6
     L = P + nq
     verify_bytes = B * (2048 * L + 143360)
     verify_flops = B * 14336 * (10 * L - 45)
     qd = torch.randn(B, c.num_attention_heads, c.head_dim, device=dev).to(torch.bfloat16)
     od = torch.empty_like(qd)
     lens_s = runner.sparse_len
-    for li in range(c.num_hidden_layers):
-        ops.draft_attention(qd, runner.sparse[li, 0], runner.sparse[li, 1], lens_s, 1, out=od)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps):
-        for li in range(c.num_hidden_layers):
-            ops.draft_attention(qd, runner.sparse[li, 0], runner.sparse[li, 1], lens_s, 1, out=od)
-    e1.record()
-    torch.cuda.synchronize()
-    t_draft = e0.elapsed_time(e1) / 1000.0 / (reps * c.num_hidden_layers)
+    t_draft = graph_time_us([lambda li=li: ops.draft_attention(qd, runner.sparse[li, 0], runner.sparse[li, 1],
+                                                               lens_s, 1, out=od)
+                             for li in range(c.num_hidden_layers)], rounds=4) / 1e6
     Ls = w["compact"] + 1
     draft_bytes = B * (2048 * Ls + 14336)
     peaks = {}

@@ -6,19 +6,28 @@
 // over the compacted sparse cache (no mask: the draft query sees every cached
 // key, std_qwen25vl.py:400-417).
 //
-// Design (HBM-bound, ~7 flop/B, and at batch 1 latency-bound): split-KV
-// flash-decoding inside one thread-block cluster per (request, KV head).
-//   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1).  CTA rank i
-//   streams keys [i*per, (i+1)*per) of the request's live length through a
-//   two-stage cp.async.bulk ring (K and V rows are contiguous in the
-//   [B, Hkv, cap, D] cache), computing all G = 7 query heads of the group with
-//   an online softmax, so every K/V byte is read from HBM once (the Triton
-//   kernel re-reads each KV head for each of its 7 query heads).  The CTAs of
-//   the cluster then combine their (m, l, O) partials through distributed
-//   shared memory -- four ranks each read a quarter of the outputs from all
-//   eight ranks' smem -- so there is one launch,
-//   no global scratch and no second kernel.  Lengths come from device memory,
-//   so the launch is graph-capturable while they change between replays.
+// Design.  The op reads 2048 B of K/V per key and does ~7 flop per byte, so it
+// is HBM-bound -- provided the math keeps up: at 6.5 TB/s the 7 query heads of
+// a KV group need ~45 TFLOP/s, more than fp32 CUDA cores sustain once the
+// conversions and reductions are counted.  So the two contractions run on the
+// tensor cores as warp-level m16n8k16 bf16 tiles (the 7 heads padded to the
+// 16-row tile), which leaves the kernel bound by the K/V stream alone.
+//
+//   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1), 4 warps/CTA.
+//   CTA rank i owns keys [i*per, (i+1)*per) of the request's live length
+//   (per = ceil(L/8) rounded up to 16).  TMA (2-D tensor maps, 128-byte
+//   swizzle, 16-row boxes, no multicast) streams its K and V rows through a
+//   two-stage ring of 64-key sub-tiles; only the boxes that hold live keys are
+//   fetched.  Each warp takes 16 keys of every sub-tile: S = Q K^T from
+//   ldmatrix'd K fragments, an online softmax on the accumulator registers,
+//   then O += P V with P reused from registers as the A operand and V
+//   fragments from ldmatrix.trans.  Every K/V byte is read from HBM once (the
+//   Triton kernel re-reads each KV head for each of its 7 query heads).
+//   The 4 warp partials are combined in shared memory, then the 8 CTAs of the
+//   cluster combine theirs through distributed shared memory (each rank
+//   finishes 112 of the 7 x 128 outputs), so there is one launch, no global
+//   scratch and no second kernel.  Lengths come from device memory, so the
+//   launch is graph-capturable while they change between replays.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -27,16 +36,22 @@ namespace stdb {
 
 constexpr int DR_D = 128;
 constexpr int DR_G = 7;
-constexpr int DR_THREADS = 256;
-constexpr int DR_SUB = 64;      // keys per pipeline stage
-constexpr int DR_CLUSTER = 8;   // CTAs per (request, KV head)
-constexpr uint32_t DR_STAGE_BYTES = DR_SUB * DR_D * 2;  // one K (or V) stage
-constexpr uint32_t DR_SMEM = 4 * DR_STAGE_BYTES + 128;  // 2 stages x (K, V) + alignment
+constexpr int DR_WARPS = 4;
+constexpr int DR_THREADS = DR_WARPS * 32;
+constexpr int DR_SUB = 64;     // keys per pipeline stage, 16 per warp
+constexpr int DR_BOX = 16;     // rows per TMA box
+constexpr int DR_STAGES = 2;
+constexpr int DR_CLUSTER = 8;  // CTAs per (request, KV head)
+constexpr uint32_t DR_HALF_BYTES = DR_SUB * 64 * 2;                // 64 keys x 64 dims (one 128-B swizzle span)
+constexpr uint32_t DR_STAGE_BYTES = 4 * DR_HALF_BYTES;             // K lo, K hi, V lo, V hi
+constexpr uint32_t DR_SMEM = DR_STAGES * DR_STAGE_BYTES + 1024;    // + alignment slack (swizzle atoms: 1 KB)
+constexpr int DR_OSTRIDE = DR_D + 4;                               // fp32 row of a warp partial (bank skew)
+constexpr int DR_OUT_PER_RANK = DR_G * DR_D / DR_CLUSTER;          // 112
+static_assert(DR_WARPS * 8 * DR_OSTRIDE * 4 + 2 * DR_WARPS * 8 * 4 <= DR_STAGES * DR_STAGE_BYTES,
+              "warp partials alias the stage buffers");
 
 struct DraftParams {
   const __nv_bfloat16* q;   // [B, Hq, D]
-  const __nv_bfloat16* k;   // [B, Hkv, cap, D]
-  const __nv_bfloat16* v;   // [B, Hkv, cap, D]
   const int32_t* lens;      // [B] device lengths
   int len_offset;           // live keys = lens[b] + len_offset
   int cap;
@@ -46,27 +61,27 @@ struct DraftParams {
   float* lse;               // [B, Hq] natural-log LSE, may be null
 };
 
-__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS, 2)
-    draft_attn_kernel(const DraftParams p) {
+// Byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled half tile.
+STD_DEV uint32_t dr_sw(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS, 3)
+    draft_attn_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                      const DraftParams p) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
 
   extern __shared__ uint8_t dsmem_raw[];
-  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 127) & ~uintptr_t(127));
-  __nv_bfloat16* sK[2] = {reinterpret_cast<__nv_bfloat16*>(sbase),
-                          reinterpret_cast<__nv_bfloat16*>(sbase + DR_STAGE_BYTES)};
-  __nv_bfloat16* sV[2] = {reinterpret_cast<__nv_bfloat16*>(sbase + 2 * DR_STAGE_BYTES),
-                          reinterpret_cast<__nv_bfloat16*>(sbase + 3 * DR_STAGE_BYTES)};
-  __shared__ float sQ[DR_G][DR_D];
-  __shared__ float sS[DR_G][DR_SUB];
-  __shared__ float sAlpha[DR_G];
-  // partials published to the cluster
+  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar[DR_STAGES];
+  // this CTA's partial, published to the cluster
   __shared__ float pm[DR_G], pl[DR_G];
   __shared__ __align__(16) float po[DR_G][DR_D];
-  __shared__ __align__(8) uint64_t bar[2];
 
   int L = p.lens[b] + p.len_offset;
   if (L > p.cap || L < 0) {
@@ -77,162 +92,201 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   per = (per + 15) & ~15;
   const int k0 = min(L, rank * per);
   const int k1 = min(L, k0 + per);
-  const int nsub = (k1 - k0 + DR_SUB - 1) / DR_SUB;
-  const size_t head_off = (static_cast<size_t>(b) * p.Hkv + kvh) * p.cap;
+  const int nkeys = k1 - k0;
+  const int nsub = (nkeys + DR_SUB - 1) / DR_SUB;
+  const int row0 = (b * p.Hkv + kvh) * p.cap + k0;  // first tensor-map row of this CTA
 
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    prefetch_tensormap(&tk);
+    prefetch_tensormap(&tv);
+#pragma unroll
+    for (int s = 0; s < DR_STAGES; ++s) mbar_init(&bar[s], 1);
     fence_barrier_init();
   }
   __syncthreads();
   auto issue = [&](int i) {
-    const int st = i & 1;
-    const int a = k0 + i * DR_SUB;
-    const uint32_t bytes = static_cast<uint32_t>(min(DR_SUB, k1 - a)) * DR_D * 2;
-    mbar_arrive_expect_tx(&bar[st], 2 * bytes);
-    bulk_load(sK[st], p.k + (head_off + a) * DR_D, bytes, &bar[st]);
-    bulk_load(sV[st], p.v + (head_off + a) * DR_D, bytes, &bar[st]);
+    const int st = i % DR_STAGES;
+    const int a = i * DR_SUB;
+    const int nbox = (min(DR_SUB, nkeys - a) + DR_BOX - 1) / DR_BOX;
+    uint8_t* s = sbase + st * DR_STAGE_BYTES;
+    mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nbox) * 4u * DR_BOX * 128u);
+    for (int j = 0; j < nbox; ++j) {
+      const int y = row0 + a + j * DR_BOX;
+      const uint32_t off = j * DR_BOX * 128;
+      tma_load_2d(s + off, &tk, &bar[st], 0, y);
+      tma_load_2d(s + DR_HALF_BYTES + off, &tk, &bar[st], 64, y);
+      tma_load_2d(s + 2 * DR_HALF_BYTES + off, &tv, &bar[st], 0, y);
+      tma_load_2d(s + 3 * DR_HALF_BYTES + off, &tv, &bar[st], 64, y);
+    }
   };
+  int issued = 0;  // sub-tiles issued so far (meaningful in thread 0)
   if (tid == 0) {
-    if (nsub > 0) issue(0);
-    if (nsub > 1) issue(1);
+    for (; issued < DR_STAGES && issued < nsub; ++issued) issue(issued);
   }
-  for (int i = tid; i < DR_G * DR_D; i += DR_THREADS) {
-    const int g = i / DR_D, d = i % DR_D;
-    sQ[g][d] = __bfloat162float(p.q[(static_cast<size_t>(b) * p.Hq + kvh * DR_G + g) * DR_D + d]);
+
+  // Q as the A operand: row gid = query head kvh*7 + gid (row 7 and rows 8..15
+  // are zero padding), k-step ks covers dims [16ks, 16ks+16).
+  uint32_t qa[8][2];
+  {
+    const bool hv = gid < DR_G;
+    const __nv_bfloat16* qrow = p.q + (static_cast<size_t>(b) * p.Hq + kvh * DR_G + (hv ? gid : 0)) * DR_D;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = hv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * tig) : 0u;
+      qa[ks][1] = hv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * tig) : 0u;
+    }
+  }
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // row gid of this warp, identical across the quad
+  bool ok = true;
+  const float sc = p.scale_log2;
+
+  for (int i = 0; i < nsub; ++i) {
+    const int st = i % DR_STAGES;
+    const int nk = min(DR_SUB, nkeys - i * DR_SUB);
+    if (ok) ok = mbar_wait(&bar[st], (i / DR_STAGES) & 1);
+    uint8_t* sK = sbase + st * DR_STAGE_BYTES;
+    uint8_t* sV = sK + 2 * DR_HALF_BYTES;
+    const int kw = warp * 16;
+    const int nvalid = min(16, nk - kw);
+    if (nvalid > 0 && ok) {
+      if (nvalid < 16) {
+        // Rows past the live length inside the last box hold whatever the
+        // cache holds there; zero their V so that P = 0 times them stays 0.
+        for (int e = lane; e < (16 - nvalid) * 16; e += 32) {
+          const int r = kw + nvalid + (e >> 4), c = e & 15;
+          *reinterpret_cast<uint4*>(sV + (c >> 3) * DR_HALF_BYTES + r * 128 + ((c & 7) << 4)) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_async_smem();
+        __syncwarp();
+      }
+      // S[16 x 16 keys] = Q K^T
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const int mi = lane >> 3;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int key = kw + (mi >> 1) * 8 + (lane & 7);
+        const int ch = (ks & 3) * 2 + (mi & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(sK + (ks >> 2) * DR_HALF_BYTES + dr_sw(key, ch)), b0, b1, b2, b3);
+        mma_bf16_16816(s[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+        mma_bf16_16816(s[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+      }
+      // online softmax on row gid (keys 2tig, 2tig+1, 8+2tig, 9+2tig)
+      float x[4];
+      x[0] = (2 * tig < nvalid) ? s[0][0] * sc : -INFINITY;
+      x[1] = (2 * tig + 1 < nvalid) ? s[0][1] * sc : -INFINITY;
+      x[2] = (8 + 2 * tig < nvalid) ? s[1][0] * sc : -INFINITY;
+      x[3] = (9 + 2 * tig < nvalid) ? s[1][1] * sc : -INFINITY;
+      float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m_run, mx);  // finite: key kw is live
+      const float alpha = ex2_approx(m_run - mn);
+      float pr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pr[e] = ex2_approx(x[e] - mn);
+      l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+      m_run = mn;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= alpha;
+        o[j][1] *= alpha;
+      }
+      const uint32_t pa0 = pack_bf16x2(pr[0], pr[1]), pa2 = pack_bf16x2(pr[2], pr[3]);
+      // O[16 x 128] += P[16 x 16 keys] V[16 keys x 128]
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const int key = kw + (mi & 1) * 8 + (lane & 7);
+        const int ch = (2 * jj & 7) + (mi >> 1);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_trans(smem_u32(sV + (jj >> 2) * DR_HALF_BYTES + dr_sw(key, ch)), v0, v1, v2, v3);
+        mma_bf16_16816(o[2 * jj], pa0, 0u, pa2, 0u, v0, v1);
+        mma_bf16_16816(o[2 * jj + 1], pa0, 0u, pa2, 0u, v2, v3);
+      }
+    }
+    __syncthreads();  // every warp is done with stage st
+    if (tid == 0 && ok && issued < nsub) issue(issued++);
+  }
+  if (tid == 0) {
+    // Normally a no-op (every issued phase has completed).  If a wait gave up,
+    // let the loads still in flight land before the stage buffers are reused
+    // or the CTA exits; these waits are bounded too.
+    for (int i = max(0, issued - DR_STAGES); i < issued; ++i) mbar_wait(&bar[i % DR_STAGES], (i / DR_STAGES) & 1);
   }
   __syncthreads();
 
-  // scores: 16 lanes per key, lane part owns dims [8*part, 8*part+8) (16 B of
-  // the 256-B key row: a half-warp reads one row without bank conflicts)
-  const int slot = lane >> 4, part = lane & 15;
-  float qr[DR_G][8];
+  // warp partials -> shared memory (the stage buffers are free now)
+  float* wo = reinterpret_cast<float*>(sbase);  // [warp][8 rows][DR_OSTRIDE]
+  float* wm = wo + DR_WARPS * 8 * DR_OSTRIDE;   // [warp][8]
+  float* wl = wm + DR_WARPS * 8;                // [warp][8]
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (gid < DR_G) {
+    float* row = wo + (warp * 8 + gid) * DR_OSTRIDE;
 #pragma unroll
-  for (int g = 0; g < DR_G; ++g)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) qr[g][j] = sQ[g][part * 8 + j];
-  // PV: thread owns dims (2*dp, 2*dp+1) of heads hg and hg+4
-  const int dp = tid & 63, hg = tid >> 6;
-  float o[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-  float m_run = -INFINITY, l_run = 0.f;  // meaningful in warp g's lanes (softmax of head g)
-  bool ok = true;
-
-  for (int i = 0; i < nsub; ++i) {
-    const int st = i & 1;
-    const int nk = min(DR_SUB, k1 - (k0 + i * DR_SUB));
-    if (ok) ok = mbar_wait(&bar[st], (i >> 1) & 1);
+    for (int j = 0; j < 16; ++j) *reinterpret_cast<float2*>(row + 8 * j + 2 * tig) = make_float2(o[j][0], o[j][1]);
+    if (tig == 0) {
+      wm[warp * 8 + gid] = (l_run > 0.f && ok) ? m_run : -INFINITY;
+      wl[warp * 8 + gid] = ok ? l_run : 0.f;
+    }
+  }
+  __syncthreads();
+  // CTA partial: thread tid owns dim tid of all 7 heads
 #pragma unroll 1
-    for (int kb = warp * 2 + slot; kb < DR_SUB; kb += 16) {
-      float acc[DR_G];
+  for (int h = 0; h < DR_G; ++h) {
+    float M = -INFINITY;
 #pragma unroll
-      for (int g = 0; g < DR_G; ++g) acc[g] = 0.f;
-      if (kb < nk) {
-        const uint4 u = *reinterpret_cast<const uint4*>(sK[st] + kb * DR_D + part * 8);
-        const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&u);
+    for (int w = 0; w < DR_WARPS; ++w) M = fmaxf(M, wm[w * 8 + h]);
+    float acc = 0.f, lsum = 0.f;
+    if (M != -INFINITY) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __bfloat1622float2(e[j]);
-#pragma unroll
-          for (int g = 0; g < DR_G; ++g) {
-            acc[g] = fmaf(qr[g][2 * j], f.x, acc[g]);
-            acc[g] = fmaf(qr[g][2 * j + 1], f.y, acc[g]);
-          }
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < DR_G; ++g) {
-        float x = acc[g];
-        x += __shfl_xor_sync(0xffffffffu, x, 1);
-        x += __shfl_xor_sync(0xffffffffu, x, 2);
-        x += __shfl_xor_sync(0xffffffffu, x, 4);
-        x += __shfl_xor_sync(0xffffffffu, x, 8);
-        if (part == 0) sS[g][kb] = (kb < nk && ok) ? x * p.scale_log2 : -INFINITY;
+      for (int w = 0; w < DR_WARPS; ++w) {
+        const float mw = wm[w * 8 + h];
+        if (mw == -INFINITY) continue;
+        const float wt = ex2_approx(mw - M);
+        acc += wt * wo[(w * 8 + h) * DR_OSTRIDE + tid];
+        lsum += wt * wl[w * 8 + h];
       }
     }
-    __syncthreads();
-    // online softmax, warp g owns head g
-    if (warp < DR_G) {
-      const int g = warp;
-      const float a0 = sS[g][lane], a1 = sS[g][lane + 32];
-      const float mc = warp_max(fmaxf(a0, a1));
-      const float mn = fmaxf(m_run, mc);
-      const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mn);
-      const float e0 = (mn == -INFINITY) ? 0.f : exp2f(a0 - mn);
-      const float e1 = (mn == -INFINITY) ? 0.f : exp2f(a1 - mn);
-      sS[g][lane] = e0;
-      sS[g][lane + 32] = e1;
-      l_run = l_run * alpha + warp_sum(e0 + e1);
-      m_run = mn;
-      if (lane == 0) sAlpha[g] = alpha;
+    po[h][tid] = acc;
+    if (tid == 0) {
+      pm[h] = M;
+      pl[h] = lsum;
     }
-    __syncthreads();
-    // O = O * alpha + P V
-    {
-      const bool h1 = hg + 4 < DR_G;
-      const float a0 = sAlpha[hg], a1 = h1 ? sAlpha[hg + 4] : 0.f;
-      o[0][0] *= a0;
-      o[0][1] *= a0;
-      o[1][0] *= a1;
-      o[1][1] *= a1;
-      const __nv_bfloat162* vcol = reinterpret_cast<const __nv_bfloat162*>(sV[st]) + dp;
-      const float* p0 = sS[hg];
-      const float* p1 = sS[h1 ? hg + 4 : hg];
-#pragma unroll 4
-      for (int j = 0; j < nk; ++j) {
-        const float2 vv = __bfloat1622float2(vcol[j * (DR_D / 2)]);
-        const float w0 = p0[j], w1 = p1[j];
-        o[0][0] = fmaf(w0, vv.x, o[0][0]);
-        o[0][1] = fmaf(w0, vv.y, o[0][1]);
-        o[1][0] = fmaf(w1, vv.x, o[1][0]);
-        o[1][1] = fmaf(w1, vv.y, o[1][1]);
-      }
-    }
-    __syncthreads();  // stage st and sS free
-    if (tid == 0 && i + 2 < nsub) issue(i + 2);
-  }
-
-  // publish this CTA's partial to the cluster
-  po[hg][2 * dp] = o[0][0];
-  po[hg][2 * dp + 1] = o[0][1];
-  if (hg + 4 < DR_G) {
-    po[hg + 4][2 * dp] = o[1][0];
-    po[hg + 4][2 * dp + 1] = o[1][1];
-  }
-  if (warp < DR_G && lane == 0) {
-    pm[warp] = (l_run > 0.f) ? m_run : -INFINITY;
-    pl[warp] = l_run;
   }
   cluster.sync();
-  // Combine: output element idx = rank * DR_THREADS + tid (ranks 0..3 cover the
-  // 7 x 128 outputs); the 8 ranks' partials are read over DSMEM, loads unrolled.
-  {
-    const int idx = rank * DR_THREADS + tid;
-    if (idx < DR_G * DR_D) {
-      const int g = idx / DR_D, d = idx % DR_D;
-      float mr[DR_CLUSTER], lr[DR_CLUSTER], orr[DR_CLUSTER];
+  // Combine the cluster: rank r finishes outputs [112 r, 112 r + 112) of the
+  // group's 7 x 128, reading every rank's partial over DSMEM.
+  if (tid < DR_OUT_PER_RANK) {
+    const int idx = rank * DR_OUT_PER_RANK + tid;
+    const int g = idx / DR_D, d = idx % DR_D;
+    float mr[DR_CLUSTER], lr[DR_CLUSTER], orr[DR_CLUSTER];
 #pragma unroll
-      for (int r = 0; r < DR_CLUSTER; ++r) {
-        mr[r] = *cluster.map_shared_rank(&pm[g], r);
-        lr[r] = *cluster.map_shared_rank(&pl[g], r);
-        orr[r] = *cluster.map_shared_rank(&po[g][d], r);
-      }
-      float m = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < DR_CLUSTER; ++r) m = fmaxf(m, mr[r]);
-      float l = 0.f, acc = 0.f;
-#pragma unroll
-      for (int r = 0; r < DR_CLUSTER; ++r) {
-        if (mr[r] == -INFINITY) continue;
-        const float w = exp2f(mr[r] - m);
-        l += w * lr[r];
-        acc += w * orr[r];
-      }
-      p.out[(static_cast<size_t>(b) * p.Hq + kvh * DR_G + g) * DR_D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
-      if (d == 0 && p.lse != nullptr)
-        p.lse[static_cast<size_t>(b) * p.Hq + kvh * DR_G + g] =
-            l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
+    for (int r = 0; r < DR_CLUSTER; ++r) {
+      mr[r] = *cluster.map_shared_rank(&pm[g], r);
+      lr[r] = *cluster.map_shared_rank(&pl[g], r);
+      orr[r] = *cluster.map_shared_rank(&po[g][d], r);
     }
+    float m = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < DR_CLUSTER; ++r) m = fmaxf(m, mr[r]);
+    float l = 0.f, acc = 0.f;
+#pragma unroll
+    for (int r = 0; r < DR_CLUSTER; ++r) {
+      if (mr[r] == -INFINITY) continue;
+      const float w = ex2_approx(mr[r] - m);
+      l += w * lr[r];
+      acc += w * orr[r];
+    }
+    p.out[(static_cast<size_t>(b) * p.Hq + kvh * DR_G + g) * DR_D + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+    if (d == 0 && p.lse != nullptr)
+      p.lse[static_cast<size_t>(b) * p.Hq + kvh * DR_G + g] =
+          l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
   }
   cluster.sync();  // keep every CTA's smem alive until the others have read it
 }
@@ -259,6 +313,9 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   if (D != stdb::DR_D || Hq != Hkv * stdb::DR_G || B <= 0 || cap <= 0) return 1;
   if (q == nullptr || k_cache == nullptr || v_cache == nullptr || lens == nullptr || out == nullptr) return 1;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) return 1;
+  if ((reinterpret_cast<uintptr_t>(q) & 3) != 0) return 1;
+  const long long rows = static_cast<long long>(B) * Hkv * cap;
+  if (rows + stdb::DR_SUB >= (1ll << 31)) return 1;  // tensor-map row coordinates are 32-bit
   static bool attr_set = false;
   if (!attr_set) {
     if (cudaFuncSetAttribute(stdb::draft_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, stdb::DR_SMEM) !=
@@ -268,10 +325,12 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
       return 3;
     attr_set = true;
   }
+  CUtensorMap tk, tv;
+  int rc = make_tmap_bf16_2d(&tk, k_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_BOX);
+  if (rc == 0) rc = make_tmap_bf16_2d(&tv, v_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_BOX);
+  if (rc != 0) return rc;
   stdb::DraftParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
-  p.k = static_cast<const __nv_bfloat16*>(k_cache);
-  p.v = static_cast<const __nv_bfloat16*>(v_cache);
   p.lens = lens;
   p.len_offset = len_offset;
   p.cap = cap;
@@ -281,6 +340,6 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
   dim3 grid(stdb::DR_CLUSTER, Hkv, B);
-  stdb::draft_attn_kernel<<<grid, stdb::DR_THREADS, stdb::DR_SMEM, static_cast<cudaStream_t>(stream)>>>(p);
+  stdb::draft_attn_kernel<<<grid, stdb::DR_THREADS, stdb::DR_SMEM, static_cast<cudaStream_t>(stream)>>>(tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

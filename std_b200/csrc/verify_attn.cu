@@ -394,39 +394,6 @@ __global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p)
 // ---------------------------------------------------------------------------
 // host: tensor maps and C ABI
 // ---------------------------------------------------------------------------
-typedef CUresult (*PFN_tmapEncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                        const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                                        CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                        CUtensorMapFloatOOBfill);
-
-static PFN_tmapEncodeTiled tmap_encoder() {
-  static PFN_tmapEncodeTiled fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_tmapEncodeTiled>(ptr);
-  }
-  return fn;
-}
-
-// 2-D bf16 tensor [rows, cols] (row pitch in bytes), box = box_cols x box_rows,
-// 128-byte swizzle.  box_cols*2 must be 128.
-static int make_tmap_bf16_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t row_pitch_bytes,
-                             uint32_t box_cols, uint32_t box_rows) {
-  PFN_tmapEncodeTiled enc = tmap_encoder();
-  if (enc == nullptr) return 3;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {row_pitch_bytes};
-  cuuint32_t box[2] = {box_cols, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : 4;
-}
-
 // Keys per split, fixed by the cache shape alone (so two calls on the same
 // cache -- an AR step and a verify block -- use the same split boundaries).
 // The split count per (request, head) is chosen so the CTAs fill whole waves of

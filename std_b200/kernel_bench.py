@@ -6,7 +6,9 @@
 
 Each repetition cycles through `--caches` distinct K/V caches (default: as
 many as keep the total above 256 MB, i.e. larger than the 126 MB L2), so the
-number measures HBM, not L2.  Prints achieved algorithmic GB/s:
+number measures HBM, not L2.  The launches are captured into a CUDA graph and
+timed over one replay (`--eager` times plain Python-level calls instead, which
+adds the host cost of each call).  Prints achieved algorithmic GB/s:
   verify: B * (2048*L + 143360) bytes per launch  (K/V rows + q/out)
   draft:  B * (2048*L + 14336)  bytes per launch
   gemm:   2*N*K (weights) + 2*M*K + 2*M*N bytes per launch
@@ -21,6 +23,7 @@ import json
 import torch
 
 from . import ops
+from .timing import graph_time_us
 
 
 def main() -> None:
@@ -36,6 +39,7 @@ def main() -> None:
     ap.add_argument("--caches", type=int, default=0)
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--eager", action="store_true", help="time eager calls (includes host launch cost)")
     a = ap.parse_args()
 
     dev = torch.device("cuda", 0)
@@ -65,20 +69,29 @@ def main() -> None:
             ops.draft_attention(q, ks[i], vs[i], lens, 0)
 
         nbytes = B * (2048 * L + 14336)
-    for i in range(a.warmup):
-        run(i % n_caches)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(a.reps):
-        run(i % n_caches)
-    e1.record()
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1000.0 / a.reps
+    us = _time(a, run, n_caches)
     assert ops.device_error() == 0
     print(json.dumps({"kernel": a.kernel, "B": B, "L": L, "nq": a.nq if a.kernel == "verify" else 1,
                       "caches": n_caches, "launch_us": us, "algorithmic_bytes": nbytes,
                       "achieved_gbs": nbytes / us / 1e3}))
+
+
+def _time(a, run, n_bufs: int) -> float:
+    """Microseconds per launch, cycling through `n_bufs` buffer sets."""
+    if not a.eager:
+        rounds = max(1, (a.reps + n_bufs - 1) // n_bufs)
+        return graph_time_us([lambda i=i: run(i) for i in range(n_bufs)], rounds=rounds)
+    for i in range(max(a.warmup, 2)):
+        run(i % n_bufs)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(a.reps, n_bufs)
+    e0.record()
+    for i in range(reps):
+        run(i % n_bufs)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / reps
 
 
 def gemm_bench(a, dev) -> None:
@@ -96,17 +109,7 @@ def gemm_bench(a, dev) -> None:
         else:
             ops.gemm(x, ws[i], y)
 
-    for i in range(max(a.warmup, 2)):
-        run(i % n_w)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = max(a.reps, n_w)
-    e0.record()
-    for i in range(reps):
-        run(i % n_w)
-    e1.record()
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1000.0 / reps
+    us = _time(a, run, n_w)
     nbytes = 2 * N * K + 2 * M * K + 2 * M * N
     print(json.dumps({"kernel": "cublas" if a.cublas else "gemm", "M": M, "N": N, "K": K, "weights": n_w,
                       "launch_us": us, "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / us / 1e3}))
