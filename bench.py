@@ -35,6 +35,13 @@ import time
 METRIC = "STD generated tokens/sec per GPU & per box (1/2/4/8 B200); draft-attn HBM GB/s"
 VIDEO_TOKEN_ID = 151656
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one verify
+# launch at the configs[4] shape (B=8, L=32906, nq=10), from one
+# `ncu --set full -k regex:verify_attn_kernel -c 1` capture of
+# `python -m std_b200.kernel_bench --kernel verify --B 8 --L 32906`.  Used only
+# when the bench runs exactly that shape.
+VERIFY_TRAFFIC = {(8, 32906, 10): 550.2e6}
+
 WORKLOADS = {
     "config4": dict(batch=8, visual=32768, text=128, k_plus_text=1024, gamma=9, max_new=128,
                     desc="configs[4]: 8 requests/GPU x (32768 visual (64x512) + 128 text), K+text=1024, gamma=9, "
@@ -336,7 +343,8 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
                    "l2": "inputs larger than L2 (15.2 GB weights + KV caches read per step)"},
         "e2e": e2e,
         "roofline": {"bound": "hbm", "kernel": "verify_attn_kernel (tcgen05)", "achieved": achieved,
-                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": None,
+                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "traffic": VERIFY_TRAFFIC.get((B, L, nq)), "traffic_unit": "bytes per launch",
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, burst)",
                      "algorithmic_bytes_per_launch": verify_bytes, "launch_us": t_verify * 1e6,
                      "tensor_tflops": verify_flops / t_verify / 1e12,
