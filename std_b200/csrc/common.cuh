@@ -65,6 +65,20 @@ STD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of the same condition (for loops that poll several
+// barriers and must not be parked on one of them).
+STD_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Gives up after about
 // one second (or 2^26 polls), records STD_DEVERR_WAIT_TIMEOUT and returns false.
 STD_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {

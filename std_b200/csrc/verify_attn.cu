@@ -105,15 +105,25 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
       mbar_init(&bar_kv_full[i], 1);
       mbar_init(&bar_kv_empty[i], 1);
     }
+    // only the warps that hold query rows take part in the softmax handshakes
+    const uint32_t live_threads = 32u * static_cast<uint32_t>(min(4, (nrows + 31) / 32));
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_s_full[i], 1);
-      mbar_init(&bar_s_free[i], 128);
-      mbar_init(&bar_p_full[i], 128);
+      mbar_init(&bar_s_free[i], live_threads);
+      mbar_init(&bar_p_full[i], live_threads);
     }
     mbar_init(&bar_mma_done, 1);
     fence_barrier_init();
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
+  }
+  if (warp < 4 && warp * 32 >= nrows) {
+    // P rows of the all-padding warps are never written by the softmax:
+    // zero them once so every P V tile reads defined values
+    for (int buf = 0; buf < 2; ++buf)
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<uint4*>(sP + buf * VF_PTILE + sw128_offset(tid, c8)) = make_uint4(0u, 0u, 0u, 0u);
+    fence_async_smem();
   }
   tc_fence_before();
   __syncthreads();
@@ -214,8 +224,10 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
     bool ok = true;
     uint32_t s[VF_CHUNK];
     uint8_t* P = sP + wg * VF_PTILE;
+    // a warp whose 32 rows are all padding (rows >= 7*nq) skips the softmax
+    const bool live = (warp & 3) * 32 < nrows;
 
-    for (int c = wg; c < nchunks; c += 2) {
+    for (int c = wg; live && c < nchunks; c += 2) {
       const int kk = c >> 1;
       if (ok) ok = mbar_wait(&bar_s_full[wg], kk & 1);  // also: O[wg] and P[wg] no longer in use
       __syncwarp();
