@@ -29,7 +29,7 @@ from . import ops
 from .model import Qwen25VLDecoder, Workspace, decode_forward, prefill_request
 
 SPARSE_ATTN_MODES = ("b200",)
-VERIFY_MODES = ("parallel",)
+VERIFY_MODES = ("parallel", "sequential")
 
 
 @dataclass
@@ -157,10 +157,13 @@ class STDRunner:
 
     def __init__(self, model: Qwen25VLDecoder, batch_size: int, layout: PromptLayout, max_new_tokens: int,
                  gamma: int = 9, k: int = 896, eos_token_id: int = -1, ignore_eos: bool = False,
-                 use_graphs: bool = True):
+                 use_graphs: bool = True, verify_mode: str = "parallel"):
         c = model.config
         if gamma < 1 or 7 * (gamma + 1) > 126:
             raise ValueError("gamma must be in [1, 17]")
+        if verify_mode not in VERIFY_MODES:
+            raise ValueError(f"verify_mode must be one of {VERIFY_MODES}")
+        self.verify_mode = verify_mode
         self.model, self.B, self.layout = model, batch_size, layout
         self.gamma, self.k, self.max_new = gamma, k, max_new_tokens
         self.eos, self.ignore_eos, self.use_graphs = eos_token_id, ignore_eos, use_graphs
@@ -260,6 +263,23 @@ class STDRunner:
                        slot_off=0, lens=self.dense_len, len_offset=nq, sparse=False, argmax_out=self.vpred.view(-1),
                        argmax_stride=self.gamma + 1, argmax_start=0)
 
+    def _verify_sequential(self, pending: int) -> None:
+        """verify_mode="sequential" (std_qwen25vl.py:504-528, :775-781, :885-893):
+        the pending bonus and every draft token go through the dense model one
+        token at a time (q_len = 1, the AR step's kernels and padded row
+        count), each prediction landing in the same slot as the parallel
+        block's.  The reference stops at the first mismatch; here the tokens
+        after it are still run (no host round trip per token), but they cannot
+        change the accepted prefix or the bonus -- both are functions of the
+        predictions up to the first mismatch -- and their cache rows lie past
+        the rolled-back dense length, so they are overwritten next round."""
+        nq = self.gamma + pending
+        for j in range(nq):
+            decode_forward(self.model, self.ws, self.dense, B=self.B, n=1, rows=self.dense_rows, tok=self.tok,
+                           tok_start=1 - pending + j, pos_base=self.dense_len, pos_off=j, slot_base=self.dense_len,
+                           slot_off=j, lens=self.dense_len, len_offset=j + 1, sparse=False,
+                           argmax_out=self.vpred.view(-1), argmax_stride=self.gamma + 1, argmax_start=j)
+
     def _accept(self, pending: int) -> None:
         from . import _lib
 
@@ -280,7 +300,10 @@ class STDRunner:
         pending = 0 if first else 1
         for i in range(self.gamma):
             self._draft_step(i)
-        self._verify(pending)
+        if self.verify_mode == "sequential":
+            self._verify_sequential(pending)
+        else:
+            self._verify(pending)
         self._accept(pending)
         self._bonus_step()
         torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
@@ -458,12 +481,12 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                           runner: Optional[STDRunner] = None) -> Tuple[GenerateResult, SparseSelection]:
     """Sparse-to-Dense greedy decoding (std_qwen25vl.py:609-978).
 
-    Implemented: verify_mode="parallel", verify_fallback="none",
+    Implemented: verify_mode="parallel" | "sequential", verify_fallback="none",
     sparse_attn_mode="b200", copy_sparse_prefill=True, fixed gamma.  Other
     values of the reference's research flags raise ValueError (there is no
     alternative backend to dispatch to)."""
     if verify_mode not in VERIFY_MODES:
-        raise ValueError(f"Unsupported verify_mode={verify_mode!r}; this build implements 'parallel'.")
+        raise ValueError(f"Unsupported verify_mode={verify_mode!r}; expected one of {VERIFY_MODES}.")
     if verify_fallback != "none":
         raise ValueError("verify_fallback other than 'none' is not part of the B200 path.")
     if sparse_attn_mode not in SPARSE_ATTN_MODES:
@@ -479,7 +502,9 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                          explicit_k)
     if runner is None:
         runner = STDRunner(model, ids.shape[0], layout, max_new_tokens, gamma=gamma, k=k, eos_token_id=eos_token_id,
-                           ignore_eos=ignore_eos)
+                           ignore_eos=ignore_eos, verify_mode=verify_mode)
+    elif runner.verify_mode != verify_mode:
+        raise ValueError("the runner was built for a different verify_mode")
     tp = runner.prefill(embeds, with_selection=True)
     dec = runner.run_std()
     torch.cuda.synchronize()

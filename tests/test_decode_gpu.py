@@ -73,7 +73,48 @@ def test_public_api_and_selection():
         assert torch.all(tk[:, 1:] > tk[:, :-1]) and int(tk.max()) < 500
     assert std.generate_len == 24 and std.decode_rounds >= 1
     with pytest.raises(ValueError):
-        std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, verify_mode="sequential")
+        std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, verify_mode="tree")
+    seq, _ = std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, max_new_tokens=24, gamma=9,
+                                   target_k_plus_text=88, ignore_eos=True, verify_mode="sequential")
+    assert tokens_equal(seq.output_ids, ar.output_ids)
+    assert seq.accept_lengths == std.accept_lengths
+
+
+@pytest.mark.parametrize("B,gamma,eos,full", [(2, 5, False, True), (3, 9, True, False)])
+def test_sequential_verify_matches_parallel(B, gamma, eos, full):
+    """verify_mode="sequential" (one dense token at a time) accepts exactly what
+    the parallel verify block accepts, round by round, and both equal AR."""
+    from std_b200 import ops
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import STDRunner, _prepare, selection_budget
+
+    model = Qwen25VLDecoder(TINY, seed=4)
+    V, T = 500, 32
+    inp = _inputs(B, V, T, TINY.vocab_size, TINY.hidden_size, seed=20 + B)
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    # full=True keeps every visual token, so most drafts are accepted and the
+    # comparison covers long accepted prefixes, not only rejections
+    k = V if full else selection_budget(layout.prompt_len, layout.text_start, V, 100, None)
+    eos_id = int(ids[0, -1]) if eos else -1
+    res = {}
+    for mode in ("parallel", "sequential"):
+        runner = STDRunner(model, B, layout, 36, gamma=gamma, k=k, eos_token_id=eos_id, ignore_eos=not eos,
+                           verify_mode=mode)
+        runner.prefill(embeds, with_selection=True)
+        runner.run_std()
+        res[mode] = (runner.out_tokens.cpu().clone(), runner.n_gen.cpu().clone(), runner.std_stats())
+        if mode == "sequential":
+            runner.run_ar()
+            ar = (runner.out_tokens.cpu().clone(), runner.n_gen.cpu().clone())
+    assert ops.device_error() == 0
+    (tp, np_, sp), (ts, ns, ss) = res["parallel"], res["sequential"]
+    assert torch.equal(np_, ns) and torch.equal(ns, ar[1])
+    for b in range(B):
+        n = int(ns[b])
+        assert tp[b, :n].tolist() == ts[b, :n].tolist() == ar[0][b, :n].tolist()
+    assert sp["accept_lengths"] == ss["accept_lengths"]
+    if full:
+        assert sum(ss["accepted"]) > 0
 
 
 def test_full_selection_accepts_nearly_everything():
