@@ -147,7 +147,8 @@ def _mm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[torc
 def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *, B: int, n: int, rows: int,
                    tok: torch.Tensor, tok_start: int, pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor,
                    slot_off: int, lens: torch.Tensor, len_offset: int, sparse: bool,
-                   argmax_out: Optional[torch.Tensor], argmax_stride: int = 1, argmax_start: int = 0) -> None:
+                   argmax_out: Optional[torch.Tensor], argmax_stride: int = 1, argmax_start: int = 0,
+                   dense_attn=None) -> None:
     """One forward of n new tokens per request through all layers (graph-capturable).
 
     cache: [layers, 2, B, Hkv, cap, D].  sparse=True uses the draft kernel
@@ -155,13 +156,17 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     tokens).  GEMMs run on `rows` >= B*n rows (the fixed padded count for dense
     forwards).  The argmax of each new token's logits goes to
     argmax_out[b*argmax_stride + argmax_start + j]; argmax_out=None skips the
-    lm_head (a draft step whose prediction is never used).
+    lm_head (a draft step whose prediction is never used).  dense_attn (a
+    seq_shard.ShardExchange on the owner rank) replaces the local verify
+    kernel by the sequence-sharded attention over every rank's key range.
     """
     c = model.config
     M = B * n
     Hq, Hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
     cos_t, sin_t = model.cos_t, model.sin_t
     x, h = ws.x[:rows], ws.h[:rows]
+    if dense_attn is not None and not sparse:
+        dense_attn.begin(n)
     ops.embed(model.embed, tok, tok_start, n, ws.x[:M])
     ops.rmsnorm(x, model.layers[0].w_in, c.rms_norm_eps, h)
     n_layers = len(model.layers)
@@ -172,6 +177,8 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
                         ws.q[:M], kc, vc)
         if sparse:
             ops.draft_attention(ws.q[:M], kc, vc, lens, len_offset, out=ws.attn[:M].view(B, Hq, D))
+        elif dense_attn is not None:
+            dense_attn.attend(li, ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset, ws.attn[:M].view(B, n, Hq, D))
         else:
             ops.verify_attention(ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset,
                                  out=ws.attn[:M].view(B, n, Hq, D))

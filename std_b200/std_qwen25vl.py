@@ -157,7 +157,7 @@ class STDRunner:
 
     def __init__(self, model: Qwen25VLDecoder, batch_size: int, layout: PromptLayout, max_new_tokens: int,
                  gamma: int = 9, k: int = 896, eos_token_id: int = -1, ignore_eos: bool = False,
-                 use_graphs: bool = True, verify_mode: str = "parallel"):
+                 use_graphs: bool = True, verify_mode: str = "parallel", shard=None):
         c = model.config
         if gamma < 1 or 7 * (gamma + 1) > 126:
             raise ValueError("gamma must be in [1, 17]")
@@ -169,10 +169,19 @@ class STDRunner:
         self.eos, self.ignore_eos, self.use_graphs = eos_token_id, ignore_eos, use_graphs
         P = layout.prompt_len
         self.compact_len = int(layout.non_visual.numel()) + k
-        self.cap_d = _round_up(P + max_new_tokens + gamma + 2, 128)
+        self.cap_d = self.dense_capacity(P, max_new_tokens, gamma)
         self.cap_s = _round_up(self.compact_len + max_new_tokens + gamma + 2, 64)
         dev = model.device
-        self.dense = initialize_past_key_values(model, batch_size, self.cap_d)
+        # With a seq_shard.ShardExchange this rank is the owner of a sequence-
+        # sharded dense cache: it stores keys [dense_shift, cap_d) locally and
+        # every dense forward attends over all ranks' ranges.
+        self.shard = shard
+        self.dense_shift = 0
+        if shard is not None:
+            if shard.plan.cap != self.cap_d or not shard.is_owner:
+                raise ValueError("the shard plan must be built for this runner's dense capacity, on the owner rank")
+            self.dense_shift = shard.plan.key_range(shard.plan.owner)[0]
+        self.dense = initialize_past_key_values(model, batch_size, self.cap_d - self.dense_shift)
         self.sparse = initialize_past_key_values(model, batch_size, self.cap_s)
         model.rope_tables(self.cap_d + 2)
         self.dense_rows = _round_up(batch_size * (gamma + 1), 16)
@@ -201,6 +210,10 @@ class STDRunner:
         self._graphs: Dict[str, torch.cuda.CUDAGraph] = {}
         self.prefill_done = False
 
+    @staticmethod
+    def dense_capacity(prompt_len: int, max_new_tokens: int, gamma: int) -> int:
+        return _round_up(prompt_len + max_new_tokens + gamma + 2, 128)
+
     # ------------------------------------------------------------------ prefill
     def prefill(self, embeds: Sequence[torch.Tensor], with_selection: bool = True) -> Dict[str, float]:
         """Prefill every request (embeds[b]: [P, H] bf16) and, for STD, select and compact."""
@@ -210,10 +223,12 @@ class STDRunner:
         scores = torch.empty(L, Hkv, P, dtype=torch.float32, device=self.model.device) if with_selection else None
         self.topk_per_request = []
         dn = []
+        # a sharded owner prefills into a whole-length cache, then hands out the ranges
+        full = self.dense if self.shard is None else initialize_past_key_values(self.model, self.B, self.cap_d)
         for b in range(self.B):
             torch.cuda.synchronize()
             t0 = time.time()
-            dn.append(prefill_request(self.model, self.dense, b, embeds[b], self.layout.text_start, scores))
+            dn.append(prefill_request(self.model, full, b, embeds[b], self.layout.text_start, scores))
             torch.cuda.synchronize()
             t1 = time.time()
             t["prefill_time"] += t1 - t0
@@ -221,11 +236,18 @@ class STDRunner:
                 topk = build_sparse_selection(scores, self.layout, self.k)
                 torch.cuda.synchronize()
                 t2 = time.time()
-                compact_sparse_prompt_cache(self.dense, self.sparse, b, self.layout, topk)
+                compact_sparse_prompt_cache(full, self.sparse, b, self.layout, topk)
                 torch.cuda.synchronize()
                 t["selection_time"] += t2 - t1
                 t["sparse_cache_time"] += time.time() - t2
                 self.topk_per_request.append(topk.clone())
+        if self.shard is not None:
+            torch.cuda.synchronize()
+            t0 = time.time()
+            self.shard.distribute(full, self.dense, P)
+            del full
+            torch.cuda.synchronize()
+            t["shard_distribute_time"] = time.time() - t0
         self.dense_next.copy_(torch.tensor(dn, dtype=torch.int32))
         self.prefill_done = True
         return t
@@ -258,10 +280,12 @@ class STDRunner:
 
     def _verify(self, pending: int) -> None:
         nq = self.gamma + pending
+        sh = self.dense_shift
         decode_forward(self.model, self.ws, self.dense, B=self.B, n=nq, rows=self.dense_rows, tok=self.tok,
                        tok_start=1 - pending, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len,
-                       slot_off=0, lens=self.dense_len, len_offset=nq, sparse=False, argmax_out=self.vpred.view(-1),
-                       argmax_stride=self.gamma + 1, argmax_start=0)
+                       slot_off=-sh, lens=self.dense_len, len_offset=nq - sh, sparse=False,
+                       argmax_out=self.vpred.view(-1), argmax_stride=self.gamma + 1, argmax_start=0,
+                       dense_attn=self.shard)
 
     def _verify_sequential(self, pending: int) -> None:
         """verify_mode="sequential" (std_qwen25vl.py:504-528, :775-781, :885-893):
@@ -274,11 +298,13 @@ class STDRunner:
         predictions up to the first mismatch -- and their cache rows lie past
         the rolled-back dense length, so they are overwritten next round."""
         nq = self.gamma + pending
+        sh = self.dense_shift
         for j in range(nq):
             decode_forward(self.model, self.ws, self.dense, B=self.B, n=1, rows=self.dense_rows, tok=self.tok,
                            tok_start=1 - pending + j, pos_base=self.dense_len, pos_off=j, slot_base=self.dense_len,
-                           slot_off=j, lens=self.dense_len, len_offset=j + 1, sparse=False,
-                           argmax_out=self.vpred.view(-1), argmax_stride=self.gamma + 1, argmax_start=j)
+                           slot_off=j - sh, lens=self.dense_len, len_offset=j + 1 - sh, sparse=False,
+                           argmax_out=self.vpred.view(-1), argmax_stride=self.gamma + 1, argmax_start=j,
+                           dense_attn=self.shard)
 
     def _accept(self, pending: int) -> None:
         from . import _lib
@@ -296,17 +322,26 @@ class STDRunner:
                        lens=self.sparse_len, len_offset=0, sparse=True, argmax_out=self.tok.view(-1),
                        argmax_stride=self.tok_stride, argmax_start=1)
 
-    def std_round(self, first: bool) -> None:
-        pending = 0 if first else 1
+    def _drafts(self) -> None:
         for i in range(self.gamma):
             self._draft_step(i)
+
+    def _verify_phase(self, pending: int) -> None:
         if self.verify_mode == "sequential":
             self._verify_sequential(pending)
         else:
             self._verify(pending)
+
+    def _post(self, pending: int) -> None:
         self._accept(pending)
         self._bonus_step()
         torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
+
+    def std_round(self, first: bool) -> None:
+        pending = 0 if first else 1
+        self._drafts()
+        self._verify_phase(pending)
+        self._post(pending)
 
     def ar_step(self) -> None:
         from . import _lib
@@ -315,9 +350,11 @@ class STDRunner:
         _lib.call("std_ar_commit", self.B, self.tok_stride, self.max_new, self.eos, 1 if self.ignore_eos else 0,
                   self.tok.data_ptr(), self.n_gen.data_ptr(), self.done.data_ptr(), self.out_tokens.data_ptr(),
                   self.active.data_ptr(), s)
+        sh = self.dense_shift
         decode_forward(self.model, self.ws, self.dense, B=self.B, n=1, rows=self.dense_rows, tok=self.tok,
-                       tok_start=0, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len, slot_off=0,
-                       lens=self.dense_len, len_offset=1, sparse=False, argmax_out=self.next_tok)
+                       tok_start=0, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len, slot_off=-sh,
+                       lens=self.dense_len, len_offset=1 - sh, sparse=False, argmax_out=self.next_tok,
+                       dense_attn=self.shard)
         _lib.call("std_ar_advance", self.B, self.active.data_ptr(), self.next_tok.data_ptr(), self.tok.data_ptr(),
                   self.tok_stride, self.dense_len.data_ptr(), self.ctx_len.data_ptr(), s)
         torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
@@ -330,8 +367,13 @@ class STDRunner:
         kernel attributes outside capture); state is reset afterwards."""
         if not self.use_graphs:
             return
-        steps = (("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False)),
-                 ("ar", self.ar_step))
+        if self.shard is None:
+            steps = (("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False)),
+                     ("ar", self.ar_step))
+        else:
+            # collectives stay outside the graphs: the dense forwards (verify,
+            # AR steps) run eagerly between captured local phases
+            steps = (("drafts", self._drafts), ("post_first", lambda: self._post(0)), ("post", lambda: self._post(1)))
         for name, fn in steps:
             if name in self._graphs:
                 continue
@@ -363,12 +405,12 @@ class STDRunner:
         self.reset()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        self._replay_or_run("std_first", lambda: self.std_round(True))
+        self._round(True)
         rounds = 1
         while not self._all_done():
             if rounds > self.max_new + 1:
                 raise RuntimeError("STD decode did not terminate")
-            self._replay_or_run("std", lambda: self.std_round(False))
+            self._round(False)
             rounds += 1
         end.record()
         end.synchronize()
@@ -391,6 +433,15 @@ class STDRunner:
         end.record()
         end.synchronize()
         return start.elapsed_time(end) / 1000.0
+
+    def _round(self, first: bool) -> None:
+        if self.shard is None:
+            self._replay_or_run("std_first" if first else "std", lambda: self.std_round(first))
+            return
+        pending = 0 if first else 1
+        self._replay_or_run("drafts", self._drafts)
+        self._verify_phase(pending)
+        self._replay_or_run("post_first" if first else "post", lambda: self._post(pending))
 
     def _replay_or_run(self, name: str, fn) -> None:
         g = self._graphs.get(name)
