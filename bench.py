@@ -369,6 +369,99 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- sequence-sharded arm
+def b200_sharded_arm(a, w, rank: int, world: int, local_rank: int) -> None:
+    """configs[3] on N > 1 GPUs: one long request whose dense cache is split by
+    sequence position; rank N-1 owns the model, the cache tail and the draft
+    steps, every other rank serves its key range each dense forward
+    (std_b200/seq_shard.py).  Total work is fixed, so scaling is strong."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from std_b200 import ops
+    from std_b200.model import QWEN25_VL_7B, Qwen25VLDecoder
+    from std_b200.seq_shard import ShardExchange, ShardPlan
+    from std_b200.std_qwen25vl import PromptLayout, STDRunner
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=dev)
+    c = QWEN25_VL_7B
+    B, P, V, T, g_ = w["batch"], w["prompt"], w["visual"], w["text"], w["gamma"]
+    cap = STDRunner.dense_capacity(P, w["max_new"], g_)
+    plan = ShardPlan.make(P, cap, world)
+    ex = ShardExchange(plan, rank, B, c.num_attention_heads, c.head_dim, g_ + 1, dev)
+    t_local, tokens_local, extra = 0.0, 0.0, {}
+    if not ex.is_owner:
+        local = torch.zeros(c.num_hidden_layers, 2, B, c.num_key_value_heads, plan.local_cap(rank), c.head_dim,
+                            dtype=torch.bfloat16, device=dev)
+        ex.distribute(None, local, P)
+        ex.serve(local, c.num_hidden_layers)
+    else:
+        model = Qwen25VLDecoder(c, seed=2, device=str(dev))
+        ids = torch.full((B, P), VIDEO_TOKEN_ID, dtype=torch.int64)
+        embeds = []
+        for b in range(B):
+            gc = torch.Generator().manual_seed(100 + b)
+            ids[b, V:] = torch.randint(0, 151643, (T,), generator=gc)
+            e = model.embed[ids[b].to(dev)]
+            gd = torch.Generator(device=dev).manual_seed(100 + b)
+            e[:V] = torch.randn(V, c.hidden_size, generator=gd, device=dev).to(torch.bfloat16)
+            embeds.append(e)
+        layout = PromptLayout.from_ids(ids[0], VIDEO_TOKEN_ID, dev)
+        runner = STDRunner(model, B, layout, w["max_new"], gamma=g_, k=w["k"], eos_token_id=-1, ignore_eos=True,
+                           shard=ex)
+        t0 = time.time()
+        runner.prefill(embeds, with_selection=True)
+        torch.cuda.synchronize()
+        extra["prefill_s"] = time.time() - t0
+        del embeds
+        runner.capture()
+        for _ in range(a.warmup):
+            runner.run_std()
+        sampler = ClockSampler(str(local_rank))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            runner.run_std()
+        e1.record()
+        torch.cuda.synchronize()
+        extra["clocks"] = sampler.stop()
+        t_local = e0.elapsed_time(e1) / 1000.0
+        tokens_local = float(a.steps * int(runner.n_gen.sum().item()))
+        std_tokens = runner.out_tokens.clone()
+        st = runner.std_stats()
+        extra["acceptance_rate"] = sum(st["accepted"]) / max(1, sum(st["proposed"]))
+        extra["rounds_per_step"] = int(runner.stats[:, 0].max().item())
+        if not a.no_ar:
+            t_ar = runner.run_ar()
+            extra["ar_tokens_per_s"] = float(runner.n_gen.sum().item()) / t_ar
+            extra["token_exact_vs_ar"] = bool(torch.equal(std_tokens, runner.out_tokens))
+        extra["device_error"] = ops.device_error()
+        ex.close()
+    t = torch.tensor([t_local, tokens_local], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank == plan.owner:
+        t_max, tokens = float(t[0]), float(t[1])
+        line = {
+            "metric": METRIC, "value": tokens / t_max, "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": 1000.0 * t_max / a.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init Qwen2.5-VL-7B-shaped decoder (std 0.02, seed 2), request seed 100",
+            "config": {"workload": w["desc"].replace("unsharded", f"dense cache sequence-sharded over {world} GPUs"),
+                       "requests": B, "prompt_len": P, "k": w["k"], "gamma": g_, "max_new_tokens": w["max_new"],
+                       "parallelism": f"seq{world}: rank {plan.owner} owns model + cache tail, ranks 0..{world - 2} "
+                                      f"serve {plan.shard} keys each",
+                       "l2": "inputs larger than L2 (15.2 GB weights read per forward)"},
+            "roofline": None, "cpu_baseline": None, "e2e": None,
+            "gpu_launches": None, **extra,
+        }
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     a = _args()
     w = _workload(a)
@@ -380,6 +473,9 @@ def main():
         sys.exit(2)
     if a.impl == "reference":
         reference_arm(a, w, rank, world)
+        return
+    if a.workload == "config3" and world > 1:
+        b200_sharded_arm(a, w, rank, world, local_rank)
         return
     b200_arm(a, w, rank, world, local_rank)
 
