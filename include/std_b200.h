@@ -136,7 +136,7 @@ int std_compact_gather(const void* dense_cache, void* sparse_cache, int layers, 
 /* modeling_qwen2_5_vl.py:1336 (embed_tokens): out[b*n+j] = table[tok[b*tok_stride+tok_start+j]]. */
 int std_embed(const void* table, int vocab, int H, const int32_t* tok, int tok_stride, int tok_start, int n, int B,
               void* out, void* stream);
-/* modeling_qwen2_5_vl.py:183-197 (Qwen2RMSNorm). */
+/* modeling_qwen2_5_vl.py:183-197 (Qwen2RMSNorm).  H % 8 == 0, H/8 <= 512. */
 int std_rmsnorm(const void* x, const void* w, float eps, int M, int H, void* out, void* stream);
 /* modeling_qwen2_5_vl.py:1200-1221 + :183-197 (residual add, then the next
  * RMSNorm): x <- bf16(x + delta) in place, out = rmsnorm(x) * w. */
@@ -166,6 +166,27 @@ int std_argmax_rows(const void* logits, int rows, int V, int n, int out_stride, 
 size_t std_gemm_workspace_bytes(int M, int N, int K);
 int std_gemm_bf16(const void* x, const void* w, const void* bias, void* y, int M, int N, int K, void* workspace,
                   size_t workspace_bytes, void* stream);
+
+/* GEMMs fused with the decode op that consumes them: the GEMM's bf16 result
+ * goes through `workspace` (>= std_gemm_epilogue_workspace_bytes) straight
+ * into the epilogue kernel, with the same arithmetic as the unfused pair.
+ * N % 8 == 0. */
+size_t std_gemm_epilogue_workspace_bytes(int M, int N, int K);
+/* Replaces: the o_proj / down_proj output, the residual add and the next
+ * RMSNorm of a decoder layer (modeling_qwen2_5_vl.py:1200-1221, Qwen2RMSNorm
+ * :183-197):  resid <- bf16(resid + bf16(x . w^T + bias));
+ * out = rmsnorm(resid) * norm_w.  norm_w == NULL: the residual add only.
+ * Same result as std_gemm_bf16 followed by std_add_rmsnorm.  N/8 <= 512. */
+int std_gemm_add_rmsnorm(const void* x, const void* w, const void* bias, void* resid, const void* norm_w, float eps,
+                         void* out, int M, int N, int K, void* workspace, size_t workspace_bytes, void* stream);
+/* Replaces: q/k/v_proj of a decode step (modeling_qwen2_5_vl.py:1050-1052),
+ * RoPE (:690-732) and KVCache.cat (kv_cache.py:54-69): qkv = x . w^T + bias
+ * (w [(Hq+2Hkv)*D, K]) then, per token row, the std_rope_append step on it.
+ * Same result as std_gemm_bf16 followed by std_rope_append. */
+int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, int B, int n, int Hq, int Hkv, int D,
+                         const int32_t* pos_base, int pos_off, const int32_t* slot_base, int slot_off,
+                         const void* cos_t, const void* sin_t, int max_pos, void* q_out, void* k_cache,
+                         void* v_cache, int cap, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- (d) fused greedy acceptance + rollback ---------------------------- */
 

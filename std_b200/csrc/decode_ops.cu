@@ -26,6 +26,8 @@ namespace stdb {
 // out[b*n + j] = table[tok[b*tok_stride + tok_start + j]]
 __global__ void embed_kernel(const __nv_bfloat16* table, int vocab, int H, const int32_t* tok, int tok_stride,
                              int tok_start, int n, __nv_bfloat16* out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int b = row / n, j = row % n;
   int id = tok[b * tok_stride + tok_start + j];
@@ -40,7 +42,7 @@ __global__ void embed_kernel(const __nv_bfloat16* table, int vocab, int H, const
 
 // ------------------------------- RMSNorm -----------------------------------
 // One block per row, one thread per 8 consecutive elements (H % 8 == 0,
-// H/8 <= 1024): every input is loaded once into registers before any store.
+// H/8 <= 512): every input is loaded once into registers before any store.
 // Sum of squares: per-thread sequential over its 8 values, xor tree inside
 // each warp, then warps in order -- the same order for every row count.
 STD_DEV float block_sum_ordered(float s, float* s_part) {
@@ -74,13 +76,30 @@ STD_DEV void store8(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// y = bf16( w * bf16( x * rsqrt(mean(x^2) + eps) ) );  with delta != null,
+// Row sources: 8 consecutive columns of one row as floats.  Bf16Rows reads a
+// bf16 matrix; NoRows is the absent operand.  gemm.cu adds GemmOut (a GEMM's
+// bf16 result assembled from its split-K partials), so a GEMM epilogue can be
+// fused into the kernels below with the same arithmetic as the unfused pair.
+struct NoRows {
+  static constexpr bool kActive = false;
+  STD_DEV void load8(size_t, int, float*) const {}
+};
+struct Bf16Rows {
+  static constexpr bool kActive = true;
+  const __nv_bfloat16* p;
+  int ld;
+  STD_DEV void load8(size_t row, int col, float* v) const { ::stdb::load8(p + row * ld + col, v); }
+};
+
+// y = bf16( w * bf16( x * rsqrt(mean(x^2) + eps) ) );  with an active delta,
 // first x <- bf16(x + delta) (the residual add), written back in place.
-__global__ void __launch_bounds__(1024) rmsnorm_kernel(__nv_bfloat16* __restrict__ x,
-                                                       const __nv_bfloat16* __restrict__ delta,
+// w == null: only the residual add (no norm, `out` untouched).
+template <class Delta>
+__global__ void __launch_bounds__(512) rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const Delta delta,
                                                        const __nv_bfloat16* __restrict__ w, float eps, int H,
                                                        __nv_bfloat16* __restrict__ out) {
   __shared__ float s_part[32];
+  pdl_wait();
   pdl_launch_dependents();  // the following GEMM may start streaming its weights
   const size_t row = blockIdx.x;
   const int c = threadIdx.x * 8;
@@ -88,15 +107,16 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(__nv_bfloat16* __restrict
   float v[8], wv[8];
   if (act) {
     load8(x + row * H + c, v);
-    load8(w + c, wv);
-    if (delta != nullptr) {
+    if (w != nullptr) load8(w + c, wv);
+    if (Delta::kActive) {
       float dv[8];
-      load8(delta + row * H + c, dv);
+      delta.load8(row, c, dv);
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = bf16_round(__fadd_rn(v[j], dv[j]));
       store8(x + row * H + c, v);
     }
   }
+  if (w == nullptr) return;  // uniform across the block
   float s = 0.f;
   if (act) {
 #pragma unroll
@@ -119,7 +139,6 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(__nv_bfloat16* __restrict
 // One block per token row; a thread owns 8 dims of the first half of one head
 // and the matching 8 of the second half (rotate_half pairs d and d + D/2).
 struct RopeParams {
-  const __nv_bfloat16* qkv;
   int n, Hq, Hkv, D, cap, max_pos;
   const int32_t* pos_base;
   int pos_off;
@@ -132,7 +151,10 @@ struct RopeParams {
   __nv_bfloat16* v_cache;
 };
 
-__global__ void __launch_bounds__(512) rope_append_kernel(const RopeParams p) {
+template <class Src>  // qkv rows [B*n, (Hq + 2 Hkv) * D]
+__global__ void __launch_bounds__(512) rope_append_kernel(const Src qkv, const RopeParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int b = row / p.n, j = row % p.n;
   const int heads = p.Hq + 2 * p.Hkv;
@@ -148,10 +170,9 @@ __global__ void __launch_bounds__(512) rope_append_kernel(const RopeParams p) {
   }
   if (!slot_ok && threadIdx.x == 0) std_set_error(STD_DEVERR_LENGTH);
   if (h >= heads) return;
-  const __nv_bfloat16* src = p.qkv + (static_cast<size_t>(row) * heads + h) * p.D;
   float lo[8], hi[8];
-  load8(src + c, lo);
-  load8(src + half + c, hi);
+  qkv.load8(row, h * p.D + c, lo);
+  qkv.load8(row, h * p.D + half + c, hi);
   __nv_bfloat16* dst;
   if (h < p.Hq) {
     dst = p.q_out + (static_cast<size_t>(row) * p.Hq + h) * p.D;
@@ -183,6 +204,7 @@ __global__ void __launch_bounds__(512) rope_append_kernel(const RopeParams p) {
 // gu rows: [gate (I) | up (I)]; out = bf16( bf16(silu(gate)) * up ), 8 per thread
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, size_t total8,
                                 __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
   pdl_launch_dependents();
   const int I8 = I / 8;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total8;
@@ -201,6 +223,8 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, siz
 }
 
 __global__ void add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, size_t n, __nv_bfloat16* out) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     out[i] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(a[i]), __bfloat162float(b[i])));
@@ -211,6 +235,8 @@ __global__ void add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, size_
 // out[(row / n) * out_stride + out_start + row % n].
 __global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logits, int V, int n, int out_stride,
                                                       int out_start, int32_t* out) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const __nv_bfloat16* lr = logits + static_cast<size_t>(row) * V;
   float best = -INFINITY;
@@ -277,6 +303,8 @@ struct AcceptParams {
 };
 
 __global__ void accept_commit_kernel(const AcceptParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= p.B || p.done[b]) return;
   const int32_t* draft = p.tok + static_cast<size_t>(b) * p.tok_stride + 1;
@@ -331,6 +359,8 @@ __global__ void accept_commit_kernel(const AcceptParams p) {
 // frozen, so a batch can keep stepping until its last request finishes.
 __global__ void ar_commit_kernel(int B, int tok_stride, int max_new, int eos, int ignore_eos, const int32_t* tok,
                                  int32_t* n_gen, int32_t* done, int32_t* out_tokens, int32_t* active) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   if (done[b]) {
@@ -347,6 +377,8 @@ __global__ void ar_commit_kernel(int B, int tok_stride, int max_new, int eos, in
 
 __global__ void ar_advance_kernel(int B, const int32_t* active, const int32_t* next_tok, int32_t* tok, int tok_stride,
                                   int32_t* dense_len, int32_t* ctx_len) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B || !active[b]) return;
   dense_len[b] += 1;
@@ -362,31 +394,35 @@ __global__ void ar_advance_kernel(int B, const int32_t* active, const int32_t* n
 extern "C" int std_embed(const void* table, int vocab, int H, const int32_t* tok, int tok_stride, int tok_start, int n,
                          int B, void* out, void* stream) {
   if (H % 8 != 0 || n <= 0 || B <= 0) return 1;
-  stdb::embed_kernel<<<B * n, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(table), vocab, H, tok, tok_stride, tok_start, n,
-      static_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::embed_kernel, dim3(B * n), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<const __nv_bfloat16*>(table), vocab, H, tok, tok_stride, tok_start, n,
+                    static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_rmsnorm(const void* x, const void* w, float eps, int M, int H, void* out, void* stream) {
   if (M <= 0 || H <= 0) return 1;
-  if (H % 8 != 0 || H / 8 > 1024) return 1;
+  if (H % 8 != 0 || H / 8 > 512) return 1;
   const int nt = ((H / 8 + 31) / 32) * 32;
-  stdb::rmsnorm_kernel<<<M, nt, 0, static_cast<cudaStream_t>(stream)>>>(
-      const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)), nullptr,
-      static_cast<const __nv_bfloat16*>(w), eps, H, static_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  if (w == nullptr) return 1;
+  return launch_pdl(stdb::rmsnorm_kernel<stdb::NoRows>, dim3(M), dim3(nt), 0, static_cast<cudaStream_t>(stream),
+                    const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)), stdb::NoRows{},
+                    static_cast<const __nv_bfloat16*>(w), eps, H, static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_add_rmsnorm(void* x, const void* delta, const void* w, float eps, int M, int H, void* out,
                                void* stream) {
   if (M <= 0 || H <= 0) return 1;
-  if (H % 8 != 0 || H / 8 > 1024 || delta == nullptr) return 1;
+  if (H % 8 != 0 || H / 8 > 512 || delta == nullptr || w == nullptr) return 1;
   const int nt = ((H / 8 + 31) / 32) * 32;
-  stdb::rmsnorm_kernel<<<M, nt, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(delta), static_cast<const __nv_bfloat16*>(w),
-      eps, H, static_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::rmsnorm_kernel<stdb::Bf16Rows>, dim3(M), dim3(nt), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<__nv_bfloat16*>(x), stdb::Bf16Rows{static_cast<const __nv_bfloat16*>(delta), H},
+                    static_cast<const __nv_bfloat16*>(w), eps, H, static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, int D, const int32_t* pos_base,
@@ -395,7 +431,6 @@ extern "C" int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, i
                                void* stream) {
   if (B <= 0 || n <= 0 || D % 16 != 0 || cap <= 0 || (Hq + 2 * Hkv) * (D / 16) > 512) return 1;
   stdb::RopeParams p;
-  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
   p.n = n;
   p.Hq = Hq;
   p.Hkv = Hkv;
@@ -412,32 +447,39 @@ extern "C" int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, i
   p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
   p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
   const int nt = (((Hq + 2 * Hkv) * (D / 16) + 31) / 32) * 32;
-  stdb::rope_append_kernel<<<B * n, nt, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  const stdb::Bf16Rows src{static_cast<const __nv_bfloat16*>(qkv), (Hq + 2 * Hkv) * D};
+  return launch_pdl(stdb::rope_append_kernel<stdb::Bf16Rows>, dim3(B * n), dim3(nt), 0,
+                    static_cast<cudaStream_t>(stream), src, p) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_silu_mul(const void* gu, int M, int I, void* out, void* stream) {
   if (M <= 0 || I <= 0 || I % 8 != 0) return 1;
   const size_t total8 = static_cast<size_t>(M) * I / 8;
   const int blocks = static_cast<int>((total8 + 255) / 256 < 148 * 8 ? (total8 + 255) / 256 : 148 * 8);
-  stdb::silu_mul_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gu), I, total8, static_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::silu_mul_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<const __nv_bfloat16*>(gu), I, total8, static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_add(const void* a, const void* b, size_t n, void* out, void* stream) {
   const int blocks = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
-  stdb::add_kernel<<<blocks > 0 ? blocks : 1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), n, static_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::add_kernel, dim3(blocks > 0 ? blocks : 1), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b), n,
+                    static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_argmax_rows(const void* logits, int rows, int V, int n, int out_stride, int out_start, int32_t* out,
                                void* stream) {
   if (rows <= 0 || V <= 0 || n <= 0) return 1;
-  stdb::argmax_kernel<<<rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __nv_bfloat16*>(logits),
-                                                                            V, n, out_stride, out_start, out);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::argmax_kernel, dim3(rows), dim3(1024), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<const __nv_bfloat16*>(logits), V, n, out_stride, out_start, out) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_accept_commit(int B, int gamma, int pending, int32_t* tok, int tok_stride, const int32_t* vpred,
@@ -467,23 +509,26 @@ extern "C" int std_accept_commit(int B, int gamma, int pending, int32_t* tok, in
   p.out_tokens = out_tokens;
   p.stats = stats;
   p.accept_hist = accept_hist;
-  stdb::accept_commit_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::accept_commit_kernel, dim3((B + 127) / 128), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), p) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_ar_commit(int B, int tok_stride, int max_new, int eos, int ignore_eos, const int32_t* tok,
                              int32_t* n_gen, int32_t* done, int32_t* out_tokens, int32_t* active, void* stream) {
   if (B <= 0 || tok_stride <= 0 || max_new <= 0) return 1;
-  stdb::ar_commit_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      B, tok_stride, max_new, eos, ignore_eos, tok, n_gen, done, out_tokens, active);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::ar_commit_kernel, dim3((B + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                    B, tok_stride, max_new, eos, ignore_eos, tok, n_gen, done, out_tokens, active) == cudaSuccess
+             ? 0
+             : 4;
 }
 
 extern "C" int std_ar_advance(int B, const int32_t* active, const int32_t* next_tok, int32_t* tok, int tok_stride,
                               int32_t* dense_len, int32_t* ctx_len, void* stream) {
   if (B <= 0 || tok_stride <= 0) return 1;
-  stdb::ar_advance_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(B, active, next_tok, tok,
-                                                                                          tok_stride, dense_len,
-                                                                                          ctx_len);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::ar_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                    B, active, next_tok, tok, tok_stride, dense_len, ctx_len) == cudaSuccess
+             ? 0
+             : 4;
 }

@@ -75,6 +75,8 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
+  pdl_wait();
+  pdl_launch_dependents();
 
   extern __shared__ uint8_t dsmem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
@@ -340,6 +342,8 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
   dim3 grid(stdb::DR_CLUSTER, Hkv, B);
-  stdb::draft_attn_kernel<<<grid, stdb::DR_THREADS, stdb::DR_SMEM, static_cast<cudaStream_t>(stream)>>>(tk, tv, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  return launch_pdl(stdb::draft_attn_kernel, grid, dim3(stdb::DR_THREADS), stdb::DR_SMEM,
+                    static_cast<cudaStream_t>(stream), tk, tv, p) == cudaSuccess
+             ? 0
+             : 4;
 }

@@ -183,6 +183,48 @@ __global__ void gemm_reduce_kernel(const float* __restrict__ partial, int splits
   }
 }
 
+// The GEMM's bf16 result read 8 columns at a time by a fused epilogue (the
+// rmsnorm and rope_append kernels of decode_ops.cu): split partials summed in
+// split order, + bias, rounded to bf16 -- the same operations, in the same
+// order, as gemm_reduce_kernel -- or, when K was not split, the GEMM's own
+// bf16 output (bias already applied).
+struct GemmOut {
+  static constexpr bool kActive = true;
+  const float* partial;        // [splits, M, N]  (splits > 1)
+  const __nv_bfloat16* y;      // [M, N]          (splits == 1)
+  const __nv_bfloat16* bias;   // [N] or null     (splits > 1)
+  int splits, M, N;
+  STD_DEV void load8(size_t row, int col, float* v) const {
+    if (splits <= 1) {
+      ::stdb::load8(y + row * N + col, v);
+      return;
+    }
+    const size_t off = row * N + col;
+    float4 a = __ldcg(reinterpret_cast<const float4*>(partial + off));
+    float4 b = __ldcg(reinterpret_cast<const float4*>(partial + off + 4));
+    for (int s = 1; s < splits; ++s) {
+      const float* ps = partial + static_cast<size_t>(s) * M * N + off;
+      const float4 c = __ldcg(reinterpret_cast<const float4*>(ps));
+      const float4 d = __ldcg(reinterpret_cast<const float4*>(ps + 4));
+      a.x += c.x;
+      a.y += c.y;
+      a.z += c.z;
+      a.w += c.w;
+      b.x += d.x;
+      b.y += d.y;
+      b.z += d.z;
+      b.w += d.w;
+    }
+    float t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    if (bias != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] += __bfloat162float(bias[col + j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = bf16_round(t[j]);
+  }
+};
+
 }  // namespace stdb
 
 // ---------------------------------------------------------------------------
@@ -215,14 +257,10 @@ extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
   return s > 1 ? static_cast<size_t>(s) * M * N * 4 : 0;
 }
 
-extern "C" int std_gemm_bf16(const void* x, const void* w, const void* bias, void* y, int M, int N, int K,
-                             void* workspace, size_t workspace_bytes, void* stream) {
-  if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % stdb::GM_BK != 0 || N % 4 != 0) return 1;
-  if (x == nullptr || w == nullptr || y == nullptr) return 1;
-  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) != 0) return 1;
-  const int splits = gemm_splits(N, K);
-  const size_t need = std_gemm_workspace_bytes(M, N, K);
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return 5;
+// Launch gemm_kernel: with splits > 1 it writes fp32 partials to `partial`,
+// otherwise bf16 y (+ bias).  Shapes are checked by the callers.
+static int gemm_launch(const void* x, const void* w, const void* bias, void* y, float* partial, int M, int N, int K,
+                       int splits, cudaStream_t s) {
   const int nmma = gemm_nmma(M);
   const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
   int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
@@ -252,33 +290,110 @@ extern "C" int std_gemm_bf16(const void* x, const void* w, const void* bias, voi
   p.stages = stages;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.y = static_cast<__nv_bfloat16*>(y);
-  p.partial = static_cast<float*>(workspace);
+  p.partial = partial;
+  // may begin while the previous kernel in the stream finishes: the weight
+  // tiles of the first stages are requested before griddepcontrol.wait
+  return launch_pdl(stdb::gemm_kernel, dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits), dim3(stdb::GM_THREADS),
+                    smem, s, tw, tx, p) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+static bool gemm_shape_ok(const void* x, const void* w, int M, int N, int K, int n_align) {
+  if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % stdb::GM_BK != 0 || N % n_align != 0) return false;
+  if (x == nullptr || w == nullptr) return false;
+  return ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+}
+
+extern "C" int std_gemm_bf16(const void* x, const void* w, const void* bias, void* y, int M, int N, int K,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (!gemm_shape_ok(x, w, M, N, K, 4) || y == nullptr) return 1;
+  const int splits = gemm_splits(N, K);
+  const size_t need = std_gemm_workspace_bytes(M, N, K);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return 5;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // both launches may begin while the previous kernel in the stream finishes
-  // (programmatic dependent launch); the kernels wait before touching its data
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits);
-  cfg.blockDim = dim3(stdb::GM_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, stdb::gemm_kernel, tw, tx, p) != cudaSuccess) return 4;
-  if (splits > 1) {
-    const size_t total4 = static_cast<size_t>(M) * N / 4;
-    const int blocks = static_cast<int>((total4 + 255) / 256 < 1184 ? (total4 + 255) / 256 : 1184);
-    cudaLaunchConfig_t rc2 = {};
-    rc2.gridDim = dim3(blocks);
-    rc2.blockDim = dim3(256);
-    rc2.stream = s;
-    rc2.attrs = attr;
-    rc2.numAttrs = 1;
-    if (cudaLaunchKernelEx(&rc2, stdb::gemm_reduce_kernel, static_cast<const float*>(p.partial), splits, M, N,
-                           p.bias, p.y) != cudaSuccess)
-      return 4;
-  }
-  return cudaGetLastError() == cudaSuccess ? 0 : 4;
+  int rc = gemm_launch(x, w, bias, y, static_cast<float*>(workspace), M, N, K, splits, s);
+  if (rc != 0 || splits == 1) return rc;
+  const size_t total4 = static_cast<size_t>(M) * N / 4;
+  const int blocks = static_cast<int>((total4 + 255) / 256 < 1184 ? (total4 + 255) / 256 : 1184);
+  return launch_pdl(stdb::gemm_reduce_kernel, dim3(blocks), dim3(256), 0, s,
+                    static_cast<const float*>(workspace), splits, M, N, static_cast<const __nv_bfloat16*>(bias),
+                    static_cast<__nv_bfloat16*>(y)) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+// Fused GEMM epilogues: the GEMM's output goes straight into the next decode
+// op, through workspace (split partials, or the bf16 output when K is not split).
+extern "C" size_t std_gemm_epilogue_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const size_t part = std_gemm_workspace_bytes(M, N, K);
+  const size_t ybytes = static_cast<size_t>(M) * N * 2;
+  const size_t b = part > ybytes ? part : ybytes;
+  return ((b + 255) / 256) * 256;
+}
+
+static stdb::GemmOut gemm_out_view(void* workspace, const void* bias, int splits, int M, int N) {
+  stdb::GemmOut o;
+  o.partial = splits > 1 ? static_cast<const float*>(workspace) : nullptr;
+  o.y = splits > 1 ? nullptr : static_cast<const __nv_bfloat16*>(workspace);
+  o.bias = splits > 1 ? static_cast<const __nv_bfloat16*>(bias) : nullptr;
+  o.splits = splits;
+  o.M = M;
+  o.N = N;
+  return o;
+}
+
+extern "C" int std_gemm_add_rmsnorm(const void* x, const void* w, const void* bias, void* resid, const void* norm_w,
+                                    float eps, void* out, int M, int N, int K, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  if (!gemm_shape_ok(x, w, M, N, K, 8) || resid == nullptr || N / 8 > 512) return 1;
+  if (norm_w != nullptr && out == nullptr) return 1;
+  if (workspace == nullptr || workspace_bytes < std_gemm_epilogue_workspace_bytes(M, N, K)) return 5;
+  const int splits = gemm_splits(N, K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(x, w, bias, workspace, static_cast<float*>(workspace), M, N, K, splits, s);
+  if (rc != 0) return rc;
+  const int nt = ((N / 8 + 31) / 32) * 32;
+  return launch_pdl(stdb::rmsnorm_kernel<stdb::GemmOut>, dim3(M), dim3(nt), 0, s, static_cast<__nv_bfloat16*>(resid),
+                    gemm_out_view(workspace, bias, splits, M, N), static_cast<const __nv_bfloat16*>(norm_w), eps, N,
+                    static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+extern "C" int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, int B, int n, int Hq,
+                                    int Hkv, int D, const int32_t* pos_base, int pos_off, const int32_t* slot_base,
+                                    int slot_off, const void* cos_t, const void* sin_t, int max_pos, void* q_out,
+                                    void* k_cache, void* v_cache, int cap, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  const int M = B * n, N = (Hq + 2 * Hkv) * D;
+  if (B <= 0 || n <= 0 || D % 16 != 0 || cap <= 0 || (Hq + 2 * Hkv) * (D / 16) > 512) return 1;
+  if (!gemm_shape_ok(x, w, M, N, K, 8)) return 1;
+  if (workspace == nullptr || workspace_bytes < std_gemm_epilogue_workspace_bytes(M, N, K)) return 5;
+  const int splits = gemm_splits(N, K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = gemm_launch(x, w, bias, workspace, static_cast<float*>(workspace), M, N, K, splits, s);
+  if (rc != 0) return rc;
+  stdb::RopeParams p;
+  p.n = n;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.D = D;
+  p.cap = cap;
+  p.max_pos = max_pos;
+  p.pos_base = pos_base;
+  p.pos_off = pos_off;
+  p.slot_base = slot_base;
+  p.slot_off = slot_off;
+  p.cos_t = static_cast<const __nv_bfloat16*>(cos_t);
+  p.sin_t = static_cast<const __nv_bfloat16*>(sin_t);
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  const int nt = (((Hq + 2 * Hkv) * (D / 16) + 31) / 32) * 32;
+  return launch_pdl(stdb::rope_append_kernel<stdb::GemmOut>, dim3(M), dim3(nt), 0, s,
+                    gemm_out_view(workspace, bias, splits, M, N), p) == cudaSuccess
+             ? 0
+             : 4;
 }

@@ -73,11 +73,15 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
                        const VerifyParams p) {
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();
   const int Lraw = p.lens[b] + p.len_offset;
   if ((Lraw > p.cap || Lraw < p.nq) && split == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
   const int L = verify_len(p, b);
   const int n_splits = (L + p.split_keys - 1) / p.split_keys;
-  if (split >= n_splits || split >= p.max_splits) return;
+  if (split >= n_splits || split >= p.max_splits) {
+    pdl_launch_dependents();
+    return;
+  }
   const int k0 = split * p.split_keys;
   const int k1 = min(k0 + p.split_keys, L);
   const int nchunks = (k1 - k0 + VF_CHUNK - 1) / VF_CHUNK;
@@ -128,6 +132,10 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Dependents may launch only once this CTA holds its TMEM: a successor that
+  // allocates TMEM before its own griddepcontrol.wait can then never take
+  // columns this CTA still needs.
+  pdl_launch_dependents();
   const uint32_t tmem = s_tmem;  // S[w]: cols 64w .. 64w+63; O[w]: cols 128 + 128w
   const int row0 = (b * p.Hkv + kvh) * p.cap;
 
@@ -362,6 +370,8 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
 // One thread per (row, 4 dims); requests whose keys fit one split are skipped
 // (the split kernel wrote them).
 __global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int L = verify_len(p, b);
   const int n_splits = (L + p.split_keys - 1) / p.split_keys;
@@ -486,10 +496,11 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
   p.ws_o = reinterpret_cast<float*>(ws + off);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(p.max_splits, Hkv, B);
-  stdb::verify_attn_kernel<<<grid, stdb::VF_THREADS, stdb::VF_SMEM, s>>>(tk, tv, p);
+  if (launch_pdl(stdb::verify_attn_kernel, grid, dim3(stdb::VF_THREADS), stdb::VF_SMEM, s, tk, tv, p) != cudaSuccess)
+    return 4;
   if (p.max_splits > 1) {
     dim3 mgrid((stdb::VF_G * nq * (stdb::VF_D / 4) + 127) / 128, Hkv, B);
-    stdb::verify_merge_kernel<<<mgrid, 128, 0, s>>>(p);
+    if (launch_pdl(stdb::verify_merge_kernel, mgrid, dim3(128), 0, s, p) != cudaSuccess) return 4;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

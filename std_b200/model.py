@@ -172,9 +172,13 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     n_layers = len(model.layers)
     for li, lw in enumerate(model.layers):
         kc, vc = cache[li, 0], cache[li, 1]
-        _mm(h, lw.w_qkv, ws.qkv[:rows], lw.b_qkv)
-        ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
-                        ws.q[:M], kc, vc)
+        if rows == M:
+            ops.gemm_rope_append(h, lw.w_qkv, lw.b_qkv, B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off,
+                                 cos_t, sin_t, ws.q[:M], kc, vc)
+        else:  # padded rows: the GEMM runs on `rows`, RoPE on the M real ones
+            _mm(h, lw.w_qkv, ws.qkv[:rows], lw.b_qkv)
+            ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
+                            ws.q[:M], kc, vc)
         if sparse:
             ops.draft_attention(ws.q[:M], kc, vc, lens, len_offset, out=ws.attn[:M].view(B, Hq, D))
         elif dense_attn is not None:
@@ -182,17 +186,14 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
         else:
             ops.verify_attention(ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset,
                                  out=ws.attn[:M].view(B, n, Hq, D))
-        _mm(ws.attn[:rows], lw.w_o, ws.o[:rows])
-        ops.add_rmsnorm(x, ws.o[:rows], lw.w_post, c.rms_norm_eps, h)
+        ops.gemm_add_rmsnorm(ws.attn[:rows], lw.w_o, x, lw.w_post, c.rms_norm_eps, h)
         _mm(h, lw.w_gu, ws.gu[:rows])
         ops.silu_mul(ws.gu[:rows], ws.act[:rows])
-        _mm(ws.act[:rows], lw.w_down, ws.o[:rows])
         if li + 1 < n_layers:
-            ops.add_rmsnorm(x, ws.o[:rows], model.layers[li + 1].w_in, c.rms_norm_eps, h)
-        elif argmax_out is not None:
-            ops.add_rmsnorm(x, ws.o[:rows], model.norm, c.rms_norm_eps, h)
-        else:
-            ops.add(x, ws.o[:rows], x)
+            next_norm = model.layers[li + 1].w_in
+        else:  # the final norm feeds lm_head; a draft step without lm_head only adds
+            next_norm = model.norm if argmax_out is not None else None
+        ops.gemm_add_rmsnorm(ws.act[:rows], lw.w_down, x, next_norm, c.rms_norm_eps, h)
     if argmax_out is None:
         return
     _mm(h, model.lm_head, ws.logits[:rows])

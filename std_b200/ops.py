@@ -190,6 +190,42 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[tor
     return out
 
 
+def gemm_add_rmsnorm(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor, norm_w: Optional[torch.Tensor],
+                     eps: float, out: Optional[torch.Tensor], bias: Optional[torch.Tensor] = None):
+    """resid <- bf16(resid + x @ w^T (+ bias)); out = rmsnorm(resid) * norm_w (norm_w None: add only).
+
+    One GEMM plus one fused epilogue kernel; equal to gemm() then add_rmsnorm()."""
+    M, K = x.shape
+    N = w.shape[0]
+    for t, n in ((x, "x"), (w, "w"), (resid, "resid")):
+        _check(t, torch.bfloat16, n)
+    nb = _lib.query("std_gemm_epilogue_workspace_bytes", M, N, K)
+    ws = workspace("gemm", nb, x.device)
+    _lib.call("std_gemm_add_rmsnorm", x.data_ptr(), w.data_ptr(), _p(bias), resid.data_ptr(), _p(norm_w), float(eps),
+              _p(out), M, N, K, ws.data_ptr(), ws.numel(), _stream())
+    return out
+
+
+def gemm_rope_append(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], B: int, n: int, Hq: int,
+                     Hkv: int, D: int, pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor, slot_off: int,
+                     cos_t: torch.Tensor, sin_t: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor,
+                     v_cache: torch.Tensor):
+    """qkv = x @ w^T + bias, then rope_append on it, as one GEMM + one fused epilogue kernel."""
+    M, K = x.shape
+    N = w.shape[0]
+    if M != B * n or N != (Hq + 2 * Hkv) * D:
+        raise ValueError("gemm_rope_append: x rows must be B*n and w rows (Hq + 2 Hkv) * D")
+    _check(x, torch.bfloat16, "x")
+    _check(w, torch.bfloat16, "w")
+    cap = k_cache.shape[-2]
+    nb = _lib.query("std_gemm_epilogue_workspace_bytes", M, N, K)
+    ws = workspace("gemm", nb, x.device)
+    _lib.call("std_gemm_rope_append", x.data_ptr(), w.data_ptr(), _p(bias), K, B, n, Hq, Hkv, D, pos_base.data_ptr(),
+              int(pos_off), slot_base.data_ptr(), int(slot_off), cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape[0],
+              q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), cap, ws.data_ptr(), ws.numel(), _stream())
+    return q_out
+
+
 def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor):
     """x <- x + delta (bf16, in place); out = rmsnorm(x) * w."""
     H = x.shape[-1]

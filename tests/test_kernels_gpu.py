@@ -373,3 +373,59 @@ def test_gemm_rows_independent_of_other_rows(ops):
     y2 = ops.gemm(x2, w, torch.empty(M, N, dtype=torch.bfloat16, device="cuda"))
     for j in (0, 9, 47, 79):
         assert torch.equal(y1[j], y2[j])
+
+
+@pytest.mark.parametrize("M,N,K,with_norm", [(8, 3584, 3584, True), (80, 3584, 18944, True), (8, 3584, 18944, False),
+                                             (16, 896, 1536, True), (200, 896, 896, True)])
+def test_gemm_add_rmsnorm_equals_unfused(ops, M, N, K, with_norm):
+    """The fused GEMM + residual + RMSNorm epilogue gives exactly the bytes of
+    gemm() followed by add_rmsnorm() (split-K and unsplit shapes)."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    resid = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
+    nw = (1 + 0.1 * torch.randn(N, generator=g, device="cuda")).to(torch.bfloat16)
+    r1, r2 = resid.clone(), resid.clone()
+    h1 = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    h2 = torch.empty_like(h1)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, w, y)
+    if with_norm:
+        ops.add_rmsnorm(r1, y, nw, 1e-6, h1)
+        ops.gemm_add_rmsnorm(x, w, r2, nw, 1e-6, h2)
+        assert torch.equal(h1, h2)
+    else:
+        ops.add(r1, y, r1)
+        ops.gemm_add_rmsnorm(x, w, r2, None, 1e-6, None)
+    assert torch.equal(r1, r2)
+    _no_device_error(ops)
+
+
+@pytest.mark.parametrize("B,n,cfg", [(8, 1, "7b"), (8, 10, "7b"), (3, 4, "tiny")])
+def test_gemm_rope_append_equals_unfused(ops, B, n, cfg):
+    """QKV GEMM fused with the split-K sum, bias, RoPE and the K/V append ==
+    gemm() then rope_append(), byte for byte, including the cache rows."""
+    Hq, Hkv, D, K = (28, 4, 128, 3584) if cfg == "7b" else (7, 1, 128, 896)
+    N = (Hq + 2 * Hkv) * D
+    M = B * n
+    g = torch.Generator(device="cuda").manual_seed(B * 100 + n)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(N, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    cap, max_pos = 256, 4096
+    ang = torch.arange(max_pos, device="cuda").float()[:, None] * (1e6 ** (-torch.arange(0, D, 2, device="cuda")
+                                                                         .float() / D))[None, :]
+    cos_t, sin_t = ang.cos().to(torch.bfloat16).contiguous(), ang.sin().to(torch.bfloat16).contiguous()
+    pos_base = torch.randint(0, 3000, (B,), generator=g, device="cuda").to(torch.int32)
+    slot_base = torch.randint(0, cap - n, (B,), generator=g, device="cuda").to(torch.int32)
+    caches = [torch.zeros(2, B, Hkv, cap, D, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    qs = [torch.empty(M, Hq, D, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    qkv = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, w, qkv, bias)
+    ops.rope_append(qkv, B, n, Hq, Hkv, D, pos_base, 3, slot_base, 0, cos_t, sin_t, qs[0], caches[0][0], caches[0][1])
+    ops.gemm_rope_append(x, w, bias, B, n, Hq, Hkv, D, pos_base, 3, slot_base, 0, cos_t, sin_t, qs[1], caches[1][0],
+                         caches[1][1])
+    assert torch.equal(qs[0], qs[1])
+    assert torch.equal(caches[0], caches[1])
+    assert caches[1].abs().sum().item() > 0
+    _no_device_error(ops)
