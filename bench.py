@@ -268,7 +268,7 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     od = torch.empty_like(qd)
     lens_s = runner.sparse_len
     t_draft = graph_time_us([lambda li=li: ops.draft_attention(qd, runner.sparse[li, 0], runner.sparse[li, 1],
-                                                               lens_s, 1, out=od)
+                                                               lens_s, 1, out=od, after_append=True)
                              for li in range(c.num_hidden_layers)], rounds=4) / 1e6
     Ls = w["compact"] + 1
     draft_bytes = B * (2048 * Ls + 14336)

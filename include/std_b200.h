@@ -54,9 +54,15 @@ int std_device_supported(void);
  * attends to keys 0 .. lens[b]+len_offset-1 (no mask); out [B, Hq, D] bf16;
  * lse [B, Hq] fp32 natural-log (optional, may be NULL).  Hq = 7*Hkv, D = 128. */
 size_t std_draft_attn_workspace_bytes(int B, int Hq, int Hkv, int D, int cap);
+/* flags: 0, or STD_DRAFT_AFTER_APPEND when the launch just before this one on
+ * `stream` writes nothing this call reads except q and, per request, the K/V
+ * row at position lens[b]+len_offset-1 (a decode step's RoPE + KV append).
+ * The kernel then reads the lengths and the older K/V rows while that launch
+ * may still be running (programmatic dependent launch). */
+#define STD_DRAFT_AFTER_APPEND 1
 int std_draft_attn(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens, int len_offset,
                    int B, int Hq, int Hkv, int D, int cap, void* out, float* lse, void* workspace,
-                   size_t workspace_bytes, void* stream);
+                   size_t workspace_bytes, int flags, void* stream);
 
 /* ---- (c) parallel dense verify attention (also AR dense decode, nq = 1) -- */
 

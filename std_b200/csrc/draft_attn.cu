@@ -17,16 +17,17 @@
 //   CTA rank i owns keys [i*per, (i+1)*per) of the request's live length
 //   (per = ceil(L/8) rounded up to 16).  TMA (2-D tensor maps, 128-byte
 //   swizzle, 16-row boxes, no multicast) streams its K and V rows through a
-//   two-stage ring of 64-key sub-tiles; only the boxes that hold live keys are
+//   three-stage ring of 64-key sub-tiles; only the boxes that hold live keys are
 //   fetched.  Each warp takes 16 keys of every sub-tile: S = Q K^T from
 //   ldmatrix'd K fragments, an online softmax on the accumulator registers,
 //   then O += P V with P reused from registers as the A operand and V
 //   fragments from ldmatrix.trans.  Every K/V byte is read from HBM once (the
 //   Triton kernel re-reads each KV head for each of its 7 query heads).
-//   The 4 warp partials are combined in shared memory, then the 8 CTAs of the
-//   cluster combine theirs through distributed shared memory (each rank
-//   finishes 112 of the 7 x 128 outputs), so there is one launch, no global
-//   scratch and no second kernel.  Lengths come from device memory, so the
+//   The 4 warp partials are combined in shared memory; each CTA then pushes
+//   its partial of output slice q into rank q's shared memory (DSMEM stores),
+//   one cluster barrier later every rank finishes its 112 of the 7 x 128
+//   outputs from local data -- one launch, no global scratch, no second
+//   kernel, one cluster barrier.  Lengths come from device memory, so the
 //   launch is graph-capturable while they change between replays.
 #include <cooperative_groups.h>
 
@@ -40,7 +41,7 @@ constexpr int DR_WARPS = 4;
 constexpr int DR_THREADS = DR_WARPS * 32;
 constexpr int DR_SUB = 64;     // keys per pipeline stage, 16 per warp
 constexpr int DR_BOX = 16;     // rows per TMA box
-constexpr int DR_STAGES = 2;
+constexpr int DR_STAGES = 3;
 constexpr int DR_CLUSTER = 8;  // CTAs per (request, KV head)
 constexpr uint32_t DR_HALF_BYTES = DR_SUB * 64 * 2;                // 64 keys x 64 dims (one 128-B swizzle span)
 constexpr uint32_t DR_STAGE_BYTES = 4 * DR_HALF_BYTES;             // K lo, K hi, V lo, V hi
@@ -59,6 +60,7 @@ struct DraftParams {
   float scale_log2;         // (1/sqrt(D)) * log2(e)
   __nv_bfloat16* out;       // [B, Hq, D]
   float* lse;               // [B, Hq] natural-log LSE, may be null
+  int flags;                // STD_DRAFT_AFTER_APPEND: see the C ABI below
 };
 
 // Byte offset of (row, 16-byte chunk) inside a 128-byte-swizzled half tile.
@@ -66,7 +68,7 @@ STD_DEV uint32_t dr_sw(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS, 3)
+__global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS, 2)
     draft_attn_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                       const DraftParams p) {
   namespace cg = cooperative_groups;
@@ -75,15 +77,27 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  pdl_wait();
-  pdl_launch_dependents();
+  // Every CTA of the cluster must be running before another writes into its
+  // shared memory: arrive now, wait just before the first push (by then the
+  // wait returns at once).
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  // After an append (the decode step's RoPE + KV-append kernel, which writes
+  // only q and the K/V row at position L-1): the lengths and every older K/V
+  // row are read while that kernel may still run; q and row L-1 only after
+  // griddepcontrol.wait.  Otherwise nothing is read before the wait.
+  const bool early = (p.flags & 1) != 0;
+  if (!early) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
 
   extern __shared__ uint8_t dsmem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bar[DR_STAGES];
-  // this CTA's partial, published to the cluster
-  __shared__ float pm[DR_G], pl[DR_G];
-  __shared__ __align__(16) float po[DR_G][DR_D];
+  // partials pushed here by every rank r of the cluster for the 112 outputs
+  // this CTA finishes (and, per head it covers, their m and l)
+  __shared__ __align__(16) float r_o[DR_CLUSTER][DR_OUT_PER_RANK];
+  __shared__ float r_m[DR_CLUSTER][DR_G], r_l[DR_CLUSTER][DR_G];
 
   int L = p.lens[b] + p.len_offset;
   if (L > p.cap || L < 0) {
@@ -97,6 +111,12 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   const int nkeys = k1 - k0;
   const int nsub = (nkeys + DR_SUB - 1) / DR_SUB;
   const int row0 = (b * p.Hkv + kvh) * p.cap + k0;  // first tensor-map row of this CTA
+  // early mode: the 16-row box holding row L-1 waits for the append
+  int defer_i = -1, defer_j = -1;
+  if (early && L - 1 >= k0 && L - 1 < k1) {
+    defer_i = (L - 1 - k0) / DR_SUB;
+    defer_j = ((L - 1 - k0) % DR_SUB) / DR_BOX;
+  }
 
   if (tid == 0) {
     prefetch_tensormap(&tk);
@@ -106,24 +126,35 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     fence_barrier_init();
   }
   __syncthreads();
-  auto issue = [&](int i) {
+  // Sub-tile i is issued by the 32 lanes of warp 0 together: lane 4j+part
+  // copies box j (16 rows) of K lo/hi (part 0/1) or V lo/hi (part 2/3).
+  // mode 0: the whole sub-tile; 1: all but the deferred box; 2: only that box
+  auto issue = [&](int i, int mode) {
     const int st = i % DR_STAGES;
     const int a = i * DR_SUB;
     const int nbox = (min(DR_SUB, nkeys - a) + DR_BOX - 1) / DR_BOX;
     uint8_t* s = sbase + st * DR_STAGE_BYTES;
-    mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nbox) * 4u * DR_BOX * 128u);
-    for (int j = 0; j < nbox; ++j) {
-      const int y = row0 + a + j * DR_BOX;
-      const uint32_t off = j * DR_BOX * 128;
-      tma_load_2d(s + off, &tk, &bar[st], 0, y);
-      tma_load_2d(s + DR_HALF_BYTES + off, &tk, &bar[st], 64, y);
-      tma_load_2d(s + 2 * DR_HALF_BYTES + off, &tv, &bar[st], 0, y);
-      tma_load_2d(s + 3 * DR_HALF_BYTES + off, &tv, &bar[st], 64, y);
+    if (mode != 2) {
+      if (lane == 0) mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nbox) * 4u * DR_BOX * 128u);
+      __syncwarp();
+    }
+    const int j = lane >> 2, part = lane & 3;
+    const bool is_deferred = i == defer_i && j == defer_j;
+    if (lane < 4 * nbox && (mode == 0 || (mode == 1) != is_deferred)) {
+      const uint32_t off = j * DR_BOX * 128 + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES;
+      tma_load_2d(s + off, part < 2 ? &tk : &tv, &bar[st], (part & 1) * 64, row0 + a + j * DR_BOX);
     }
   };
-  int issued = 0;  // sub-tiles issued so far (meaningful in thread 0)
-  if (tid == 0) {
-    for (; issued < DR_STAGES && issued < nsub; ++issued) issue(issued);
+  // sub-tiles issued so far: the same value in every thread (warp 0 issues),
+  // so the block-wide barriers below that depend on it are uniform
+  int issued = min(DR_STAGES, nsub);
+  if (warp == 0) {
+    for (int i = 0; i < issued; ++i) issue(i, early ? 1 : 0);
+  }
+  if (early) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (warp == 0 && defer_i >= 0 && defer_i < issued) issue(defer_i, 2);
   }
 
   // Q as the A operand: row gid = query head kvh*7 + gid (row 7 and rows 8..15
@@ -150,6 +181,7 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     const int st = i % DR_STAGES;
     const int nk = min(DR_SUB, nkeys - i * DR_SUB);
     if (ok) ok = mbar_wait(&bar[st], (i / DR_STAGES) & 1);
+    ok = __all_sync(0xffffffffu, ok);  // warp-uniform: guards warp-collective code below
     uint8_t* sK = sbase + st * DR_STAGE_BYTES;
     uint8_t* sV = sK + 2 * DR_HALF_BYTES;
     const int kw = warp * 16;
@@ -166,8 +198,10 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
         fence_async_smem();
         __syncwarp();
       }
-      // S[16 x 16 keys] = Q K^T
+      // S[16 x 16 keys] = Q K^T, even and odd k-steps in separate
+      // accumulators (four independent MMA chains instead of two)
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const int mi = lane >> 3;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -175,8 +209,15 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
         const int ch = (ks & 3) * 2 + (mi & 1);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(smem_u32(sK + (ks >> 2) * DR_HALF_BYTES + dr_sw(key, ch)), b0, b1, b2, b3);
-        mma_bf16_16816(s[0], qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
-        mma_bf16_16816(s[1], qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+        float* d0 = (ks & 1) ? s2[0] : s[0];
+        float* d1 = (ks & 1) ? s2[1] : s[1];
+        mma_bf16_16816(d0, qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
+        mma_bf16_16816(d1, qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        s[0][e] += s2[0][e];
+        s[1][e] += s2[1][e];
       }
       // online softmax on row gid (keys 2tig, 2tig+1, 8+2tig, 9+2tig)
       float x[4];
@@ -211,8 +252,11 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
         mma_bf16_16816(o[2 * jj + 1], pa0, 0u, pa2, 0u, v2, v3);
       }
     }
-    __syncthreads();  // every warp is done with stage st
-    if (tid == 0 && ok && issued < nsub) issue(issued++);
+    if (issued < nsub) {  // uniform: a refill follows
+      __syncthreads();    // every warp is done with stage st
+      if (warp == 0 && __all_sync(0xffffffffu, ok)) issue(issued, 0);
+      ++issued;
+    }
   }
   if (tid == 0) {
     // Normally a no-op (every issued phase has completed).  If a wait gave up,
@@ -238,8 +282,9 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     }
   }
   __syncthreads();
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   // CTA partial: thread tid owns dim tid of all 7 heads
-#pragma unroll 1
+#pragma unroll
   for (int h = 0; h < DR_G; ++h) {
     float M = -INFINITY;
 #pragma unroll
@@ -255,24 +300,31 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
         lsum += wt * wl[w * 8 + h];
       }
     }
-    po[h][tid] = acc;
+    // push output h*128 + tid to the rank that finishes it (DSMEM store)
+    const int idx = h * DR_D + tid;
+    *cluster.map_shared_rank(&r_o[rank][idx % DR_OUT_PER_RANK], idx / DR_OUT_PER_RANK) = acc;
     if (tid == 0) {
-      pm[h] = M;
-      pl[h] = lsum;
+      for (int q = (h * DR_D) / DR_OUT_PER_RANK; q <= (h * DR_D + DR_D - 1) / DR_OUT_PER_RANK; ++q) {
+        *cluster.map_shared_rank(&r_m[rank][h], q) = M;
+        *cluster.map_shared_rank(&r_l[rank][h], q) = lsum;
+      }
     }
   }
+  // One cluster barrier: every push has landed (release/acquire), and after it
+  // no CTA touches another's shared memory, so none has to wait for the
+  // others before exiting.
   cluster.sync();
-  // Combine the cluster: rank r finishes outputs [112 r, 112 r + 112) of the
-  // group's 7 x 128, reading every rank's partial over DSMEM.
+  // Rank r finishes outputs [112 r, 112 r + 112) of the group's 7 x 128 from
+  // the 8 partials in its own shared memory.
   if (tid < DR_OUT_PER_RANK) {
     const int idx = rank * DR_OUT_PER_RANK + tid;
     const int g = idx / DR_D, d = idx % DR_D;
     float mr[DR_CLUSTER], lr[DR_CLUSTER], orr[DR_CLUSTER];
 #pragma unroll
     for (int r = 0; r < DR_CLUSTER; ++r) {
-      mr[r] = *cluster.map_shared_rank(&pm[g], r);
-      lr[r] = *cluster.map_shared_rank(&pl[g], r);
-      orr[r] = *cluster.map_shared_rank(&po[g][d], r);
+      mr[r] = r_m[r][g];
+      lr[r] = r_l[r][g];
+      orr[r] = r_o[r][tid];
     }
     float m = -INFINITY;
 #pragma unroll
@@ -290,7 +342,6 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
       p.lse[static_cast<size_t>(b) * p.Hq + kvh * DR_G + g] =
           l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
   }
-  cluster.sync();  // keep every CTA's smem alive until the others have read it
 }
 
 }  // namespace stdb
@@ -309,7 +360,7 @@ extern "C" size_t std_draft_attn_workspace_bytes(int B, int Hq, int Hkv, int D, 
 
 extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
                               int len_offset, int B, int Hq, int Hkv, int D, int cap, void* out, float* lse,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+                              void* workspace, size_t workspace_bytes, int flags, void* stream) {
   (void)workspace;
   (void)workspace_bytes;
   if (D != stdb::DR_D || Hq != Hkv * stdb::DR_G || B <= 0 || cap <= 0) return 1;
@@ -341,6 +392,7 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
+  p.flags = flags & 1;
   dim3 grid(stdb::DR_CLUSTER, Hkv, B);
   return launch_pdl(stdb::draft_attn_kernel, grid, dim3(stdb::DR_THREADS), stdb::DR_SMEM,
                     static_cast<cudaStream_t>(stream), tk, tv, p) == cudaSuccess

@@ -10,7 +10,9 @@ number measures HBM, not L2.  The launches are captured into a CUDA graph and
 timed over one replay (`--eager` times plain Python-level calls instead, which
 adds the host cost of each call).  Prints achieved algorithmic GB/s:
   verify: B * (2048*L + 143360) bytes per launch  (K/V rows + q/out)
-  draft:  B * (2048*L + 14336)  bytes per launch
+  draft:  B * (2048*L + 14336)  bytes per launch (launched as in a decode
+          step, STD_DRAFT_AFTER_APPEND: the preceding draft launch writes none
+          of its inputs)
   gemm:   2*N*K (weights) + 2*M*K + 2*M*N bytes per launch
 This is also the target command of the ncu captures summarised in profiles/.
 """
@@ -66,7 +68,7 @@ def main() -> None:
         lens = torch.full((B,), L, dtype=torch.int32, device=dev)
 
         def run(i):
-            ops.draft_attention(q, ks[i], vs[i], lens, 0)
+            ops.draft_attention(q, ks[i], vs[i], lens, 0, after_append=True)
 
         nbytes = B * (2048 * L + 14336)
     us = _time(a, run, n_caches)

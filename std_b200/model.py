@@ -180,7 +180,8 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
             ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
                             ws.q[:M], kc, vc)
         if sparse:
-            ops.draft_attention(ws.q[:M], kc, vc, lens, len_offset, out=ws.attn[:M].view(B, Hq, D))
+            ops.draft_attention(ws.q[:M], kc, vc, lens, len_offset, out=ws.attn[:M].view(B, Hq, D),
+                                after_append=True)
         elif dense_attn is not None:
             dense_attn.attend(li, ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset, ws.attn[:M].view(B, n, Hq, D))
         else:

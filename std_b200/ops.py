@@ -53,8 +53,13 @@ def workspace(kind: str, nbytes: int, device: torch.device) -> torch.Tensor:
 # ----------------------------------------------------------------------------
 
 def draft_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
-                    len_offset: int = 0, out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
-    """q [B, Hq, D] bf16; caches [B, Hkv, cap, D] bf16; lens [B] int32 (device)."""
+                    len_offset: int = 0, out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                    after_append: bool = False):
+    """q [B, Hq, D] bf16; caches [B, Hkv, cap, D] bf16; lens [B] int32 (device).
+
+    after_append=True (STD_DRAFT_AFTER_APPEND): the previous launch on the
+    stream writes only q and each request's newest K/V row, so the kernel may
+    start reading the older rows before it finishes."""
     B, Hq, D = q.shape
     _, Hkv, cap, _ = k_cache.shape
     for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
@@ -65,7 +70,8 @@ def draft_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     nb = _lib.query("std_draft_attn_workspace_bytes", B, Hq, Hkv, D, cap)
     ws = workspace("draft", nb, q.device)
     _lib.call("std_draft_attn", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr(), int(len_offset),
-              B, Hq, Hkv, D, cap, out.data_ptr(), _p(lse), ws.data_ptr(), ws.numel(), _stream())
+              B, Hq, Hkv, D, cap, out.data_ptr(), _p(lse), ws.data_ptr(), ws.numel(), 1 if after_append else 0,
+              _stream())
     return out
 
 

@@ -28,7 +28,7 @@ def test_host_side_argument_checks_without_gpu():
     lib = _lib.load()
     assert lib.std_version() == 100
     # bad shapes are rejected on the host before any CUDA call
-    assert lib.std_draft_attn(None, None, None, None, 0, 1, 28, 4, 64, 16, None, None, None, 0, None) == 1
+    assert lib.std_draft_attn(None, None, None, None, 0, 1, 28, 4, 64, 16, None, None, None, 0, 0, None) == 1
     assert lib.std_verify_attn(None, None, None, None, 0, 19, 1, 1, 28, 4, 128, 16, None, None, None, 0, None) == 1
     assert lib.std_topk_select(None, 10, 1, None, 5, 6, None, None) == 1
     assert lib.std_draft_attn_workspace_bytes(1, 28, 4, 128, 1024) == 0  # merged in DSMEM

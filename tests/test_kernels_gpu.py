@@ -429,3 +429,32 @@ def test_gemm_rope_append_equals_unfused(ops, B, n, cfg):
     assert torch.equal(caches[0], caches[1])
     assert caches[1].abs().sum().item() > 0
     _no_device_error(ops)
+
+
+def test_draft_after_append_reads_the_new_row(ops):
+    """STD_DRAFT_AFTER_APPEND: the draft kernel starts on the older K/V rows
+    while the preceding RoPE + append kernel still runs; the appended row and q
+    must still be the new ones.  Compared against the same draft launched
+    after a full synchronisation, over several steps."""
+    B, Hq, Hkv, D, cap = 8, 28, 4, 128, 1280
+    g = torch.Generator(device="cuda").manual_seed(5)
+    k = torch.randn(B, Hkv, cap, D, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, Hkv, cap, D, generator=g, device="cuda").to(torch.bfloat16)
+    lens = torch.full((B,), 1000, dtype=torch.int32, device="cuda")
+    lens[1] = 1001
+    lens[5] = 1063
+    max_pos = 4096
+    ang = torch.arange(max_pos, device="cuda").float()[:, None] * (1e6 ** (-torch.arange(0, D, 2, device="cuda")
+                                                                         .float() / D))[None, :]
+    cos_t, sin_t = ang.cos().to(torch.bfloat16).contiguous(), ang.sin().to(torch.bfloat16).contiguous()
+    q = torch.empty(B, Hq, D, dtype=torch.bfloat16, device="cuda")
+    for step in range(4):
+        qkv = torch.randn(B, (Hq + 2 * Hkv) * D, generator=g, device="cuda").to(torch.bfloat16)
+        torch.cuda.synchronize()
+        ops.rope_append(qkv, B, 1, Hq, Hkv, D, lens, step, lens, step, cos_t, sin_t, q, k, v)
+        fast = ops.draft_attention(q, k, v, lens, step + 1, after_append=True)
+        torch.cuda.synchronize()
+        ref = ops.draft_attention(q, k, v, lens, step + 1)
+        torch.cuda.synchronize()
+        assert torch.equal(fast, ref), step
+    _no_device_error(ops)
