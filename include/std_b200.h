@@ -159,7 +159,7 @@ int std_silu_mul(const void* gu, int M, int I, void* out, void* stream);
 /* residual add (modeling_qwen2_5_vl.py:1200-1221). */
 int std_add(const void* a, const void* b, size_t n, void* out, void* stream);
 /* std_qwen25vl.py:98-99, :806 (torch.argmax, first index on ties):
- * out[(row/n)*out_stride + out_start + row%n] = argmax(logits[row, :V]). */
+ * out[(row/n)*out_stride + out_start + row%n] = argmax(logits[row, :V]).  V % 8 == 0. */
 int std_argmax_rows(const void* logits, int rows, int V, int n, int out_stride, int out_start, int32_t* out,
                     void* stream);
 
@@ -185,6 +185,15 @@ size_t std_gemm_epilogue_workspace_bytes(int M, int N, int K);
  * Same result as std_gemm_bf16 followed by std_add_rmsnorm.  N/8 <= 512. */
 int std_gemm_add_rmsnorm(const void* x, const void* w, const void* bias, void* resid, const void* norm_w, float eps,
                          void* out, int M, int N, int K, void* workspace, size_t workspace_bytes, void* stream);
+/* Replaces: lm_head (modeling_qwen2_5_vl.py:1749) + the greedy argmax of the
+ * decode loops (std_qwen25vl.py:98-99, :806): for the first rows_out rows of
+ * x [M, K] . w [N, K]^T, out[(t/n)*out_stride + out_start + t%n] = first
+ * column of the maximum bf16 logit, without storing the logits.  keys: M
+ * uint64 scratch, all zero on entry (zero it once before the first call); the
+ * call leaves it zero.  Same result as std_gemm_bf16 + std_argmax_rows. */
+int std_gemm_argmax(const void* x, const void* w, int M, int N, int K, int rows_out, int n, int out_stride,
+                    int out_start, int32_t* out, unsigned long long* keys, void* workspace, size_t workspace_bytes,
+                    void* stream);
 /* Replaces: q/k/v_proj of a decode step (modeling_qwen2_5_vl.py:1050-1052),
  * RoPE (:690-732) and KVCache.cat (kv_cache.py:54-69): qkv = x . w^T + bias
  * (w [(Hq+2Hkv)*D, K]) then, per token row, the std_rope_append step on it.

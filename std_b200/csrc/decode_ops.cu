@@ -231,21 +231,27 @@ __global__ void add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, size_
 }
 
 // ------------------------------- argmax ------------------------------------
-// out[row] = first index of the maximum of logits[row, :V] (bf16).  Written to
-// out[(row / n) * out_stride + out_start + row % n].
-__global__ void __launch_bounds__(1024) argmax_kernel(const __nv_bfloat16* logits, int V, int n, int out_stride,
-                                                      int out_start, int32_t* out) {
+// out[row] = first index of the maximum of the row's V bf16 logits (V % 8 ==
+// 0), read 8 columns at a time from a row source (a logits matrix, or a
+// GEMM's split-K partials).  Written to out[(row / n) * out_stride +
+// out_start + row % n].
+template <class Src>
+__global__ void __launch_bounds__(1024) argmax_kernel(const Src logits, int V, int n, int out_stride, int out_start,
+                                                      int32_t* out) {
   pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x;
-  const __nv_bfloat16* lr = logits + static_cast<size_t>(row) * V;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = __bfloat162float(lr[i]);
-    if (v > best || (v == best && i < bi)) {
-      best = v;
-      bi = i;
+  for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
+    float v8[8];
+    logits.load8(row, c, v8);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (v8[k] > best || (v8[k] == best && c + k < bi)) {
+        best = v8[k];
+        bi = c + k;
+      }
     }
   }
 #pragma unroll
@@ -476,8 +482,10 @@ extern "C" int std_add(const void* a, const void* b, size_t n, void* out, void* 
 extern "C" int std_argmax_rows(const void* logits, int rows, int V, int n, int out_stride, int out_start, int32_t* out,
                                void* stream) {
   if (rows <= 0 || V <= 0 || n <= 0) return 1;
-  return launch_pdl(stdb::argmax_kernel, dim3(rows), dim3(1024), 0, static_cast<cudaStream_t>(stream),
-                    static_cast<const __nv_bfloat16*>(logits), V, n, out_stride, out_start, out) == cudaSuccess
+  if (V % 8 != 0) return 1;
+  return launch_pdl(stdb::argmax_kernel<stdb::Bf16Rows>, dim3(rows), dim3(1024), 0, static_cast<cudaStream_t>(stream),
+                    stdb::Bf16Rows{static_cast<const __nv_bfloat16*>(logits), V}, V, n, out_stride, out_start,
+                    out) == cudaSuccess
              ? 0
              : 4;
 }

@@ -37,6 +37,11 @@ struct GemmParams {
   const __nv_bfloat16* bias;  // [N] or null
   __nv_bfloat16* y;           // [M, N]
   float* partial;             // [splits, M, N] (splits > 1)
+  // fused greedy argmax (splits == 1): instead of storing y, fold each row's
+  // bf16 values into amax_keys[t] (rows t < amax_rows) with atomicMax on
+  // (order_key(value) << 32 | ~column): the maximum, first column on ties
+  unsigned long long* amax_keys;
+  int amax_rows;
 };
 
 __global__ void __launch_bounds__(GM_THREADS)
@@ -129,7 +134,26 @@ __global__ void __launch_bounds__(GM_THREADS)
   const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const float bias = (p.splits == 1 && p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
   // ncols is a power of two >= max(nmma, 32), so 32-column loads stay inside it
-  for (int t0 = 0; t0 < p.nmma; t0 += 32) {
+  for (int t0 = 0; p.amax_keys != nullptr && t0 < p.nmma; t0 += 32) {
+    uint32_t v[32];
+    tmem_ld32(trow + t0, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = t0 + j;
+      unsigned long long key = 0ull;
+      if (t < p.amax_rows && f < p.N)
+        key = (static_cast<unsigned long long>(order_key(bf16_round(__uint_as_float(v[j]) + bias))) << 32) |
+              (0xFFFFFFFFu - static_cast<uint32_t>(f));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if (lane == 0 && key != 0ull) atomicMax(&p.amax_keys[t], key);
+    }
+  }
+  for (int t0 = 0; p.amax_keys == nullptr && t0 < p.nmma; t0 += 32) {
     uint32_t v[32];
     tmem_ld32(trow + t0, v);
     tmem_wait_ld();
@@ -225,6 +249,20 @@ struct GemmOut {
   }
 };
 
+// out[(t / n) * out_stride + out_start + t % n] = column of amax_keys[t]; the
+// keys are cleared for the next call.
+__global__ void argmax_keys_kernel(unsigned long long* keys, int rows, int n, int out_stride, int out_start,
+                                   int32_t* out) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rows) return;
+  const unsigned long long k = keys[t];
+  out[(t / n) * out_stride + out_start + t % n] =
+      k == 0ull ? 0 : static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+  keys[t] = 0ull;
+}
+
 }  // namespace stdb
 
 // ---------------------------------------------------------------------------
@@ -260,7 +298,7 @@ extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
 // Launch gemm_kernel: with splits > 1 it writes fp32 partials to `partial`,
 // otherwise bf16 y (+ bias).  Shapes are checked by the callers.
 static int gemm_launch(const void* x, const void* w, const void* bias, void* y, float* partial, int M, int N, int K,
-                       int splits, cudaStream_t s) {
+                       int splits, cudaStream_t s, unsigned long long* amax_keys = nullptr, int amax_rows = 0) {
   const int nmma = gemm_nmma(M);
   const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
   int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
@@ -291,6 +329,8 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.y = static_cast<__nv_bfloat16*>(y);
   p.partial = partial;
+  p.amax_keys = amax_keys;
+  p.amax_rows = amax_rows;
   // may begin while the previous kernel in the stream finishes: the weight
   // tiles of the first stages are requested before griddepcontrol.wait
   return launch_pdl(stdb::gemm_kernel, dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits), dim3(stdb::GM_THREADS),
@@ -394,6 +434,32 @@ extern "C" int std_gemm_rope_append(const void* x, const void* w, const void* bi
   const int nt = (((Hq + 2 * Hkv) * (D / 16) + 31) / 32) * 32;
   return launch_pdl(stdb::rope_append_kernel<stdb::GemmOut>, dim3(M), dim3(nt), 0, s,
                     gemm_out_view(workspace, bias, splits, M, N), p) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+// lm_head + greedy argmax: the argmax of each of the first `rows_out` rows of
+// x . w^T (bf16 logits, first index on ties) without storing the logits.
+extern "C" int std_gemm_argmax(const void* x, const void* w, int M, int N, int K, int rows_out, int n, int out_stride,
+                               int out_start, int32_t* out, unsigned long long* keys, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (!gemm_shape_ok(x, w, M, N, K, 8) || out == nullptr || keys == nullptr) return 1;
+  if (rows_out <= 0 || rows_out > M || n <= 0) return 1;
+  const int splits = gemm_splits(N, K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (splits == 1) {
+    int rc = gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, keys, rows_out);
+    if (rc != 0) return rc;
+    return launch_pdl(stdb::argmax_keys_kernel, dim3((rows_out + 127) / 128), dim3(128), 0, s, keys, rows_out, n,
+                      out_stride, out_start, out) == cudaSuccess
+               ? 0
+               : 4;
+  }
+  if (workspace == nullptr || workspace_bytes < std_gemm_epilogue_workspace_bytes(M, N, K)) return 5;
+  int rc = gemm_launch(x, w, nullptr, workspace, static_cast<float*>(workspace), M, N, K, splits, s);
+  if (rc != 0) return rc;
+  return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,
+                    gemm_out_view(workspace, nullptr, splits, M, N), N, n, out_stride, out_start, out) == cudaSuccess
              ? 0
              : 4;
 }

@@ -11,7 +11,7 @@ Compute split:
   * decode forwards: every kernel is from libstd_b200.so -- the tcgen05
     weight-streaming GEMM for projections, MLP and lm_head, RMSNorm (fused
     with the residual add), RoPE + KV append, draft / verify attention,
-    SiLU*up, argmax;
+    SiLU*up, lm_head fused with the greedy argmax;
   * prefill (thousands of rows): cuBLAS GEMMs through torch and torch SDPA
     attention (library flash/efficient kernels), as the reference does.
 Dense decode forwards (AR steps and verify) always run their GEMMs on the same
@@ -136,7 +136,6 @@ class Workspace:
         self.o = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
         self.gu = torch.zeros(rows, 2 * c.intermediate_size, device=d, dtype=dt)
         self.act = torch.zeros(rows, c.intermediate_size, device=d, dtype=dt)
-        self.logits = torch.zeros(rows, c.vocab_size, device=d, dtype=dt)
 
 
 def _mm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[torch.Tensor] = None):
@@ -197,8 +196,7 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
         ops.gemm_add_rmsnorm(ws.act[:rows], lw.w_down, x, next_norm, c.rms_norm_eps, h)
     if argmax_out is None:
         return
-    _mm(h, model.lm_head, ws.logits[:rows])
-    ops.argmax_rows(ws.logits[:M], argmax_out, n=n, out_stride=argmax_stride, out_start=argmax_start)
+    ops.gemm_argmax(h, model.lm_head, argmax_out, rows_out=M, n=n, out_stride=argmax_stride, out_start=argmax_start)
 
 
 # ---------------------------------------------------------------------- prefill

@@ -212,6 +212,25 @@ def gemm_add_rmsnorm(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor, norm
     return out
 
 
+def gemm_argmax(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, rows_out: Optional[int] = None, n: int = 1,
+                out_stride: int = 1, out_start: int = 0):
+    """Greedy argmax of x @ w^T's bf16 rows (lm_head + argmax) without storing the logits.
+
+    Result t (< rows_out, default all rows) goes to out[(t//n)*out_stride + out_start + t%n]."""
+    M, K = x.shape
+    N = w.shape[0]
+    _check(x, torch.bfloat16, "x")
+    _check(w, torch.bfloat16, "w")
+    _check(out, torch.int32, "out")
+    rows_out = M if rows_out is None else rows_out
+    keys = workspace("argmax_keys", M * 8, x.device)  # zero-initialised, left zero by every call
+    nb = _lib.query("std_gemm_epilogue_workspace_bytes", M, N, K)
+    ws = workspace("gemm", nb, x.device)
+    _lib.call("std_gemm_argmax", x.data_ptr(), w.data_ptr(), M, N, K, rows_out, n, out_stride, out_start,
+              out.data_ptr(), keys.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    return out
+
+
 def gemm_rope_append(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], B: int, n: int, Hq: int,
                      Hkv: int, D: int, pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor, slot_off: int,
                      cos_t: torch.Tensor, sin_t: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor,

@@ -458,3 +458,29 @@ def test_draft_after_append_reads_the_new_row(ops):
         torch.cuda.synchronize()
         assert torch.equal(fast, ref), step
     _no_device_error(ops)
+
+
+@pytest.mark.parametrize("M,rows_out,N,K", [(8, 8, 152064, 3584), (80, 72, 152064, 3584), (80, 8, 1024, 896),
+                                            (16, 3, 4096, 896)])
+def test_gemm_argmax_equals_unfused(ops, M, rows_out, N, K):
+    """lm_head with the fused greedy argmax (no logits stored) == gemm() then
+    argmax_rows(), including ties (duplicated weight rows) and the split-K
+    fallback for small vocabularies; the key scratch is left zeroed."""
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    w[N - 1] = w[N // 2]   # exact ties: the first index must win
+    w[7] = w[N - 7]
+    logits = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, w, logits)
+    n = 4 if rows_out % 4 == 0 else 1
+    stride = 6
+    want = torch.full(((rows_out // n + 1) * stride,), -1, dtype=torch.int32, device="cuda")
+    got = want.clone()
+    ops.argmax_rows(logits[:rows_out], want, n=n, out_stride=stride, out_start=1)
+    for _ in range(2):  # the second call checks the keys were cleared
+        ops.gemm_argmax(x, w, got, rows_out=rows_out, n=n, out_stride=stride, out_start=1)
+        assert torch.equal(got, want)
+    assert torch.equal(want[1::stride][: rows_out // n], logits[:rows_out:n].float().argmax(dim=1).to(torch.int32)) \
+        or n != 1
+    _no_device_error(ops)
