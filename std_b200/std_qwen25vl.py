@@ -19,6 +19,7 @@ request keeps its own lengths and finishes independently.
 from __future__ import annotations
 
 import math
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -129,11 +130,63 @@ class PromptLayout:
         return PromptLayout(int(ids_cpu.numel()), last + 1, vis.to(device), nv.to(device))
 
 
-def initialize_past_key_values(model: Qwen25VLDecoder, batch_size: int, max_cache_len: int) -> torch.Tensor:
-    """One preallocated cache [layers, 2, B, Hkv, cap, D] (kv_cache.py:72-165)."""
+def allocate_kv_cache(model: Qwen25VLDecoder, batch_size: int, max_cache_len: int) -> torch.Tensor:
+    """One preallocated cache [layers, 2, B, Hkv, cap, D] bf16 -- the memory
+    layout of the reference's past_key_values_data [2*layers, B, Hkv, cap, D]
+    (kv_cache.py:72-165), with every layer's K and V slices contiguous."""
     c = model.config
     return torch.zeros(c.num_hidden_layers, 2, batch_size, c.num_key_value_heads, max_cache_len, c.head_dim,
                        device=model.device, dtype=model.dtype)
+
+
+class KVCache:
+    """One (layer, K or V) slice of a decode cache with the reference's
+    interface (kv_cache.py:6-69): data [B, Hkv, cap, D], current_length a 0-d
+    int64 tensor; shape reports the filled length, cat appends along dim 2,
+    copy moves rows selected by indices to prev_length.  The B200 decode loop
+    keeps its lengths on the device instead (STDRunner); this view is for
+    callers written against the reference's cache objects."""
+
+    def __init__(self, data: torch.Tensor, current_length: torch.Tensor):
+        self.data = data
+        self.current_length = current_length
+
+    @property
+    def shape(self):
+        return (self.data.shape[0], self.data.shape[1], int(self.current_length.item()), self.data.shape[3])
+
+    def copy(self, indices: torch.Tensor, prev_length: int, dim: int = 2) -> None:
+        tgt = self.data.index_select(dim, indices.to(self.data.device))
+        self.data.narrow(dim, prev_length, tgt.shape[dim]).copy_(tgt, non_blocking=True)
+        self.current_length.fill_(prev_length + tgt.shape[dim])
+
+    def cat(self, tensor: torch.Tensor, dim: int = 2) -> torch.Tensor:
+        n = int(self.current_length.item())
+        self.data.narrow(dim, n, tensor.shape[dim]).copy_(tensor)
+        self.current_length.add_(tensor.shape[dim])
+        return torch.narrow(self.data, 2, 0, n + tensor.shape[dim])
+
+
+def kv_cache_views(cache: torch.Tensor, current_length_data: Optional[torch.Tensor] = None):
+    """Reference-shaped views of an allocate_kv_cache tensor: (past_key_values
+    [[KVCache K, KVCache V] per layer], [data as [2*layers, B, Hkv, cap, D]],
+    current_length_data [2*layers] int64 on the CPU)."""
+    L = cache.shape[0]
+    data = cache.view(2 * L, *cache.shape[2:])
+    if current_length_data is None:
+        current_length_data = torch.zeros(2 * L, dtype=torch.long, device="cpu")
+    pkv = [[KVCache(data[2 * i + j], current_length_data[2 * i + j]) for j in range(2)] for i in range(L)]
+    return pkv, [data], current_length_data
+
+
+def initialize_past_key_values(model: Qwen25VLDecoder, batch_size: int = 1, max_cache_len: Optional[int] = None):
+    """kv_cache.py:72-165: (past_key_values, past_key_values_data_list,
+    current_length_data) over one zeroed cache.  Capacity: max_cache_len, else
+    SPECVLM_MAX_CACHE_LEN, else 16384 (the reference's default for this
+    model).  All layers live on the model's device."""
+    if max_cache_len is None:
+        max_cache_len = int(os.environ.get("SPECVLM_MAX_CACHE_LEN", 16384))
+    return kv_cache_views(allocate_kv_cache(model, batch_size, max_cache_len))
 
 
 def build_sparse_selection(scores: torch.Tensor, layout: PromptLayout, k: int) -> torch.Tensor:
@@ -181,8 +234,8 @@ class STDRunner:
             if shard.plan.cap != self.cap_d or not shard.is_owner:
                 raise ValueError("the shard plan must be built for this runner's dense capacity, on the owner rank")
             self.dense_shift = shard.plan.key_range(shard.plan.owner)[0]
-        self.dense = initialize_past_key_values(model, batch_size, self.cap_d - self.dense_shift)
-        self.sparse = initialize_past_key_values(model, batch_size, self.cap_s)
+        self.dense = allocate_kv_cache(model, batch_size, self.cap_d - self.dense_shift)
+        self.sparse = allocate_kv_cache(model, batch_size, self.cap_s)
         model.rope_tables(self.cap_d + 2)
         self.dense_rows = _round_up(batch_size * (gamma + 1), 16)
         self.ws = Workspace(model, max(self.dense_rows, batch_size))
@@ -224,7 +277,7 @@ class STDRunner:
         self.topk_per_request = []
         dn = []
         # a sharded owner prefills into a whole-length cache, then hands out the ranges
-        full = self.dense if self.shard is None else initialize_past_key_values(self.model, self.B, self.cap_d)
+        full = self.dense if self.shard is None else allocate_kv_cache(self.model, self.B, self.cap_d)
         for b in range(self.B):
             torch.cuda.synchronize()
             t0 = time.time()
