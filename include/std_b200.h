@@ -64,6 +64,18 @@ int std_draft_attn(const void* q, const void* k_cache, const void* v_cache, cons
                    int B, int Hq, int Hkv, int D, int cap, void* out, float* lse, void* workspace,
                    size_t workspace_bytes, int flags, void* stream);
 
+/* Index-based sparse cache (the reference's unused gather variant,
+ * std_qwen25vl.py:323-351, made the draft path): request b, KV head h attends
+ * to dense_k/v rows idx[b][h][0 .. n_idx) (ascending prompt positions of this
+ * layer's selection, read in place from the dense cache [B, Hkv, cap_dense, D])
+ * followed by rows 0 .. L-n_idx-1 of the tail [B, Hkv, tail_cap, D] that holds
+ * the generated tokens' draft-path K/V; L = lens[b]+len_offset.  Same result,
+ * byte for byte, as std_draft_attn over the compacted copy of those rows. */
+int std_draft_attn_indexed(const void* q, const void* dense_k, const void* dense_v, int cap_dense,
+                           const int32_t* idx, int n_idx, const void* tail_k, const void* tail_v, int tail_cap,
+                           const int32_t* lens, int len_offset, int B, int Hq, int Hkv, int D, void* out, float* lse,
+                           void* stream);
+
 /* ---- (c) parallel dense verify attention (also AR dense decode, nq = 1) -- */
 
 /* Replaces: modeling_qwen2_5_vl.py:1096-1133 (repeat_kv + F.sdpa with the

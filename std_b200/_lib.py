@@ -31,6 +31,7 @@ SIGNATURES: Dict[str, tuple] = {
     "std_device_supported": (I, []),
     "std_draft_attn_workspace_bytes": (SZ, [I, I, I, I, I]),
     "std_draft_attn": (I, [P, P, P, PI32, I, I, I, I, I, I, P, PF, P, SZ, I, P]),
+    "std_draft_attn_indexed": (I, [P, P, P, I, PI32, I, P, P, I, PI32, I, I, I, I, I, P, PF, P]),
     "std_verify_attn_workspace_bytes": (SZ, [I, I, I]),
     "std_verify_attn": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, P, PF, P, SZ, P]),
     "std_verify_attn_noalloc": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, P, PF, P]),

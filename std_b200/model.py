@@ -147,7 +147,7 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
                    tok: torch.Tensor, tok_start: int, pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor,
                    slot_off: int, lens: torch.Tensor, len_offset: int, sparse: bool,
                    argmax_out: Optional[torch.Tensor], argmax_stride: int = 1, argmax_start: int = 0,
-                   dense_attn=None) -> None:
+                   dense_attn=None, sparse_index=None) -> None:
     """One forward of n new tokens per request through all layers (graph-capturable).
 
     cache: [layers, 2, B, Hkv, cap, D].  sparse=True uses the draft kernel
@@ -158,6 +158,9 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     lm_head (a draft step whose prediction is never used).  dense_attn (a
     seq_shard.ShardExchange on the owner rank) replaces the local verify
     kernel by the sequence-sharded attention over every rank's key range.
+    sparse_index = (dense cache, selection [layers, B, Hkv, n_idx] int32):
+    the draft reads its prompt rows from the dense cache by position and
+    `cache` holds only the generated tokens' draft-path K/V (the tail).
     """
     c = model.config
     M = B * n
@@ -178,7 +181,11 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
             _mm(h, lw.w_qkv, ws.qkv[:rows], lw.b_qkv)
             ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
                             ws.q[:M], kc, vc)
-        if sparse:
+        if sparse and sparse_index is not None:
+            dense, sel = sparse_index
+            ops.draft_attention_indexed(ws.q[:M], dense[li, 0], dense[li, 1], sel[li], kc, vc, lens, len_offset,
+                                        out=ws.attn[:M].view(B, Hq, D))
+        elif sparse:
             ops.draft_attention(ws.q[:M], kc, vc, lens, len_offset, out=ws.attn[:M].view(B, Hq, D),
                                 after_append=True)
         elif dense_attn is not None:

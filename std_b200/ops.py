@@ -75,6 +75,28 @@ def draft_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     return out
 
 
+def draft_attention_indexed(q: torch.Tensor, dense_k: torch.Tensor, dense_v: torch.Tensor, idx: torch.Tensor,
+                            tail_k: torch.Tensor, tail_v: torch.Tensor, lens: torch.Tensor, len_offset: int = 0,
+                            out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None):
+    """Draft attention over dense-cache rows idx [B, Hkv, n_idx] (int32,
+    ascending) followed by the tail [B, Hkv, tail_cap, D]; keys per request =
+    lens[b] + len_offset."""
+    B, Hq, D = q.shape
+    _, Hkv, cap_d, _ = dense_k.shape
+    for t, n in ((q, "q"), (dense_k, "dense_k"), (dense_v, "dense_v"), (tail_k, "tail_k"), (tail_v, "tail_v")):
+        _check(t, torch.bfloat16, n)
+    _check(idx, torch.int32, "idx")
+    _check(lens, torch.int32, "lens")
+    if idx.shape[:2] != (B, Hkv):
+        raise ValueError("idx must be [B, Hkv, n_idx]")
+    if out is None:
+        out = torch.empty_like(q)
+    _lib.call("std_draft_attn_indexed", q.data_ptr(), dense_k.data_ptr(), dense_v.data_ptr(), cap_d, idx.data_ptr(),
+              idx.shape[2], tail_k.data_ptr(), tail_v.data_ptr(), tail_k.shape[2], lens.data_ptr(), int(len_offset),
+              B, Hq, Hkv, D, out.data_ptr(), _p(lse), _stream())
+    return out
+
+
 def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
                      len_offset: int, causal: bool = True, out: Optional[torch.Tensor] = None,
                      lse: Optional[torch.Tensor] = None):

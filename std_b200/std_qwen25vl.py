@@ -30,6 +30,12 @@ from . import ops
 from .model import Qwen25VLDecoder, Workspace, decode_forward, prefill_request
 
 SPARSE_ATTN_MODES = ("b200",)
+# "compact": the selected prompt rows are copied into a per-request sparse
+# cache (the reference's copy + compaction, std_qwen25vl.py:265-320);
+# "indexed": the draft reads them in place from the dense cache by position
+# (the reference's gather variant, :323-351) and only generated tokens get
+# sparse-path K/V rows.
+SPARSE_CACHE_MODES = ("compact", "indexed")
 VERIFY_MODES = ("parallel", "sequential")
 
 
@@ -210,13 +216,19 @@ class STDRunner:
 
     def __init__(self, model: Qwen25VLDecoder, batch_size: int, layout: PromptLayout, max_new_tokens: int,
                  gamma: int = 9, k: int = 896, eos_token_id: int = -1, ignore_eos: bool = False,
-                 use_graphs: bool = True, verify_mode: str = "parallel", shard=None):
+                 use_graphs: bool = True, verify_mode: str = "parallel", shard=None,
+                 sparse_cache: str = "compact"):
         c = model.config
         if gamma < 1 or 7 * (gamma + 1) > 126:
             raise ValueError("gamma must be in [1, 17]")
         if verify_mode not in VERIFY_MODES:
             raise ValueError(f"verify_mode must be one of {VERIFY_MODES}")
+        if sparse_cache not in SPARSE_CACHE_MODES:
+            raise ValueError(f"sparse_cache must be one of {SPARSE_CACHE_MODES}")
+        if sparse_cache == "indexed" and shard is not None:
+            raise ValueError("an indexed sparse cache reads the dense prompt rows, which a sharded owner does not hold")
         self.verify_mode = verify_mode
+        self.sparse_cache = sparse_cache
         self.model, self.B, self.layout = model, batch_size, layout
         self.gamma, self.k, self.max_new = gamma, k, max_new_tokens
         self.eos, self.ignore_eos, self.use_graphs = eos_token_id, ignore_eos, use_graphs
@@ -235,7 +247,16 @@ class STDRunner:
                 raise ValueError("the shard plan must be built for this runner's dense capacity, on the owner rank")
             self.dense_shift = shard.plan.key_range(shard.plan.owner)[0]
         self.dense = allocate_kv_cache(model, batch_size, self.cap_d - self.dense_shift)
-        self.sparse = allocate_kv_cache(model, batch_size, self.cap_s)
+        if sparse_cache == "indexed":
+            # tail: draft-path K/V of generated tokens; prompt rows by position
+            self.sparse_shift = self.compact_len
+            self.sparse = allocate_kv_cache(model, batch_size, _round_up(max_new_tokens + gamma + 2, 64))
+            self.sel_idx = torch.zeros(c.num_hidden_layers, batch_size, c.num_key_value_heads, self.compact_len,
+                                       dtype=torch.int32, device=model.device)
+        else:
+            self.sparse_shift = 0
+            self.sparse = allocate_kv_cache(model, batch_size, self.cap_s)
+            self.sel_idx = None
         model.rope_tables(self.cap_d + 2)
         self.dense_rows = _round_up(batch_size * (gamma + 1), 16)
         self.ws = Workspace(model, max(self.dense_rows, batch_size))
@@ -289,7 +310,11 @@ class STDRunner:
                 topk = build_sparse_selection(scores, self.layout, self.k)
                 torch.cuda.synchronize()
                 t2 = time.time()
-                compact_sparse_prompt_cache(full, self.sparse, b, self.layout, topk)
+                if self.sel_idx is not None:
+                    nv = self.layout.non_visual.view(1, 1, -1).expand(topk.shape[0], topk.shape[1], -1)
+                    self.sel_idx[:, b] = torch.cat([nv, topk], dim=-1).sort(dim=-1).values
+                else:
+                    compact_sparse_prompt_cache(full, self.sparse, b, self.layout, topk)
                 torch.cuda.synchronize()
                 t["selection_time"] += t2 - t1
                 t["sparse_cache_time"] += time.time() - t2
@@ -323,13 +348,16 @@ class STDRunner:
         self.all_done.zero_()
 
     # ------------------------------------------------------------------ steps
+    def _sparse_index(self):
+        return None if self.sel_idx is None else (self.dense, self.sel_idx)
+
     def _draft_step(self, i: int) -> None:
         last = i == self.gamma - 1
         decode_forward(self.model, self.ws, self.sparse, B=self.B, n=1, rows=self.B, tok=self.tok, tok_start=1 + i,
-                       pos_base=self.ctx_len, pos_off=i, slot_base=self.sparse_len, slot_off=i,
+                       pos_base=self.ctx_len, pos_off=i, slot_base=self.sparse_len, slot_off=i - self.sparse_shift,
                        lens=self.sparse_len, len_offset=i + 1, sparse=True,
                        argmax_out=None if last else self.tok.view(-1), argmax_stride=self.tok_stride,
-                       argmax_start=2 + i)
+                       argmax_start=2 + i, sparse_index=self._sparse_index())
 
     def _verify(self, pending: int) -> None:
         nq = self.gamma + pending
@@ -371,9 +399,9 @@ class STDRunner:
 
     def _bonus_step(self) -> None:
         decode_forward(self.model, self.ws, self.sparse, B=self.B, n=1, rows=self.B, tok=self.tok, tok_start=0,
-                       pos_base=self.ctx_len, pos_off=-1, slot_base=self.sparse_len, slot_off=-1,
+                       pos_base=self.ctx_len, pos_off=-1, slot_base=self.sparse_len, slot_off=-1 - self.sparse_shift,
                        lens=self.sparse_len, len_offset=0, sparse=True, argmax_out=self.tok.view(-1),
-                       argmax_stride=self.tok_stride, argmax_start=1)
+                       argmax_stride=self.tok_stride, argmax_start=1, sparse_index=self._sparse_index())
 
     def _drafts(self) -> None:
         for i in range(self.gamma):
@@ -581,14 +609,16 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                           adaptive_gamma_mode: str = "accept_len", copy_sparse_prefill: bool = True,
                           profile_prefill: bool = False, verify_attn_backend: str = "default",
                           verify_margin_threshold: Optional[float] = None, use_compile: bool = False,
-                          ignore_eos: bool = False,
-                          runner: Optional[STDRunner] = None) -> Tuple[GenerateResult, SparseSelection]:
+                          ignore_eos: bool = False, runner: Optional[STDRunner] = None,
+                          sparse_cache: str = "compact") -> Tuple[GenerateResult, SparseSelection]:
     """Sparse-to-Dense greedy decoding (std_qwen25vl.py:609-978).
 
     Implemented: verify_mode="parallel" | "sequential", verify_fallback="none",
     sparse_attn_mode="b200", copy_sparse_prefill=True, fixed gamma.  Other
     values of the reference's research flags raise ValueError (there is no
-    alternative backend to dispatch to)."""
+    alternative backend to dispatch to).  B200 extension: sparse_cache=
+    "indexed" reads the selected prompt rows in place from the dense cache
+    instead of compacting a copy (same tokens)."""
     if verify_mode not in VERIFY_MODES:
         raise ValueError(f"Unsupported verify_mode={verify_mode!r}; expected one of {VERIFY_MODES}.")
     if verify_fallback != "none":
@@ -606,7 +636,7 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                          explicit_k)
     if runner is None:
         runner = STDRunner(model, ids.shape[0], layout, max_new_tokens, gamma=gamma, k=k, eos_token_id=eos_token_id,
-                           ignore_eos=ignore_eos, verify_mode=verify_mode)
+                           ignore_eos=ignore_eos, verify_mode=verify_mode, sparse_cache=sparse_cache)
     elif runner.verify_mode != verify_mode:
         raise ValueError("the runner was built for a different verify_mode")
     tp = runner.prefill(embeds, with_selection=True)

@@ -137,3 +137,33 @@ def test_full_selection_accepts_nearly_everything():
     std_tokens = runner.out_tokens.clone()
     runner.run_ar()
     assert torch.equal(std_tokens, runner.out_tokens)
+
+
+@pytest.mark.parametrize("B,gamma", [(2, 5), (1, 9)])
+def test_indexed_sparse_cache_matches_compacted(B, gamma):
+    """sparse_cache="indexed" (prompt rows read in place from the dense cache)
+    produces the same tokens and accept lengths as the compacted copy, and
+    both equal AR."""
+    from std_b200 import ops
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import STDRunner, _prepare, selection_budget
+
+    model = Qwen25VLDecoder(TINY, seed=6)
+    V, T = 700, 24
+    inp = _inputs(B, V, T, TINY.vocab_size, TINY.hidden_size, seed=40 + B)
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    res = {}
+    for mode, k in (("compact", V), ("indexed", V), ("compact", 150), ("indexed", 150)):
+        runner = STDRunner(model, B, layout, 30, gamma=gamma, k=k, ignore_eos=True, sparse_cache=mode)
+        runner.prefill(embeds, with_selection=True)
+        runner.run_std()
+        res[(mode, k)] = (runner.out_tokens.cpu().clone(), runner.std_stats()["accept_lengths"])
+        if mode == "indexed" and k == 150:
+            runner.run_ar()
+            ar = runner.out_tokens.cpu().clone()
+    assert ops.device_error() == 0
+    for k in (V, 150):
+        assert torch.equal(res[("compact", k)][0], res[("indexed", k)][0])
+        assert res[("compact", k)][1] == res[("indexed", k)][1]
+    assert torch.equal(res[("indexed", 150)][0], ar)
+    assert sum(map(sum, res[("indexed", V)][1])) > 0   # full selection: long accepted prefixes exercised

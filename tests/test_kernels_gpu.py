@@ -484,3 +484,37 @@ def test_gemm_argmax_equals_unfused(ops, M, rows_out, N, K):
     assert torch.equal(want[1::stride][: rows_out // n], logits[:rows_out:n].float().argmax(dim=1).to(torch.int32)) \
         or n != 1
     _no_device_error(ops)
+
+
+@pytest.mark.parametrize("B,n_idx,tail", [(8, 1024, 1), (1, 1024, 130), (3, 896, 40), (2, 3968, 129)])
+def test_draft_indexed_equals_compacted(ops, B, n_idx, tail):
+    """Index-based sparse cache: reading the selected prompt rows in place from
+    the dense cache (plus a tail of generated rows) gives the same bytes as the
+    draft kernel over the compacted copy of the same rows."""
+    Hkv, Hq, D, P = 4, 28, 128, 4200
+    g = torch.Generator(device="cuda").manual_seed(B * 10 + tail)
+    dense_k = torch.randn(B, Hkv, P + 64, D, generator=g, device="cuda").to(torch.bfloat16)
+    dense_v = torch.randn(B, Hkv, P + 64, D, generator=g, device="cuda").to(torch.bfloat16)
+    idx = torch.stack([torch.stack([torch.randperm(P, generator=torch.Generator().manual_seed(b * 7 + h))[:n_idx]
+                                    .sort().values for h in range(Hkv)]) for b in range(B)]).to(torch.int32).cuda()
+    tail_cap = 192
+    tail_k = torch.randn(B, Hkv, tail_cap, D, generator=g, device="cuda").to(torch.bfloat16)
+    tail_v = torch.randn(B, Hkv, tail_cap, D, generator=g, device="cuda").to(torch.bfloat16)
+    cap_c = n_idx + tail_cap
+    comp_k = torch.zeros(B, Hkv, cap_c, D, dtype=torch.bfloat16, device="cuda")
+    comp_v = torch.zeros_like(comp_k)
+    for b in range(B):
+        for h in range(Hkv):
+            comp_k[b, h, :n_idx] = dense_k[b, h, idx[b, h].long()]
+            comp_v[b, h, :n_idx] = dense_v[b, h, idx[b, h].long()]
+    comp_k[:, :, n_idx:] = tail_k
+    comp_v[:, :, n_idx:] = tail_v
+    q = torch.randn(B, Hq, D, generator=g, device="cuda").to(torch.bfloat16)
+    lens = torch.full((B,), n_idx + tail - 1, dtype=torch.int32, device="cuda")
+    lse_a = torch.empty(B, Hq, device="cuda")
+    lse_b = torch.empty(B, Hq, device="cuda")
+    a = ops.draft_attention(q, comp_k, comp_v, lens, 1, lse=lse_a)
+    b_ = ops.draft_attention_indexed(q, dense_k, dense_v, idx, tail_k, tail_v, lens, 1, lse=lse_b)
+    assert torch.equal(a, b_)
+    assert torch.equal(lse_a, lse_b)
+    _no_device_error(ops)
