@@ -166,8 +166,10 @@ int std_add_rmsnorm(void* x, const void* delta, const void* w, float eps, int M,
 int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, int D, const int32_t* pos_base, int pos_off,
                     const int32_t* slot_base, int slot_off, const void* cos_t, const void* sin_t, int max_pos,
                     void* q_out, void* k_cache, void* v_cache, int cap, void* stream);
-/* modeling_qwen2_5_vl.py:674-687 (Qwen2MLP act_fn(gate) * up), gu = [gate | up]. */
-int std_silu_mul(const void* gu, int M, int I, void* out, void* stream);
+/* modeling_qwen2_5_vl.py:674-687 (Qwen2MLP act_fn(gate) * up): gu rows of 2I
+ * columns, [gate | up] halves, or with interleaved != 0 64-feature
+ * [gate | up] blocks (I % 64 == 0); out [M, I]. */
+int std_silu_mul(const void* gu, int M, int I, int interleaved, void* out, void* stream);
 /* residual add (modeling_qwen2_5_vl.py:1200-1221). */
 int std_add(const void* a, const void* b, size_t n, void* out, void* stream);
 /* std_qwen25vl.py:98-99, :806 (torch.argmax, first index on ties):
@@ -197,6 +199,14 @@ size_t std_gemm_epilogue_workspace_bytes(int M, int N, int K);
  * Same result as std_gemm_bf16 followed by std_add_rmsnorm.  N/8 <= 512. */
 int std_gemm_add_rmsnorm(const void* x, const void* w, const void* bias, void* resid, const void* norm_w, float eps,
                          void* out, int M, int N, int K, void* workspace, size_t workspace_bytes, void* stream);
+/* Replaces: Qwen2MLP's act_fn(gate_proj(x)) * up_proj(x)
+ * (modeling_qwen2_5_vl.py:674-687): act[M, I] from x [M, K] and the fused
+ * gate/up weights w [2I, K] stored as 64-row [gate | up] blocks (a checkpoint
+ * loader interleaves gate_proj and up_proj rows that way), without storing
+ * the [M, 2I] intermediate.  Same result as std_gemm_bf16 followed by
+ * std_silu_mul(interleaved = 1).  I % 64 == 0. */
+int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int K, void* act, void* workspace,
+                      size_t workspace_bytes, void* stream);
 /* Replaces: lm_head (modeling_qwen2_5_vl.py:1749) + the greedy argmax of the
  * decode loops (std_qwen25vl.py:98-99, :806): for the first rows_out rows of
  * x [M, K] . w [N, K]^T, out[(t/n)*out_stride + out_start + t%n] = first

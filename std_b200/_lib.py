@@ -45,13 +45,14 @@ SIGNATURES: Dict[str, tuple] = {
     "std_gemm_bf16": (I, [P, P, P, P, I, I, I, P, SZ, P]),
     "std_gemm_epilogue_workspace_bytes": (SZ, [I, I, I]),
     "std_gemm_add_rmsnorm": (I, [P, P, P, P, P, F, P, I, I, I, P, SZ, P]),
+    "std_gemm_silu_mul": (I, [P, P, I, I, I, P, P, SZ, P]),
     "std_gemm_argmax": (I, [P, P, I, I, I, I, I, I, I, PI32, P, P, SZ, P]),
     "std_gemm_rope_append": (I, [P, P, P, I, I, I, I, I, I, P, I, P, I, P, P, I, P, P, P, I, P, SZ, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
     "std_rmsnorm": (I, [P, P, F, I, I, P, P]),
     "std_add_rmsnorm": (I, [P, P, P, F, I, I, P, P]),
     "std_rope_append": (I, [P, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I, P]),
-    "std_silu_mul": (I, [P, I, I, P, P]),
+    "std_silu_mul": (I, [P, I, I, I, P, P]),
     "std_add": (I, [P, P, SZ, P, P]),
     "std_argmax_rows": (I, [P, I, I, I, I, I, PI32, P]),
     "std_accept_commit": (I, [I, I, I, PI32, I, PI32, I, PI32, I, I, I, PI32, PI32, PI32, PI32, PI32, PI32, PI32,

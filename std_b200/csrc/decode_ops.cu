@@ -201,23 +201,31 @@ __global__ void __launch_bounds__(512) rope_append_kernel(const Src qkv, const R
 }
 
 // ------------------------------- SiLU * up ---------------------------------
-// gu rows: [gate (I) | up (I)]; out = bf16( bf16(silu(gate)) * up ), 8 per thread
-__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, size_t total8,
-                                __nv_bfloat16* __restrict__ out) {
+// out = bf16( bf16(silu(gate)) * up ), 8 features per thread.  gu rows hold
+// 2I columns: [gate (I) | up (I)], or with `interleaved` 64-feature blocks
+// [gate 64 | up 64] (the layout that lets the gate/up GEMM finish SiLU in its
+// own epilogue: one 128-row weight tile = 64 gate + 64 up rows).
+STD_DEV float silu_times(float g, float u) {
+  const float sg = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, __expf(-g))));
+  return __fmul_rn(sg, u);
+}
+
+template <class Src>
+__global__ void silu_mul_kernel(const Src gu, int I, int interleaved, size_t total8, __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_launch_dependents();
   const int I8 = I / 8;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total8;
        idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t row = idx / I8, c = (idx % I8) * 8;
+    const size_t row = idx / I8;
+    const int c = static_cast<int>(idx % I8) * 8;
+    const int gc = interleaved ? (c >> 6) * 128 + (c & 63) : c;
+    const int uc = interleaved ? gc + 64 : I + c;
     float g[8], u[8], y[8];
-    load8(gu + row * 2 * I + c, g);
-    load8(gu + row * 2 * I + I + c, u);
+    gu.load8(row, gc, g);
+    gu.load8(row, uc, u);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float sg = bf16_round(__fdiv_rn(g[k], __fadd_rn(1.0f, __expf(-g[k]))));
-      y[k] = __fmul_rn(sg, u[k]);
-    }
+    for (int k = 0; k < 8; ++k) y[k] = silu_times(g[k], u[k]);
     store8(out + row * I + c, y);
   }
 }
@@ -460,12 +468,13 @@ extern "C" int std_rope_append(const void* qkv, int B, int n, int Hq, int Hkv, i
              : 4;
 }
 
-extern "C" int std_silu_mul(const void* gu, int M, int I, void* out, void* stream) {
-  if (M <= 0 || I <= 0 || I % 8 != 0) return 1;
+extern "C" int std_silu_mul(const void* gu, int M, int I, int interleaved, void* out, void* stream) {
+  if (M <= 0 || I <= 0 || I % 8 != 0 || (interleaved && I % 64 != 0)) return 1;
   const size_t total8 = static_cast<size_t>(M) * I / 8;
   const int blocks = static_cast<int>((total8 + 255) / 256 < 148 * 8 ? (total8 + 255) / 256 : 148 * 8);
-  return launch_pdl(stdb::silu_mul_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                    static_cast<const __nv_bfloat16*>(gu), I, total8, static_cast<__nv_bfloat16*>(out)) == cudaSuccess
+  return launch_pdl(stdb::silu_mul_kernel<stdb::Bf16Rows>, dim3(blocks), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), stdb::Bf16Rows{static_cast<const __nv_bfloat16*>(gu), 2 * I},
+                    I, interleaved ? 1 : 0, total8, static_cast<__nv_bfloat16*>(out)) == cudaSuccess
              ? 0
              : 4;
 }

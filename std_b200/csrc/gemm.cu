@@ -42,6 +42,10 @@ struct GemmParams {
   // (order_key(value) << 32 | ~column): the maximum, first column on ties
   unsigned long long* amax_keys;
   int amax_rows;
+  // fused SiLU * up (splits == 1; weights in 64-row [gate | up] blocks): tile
+  // rows 0..63 are gate, 64..127 up of features 64*tile ..; writes
+  // act[t][64*tile + r] = bf16(bf16(silu(gate)) * up) instead of y
+  __nv_bfloat16* act;
 };
 
 __global__ void __launch_bounds__(GM_THREADS)
@@ -153,7 +157,40 @@ __global__ void __launch_bounds__(GM_THREADS)
       if (lane == 0 && key != 0ull) atomicMax(&p.amax_keys[t], key);
     }
   }
-  for (int t0 = 0; p.amax_keys == nullptr && t0 < p.nmma; t0 += 32) {
+  if (p.act != nullptr) {
+    // the stage buffers are free (every MMA retired): up rows go through smem
+    // [token][64] so that the gate rows' threads can pair them
+    __nv_bfloat16* s_up = reinterpret_cast<__nv_bfloat16*>(smem);
+    const int r = warp * 32 + lane;
+    if (warp >= 2) {
+      for (int t0 = 0; t0 < p.nmma; t0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(trow + t0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) s_up[(t0 + j) * 64 + (r - 64)] = __float2bfloat16_rn(__uint_as_float(v[j]));
+      }
+    }
+    __syncthreads();
+    if (warp < 2) {
+      const int I = p.N / 2;
+      const int feat = tile * 64 + r;
+      for (int t0 = 0; t0 < p.nmma; t0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(trow + t0, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int t = t0 + j;
+          if (t >= p.M) continue;
+          const float g = bf16_round(__uint_as_float(v[j]));
+          const float u = __bfloat162float(s_up[t * 64 + r]);
+          p.act[static_cast<size_t>(t) * I + feat] = __float2bfloat16_rn(silu_times(g, u));
+        }
+      }
+    }
+  }
+  for (int t0 = 0; p.amax_keys == nullptr && p.act == nullptr && t0 < p.nmma; t0 += 32) {
     uint32_t v[32];
     tmem_ld32(trow + t0, v);
     tmem_wait_ld();
@@ -298,7 +335,8 @@ extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
 // Launch gemm_kernel: with splits > 1 it writes fp32 partials to `partial`,
 // otherwise bf16 y (+ bias).  Shapes are checked by the callers.
 static int gemm_launch(const void* x, const void* w, const void* bias, void* y, float* partial, int M, int N, int K,
-                       int splits, cudaStream_t s, unsigned long long* amax_keys = nullptr, int amax_rows = 0) {
+                       int splits, cudaStream_t s, unsigned long long* amax_keys = nullptr, int amax_rows = 0,
+                       void* act = nullptr) {
   const int nmma = gemm_nmma(M);
   const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
   int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
@@ -331,6 +369,7 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   p.partial = partial;
   p.amax_keys = amax_keys;
   p.amax_rows = amax_rows;
+  p.act = static_cast<__nv_bfloat16*>(act);
   // may begin while the previous kernel in the stream finishes: the weight
   // tiles of the first stages are requested before griddepcontrol.wait
   return launch_pdl(stdb::gemm_kernel, dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits), dim3(stdb::GM_THREADS),
@@ -460,6 +499,27 @@ extern "C" int std_gemm_argmax(const void* x, const void* w, int M, int N, int K
   if (rc != 0) return rc;
   return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,
                     gemm_out_view(workspace, nullptr, splits, M, N), N, n, out_stride, out_start, out) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+// Qwen2MLP's act_fn(gate_proj(x)) * up_proj(x) in one pass over the fused
+// gate/up weights w [2I, K] stored as 64-row [gate | up] blocks.
+extern "C" int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int K, void* act, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  const int N = 2 * I;
+  if (!gemm_shape_ok(x, w, M, N, K, 8) || act == nullptr || I % 64 != 0) return 1;
+  const int splits = gemm_splits(N, K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (splits == 1) return gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, nullptr, 0, act);
+  if (workspace == nullptr || workspace_bytes < std_gemm_epilogue_workspace_bytes(M, N, K)) return 5;
+  int rc = gemm_launch(x, w, nullptr, workspace, static_cast<float*>(workspace), M, N, K, splits, s);
+  if (rc != 0) return rc;
+  const size_t total8 = static_cast<size_t>(M) * I / 8;
+  const int blocks = static_cast<int>((total8 + 255) / 256 < 148 * 8 ? (total8 + 255) / 256 : 148 * 8);
+  return launch_pdl(stdb::silu_mul_kernel<stdb::GemmOut>, dim3(blocks), dim3(256), 0, s,
+                    gemm_out_view(workspace, nullptr, splits, M, N), I, 1, total8,
+                    static_cast<__nv_bfloat16*>(act)) == cudaSuccess
              ? 0
              : 4;
 }

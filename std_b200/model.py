@@ -92,6 +92,9 @@ class Qwen25VLDecoder:
             lw.b_qkv = torch.zeros(c.qkv_size, device=self.device, dtype=dtype)
             lw.w_o = normal(H, H)
             lw.w_post = torch.ones(H, device=self.device, dtype=dtype)
+            # gate_proj and up_proj rows interleaved in 64-row blocks
+            # [gate 64 | up 64] (a checkpoint loader permutes them so), so one
+            # 128-row GEMM tile yields both halves of 64 features
             lw.w_gu = normal(2 * I, H)
             lw.w_down = normal(H, I)
             self.layers.append(lw)
@@ -134,7 +137,6 @@ class Workspace:
         self.q = torch.zeros(rows, c.num_attention_heads, c.head_dim, device=d, dtype=dt)
         self.attn = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
         self.o = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
-        self.gu = torch.zeros(rows, 2 * c.intermediate_size, device=d, dtype=dt)
         self.act = torch.zeros(rows, c.intermediate_size, device=d, dtype=dt)
 
 
@@ -194,8 +196,7 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
             ops.verify_attention(ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset,
                                  out=ws.attn[:M].view(B, n, Hq, D))
         ops.gemm_add_rmsnorm(ws.attn[:rows], lw.w_o, x, lw.w_post, c.rms_norm_eps, h)
-        _mm(h, lw.w_gu, ws.gu[:rows])
-        ops.silu_mul(ws.gu[:rows], ws.act[:rows])
+        ops.gemm_silu_mul(h, lw.w_gu, ws.act[:rows])
         if li + 1 < n_layers:
             next_norm = model.layers[li + 1].w_in
         else:  # the final norm feeds lm_head; a draft step without lm_head only adds
@@ -276,7 +277,7 @@ def prefill_segment(model: Qwen25VLDecoder, cache: torch.Tensor, b: int, x: torc
             s1 = min(S, s0 + chunk)
             gu = h[s0:s1] @ lw.w_gu.t()
             act = torch.empty(s1 - s0, c.intermediate_size, device=dev, dtype=model.dtype)
-            ops.silu_mul(gu, act)
+            ops.silu_mul(gu, act, interleaved=True)
             x[s0:s1] = x[s0:s1] + act @ lw.w_down.t()
             del gu, act
         del h

@@ -292,10 +292,25 @@ def rope_append(qkv: torch.Tensor, B: int, n: int, Hq: int, Hkv: int, D: int, po
     return q_out
 
 
-def silu_mul(gu: torch.Tensor, out: torch.Tensor):
+def silu_mul(gu: torch.Tensor, out: torch.Tensor, interleaved: bool = False):
+    """out = silu(gate) * up; gu columns [gate | up] or 64-feature [gate | up] blocks (interleaved)."""
     I2 = gu.shape[-1]
     M = gu.numel() // I2
-    _lib.call("std_silu_mul", gu.data_ptr(), M, I2 // 2, out.data_ptr(), _stream())
+    _lib.call("std_silu_mul", gu.data_ptr(), M, I2 // 2, 1 if interleaved else 0, out.data_ptr(), _stream())
+    return out
+
+
+def gemm_silu_mul(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor):
+    """out[M, I] = silu(x @ gate^T) * (x @ up^T) with w_gu [2I, K] in 64-row [gate | up] blocks."""
+    M, K = x.shape
+    N = w_gu.shape[0]
+    _check(x, torch.bfloat16, "x")
+    _check(w_gu, torch.bfloat16, "w_gu")
+    _check(out, torch.bfloat16, "out")
+    nb = _lib.query("std_gemm_epilogue_workspace_bytes", M, N, K)
+    ws = workspace("gemm", nb, x.device)
+    _lib.call("std_gemm_silu_mul", x.data_ptr(), w_gu.data_ptr(), M, N // 2, K, out.data_ptr(), ws.data_ptr(),
+              ws.numel(), _stream())
     return out
 
 

@@ -518,3 +518,26 @@ def test_draft_indexed_equals_compacted(ops, B, n_idx, tail):
     assert torch.equal(a, b_)
     assert torch.equal(lse_a, lse_b)
     _no_device_error(ops)
+
+
+@pytest.mark.parametrize("M,I,K", [(8, 18944, 3584), (80, 18944, 3584), (16, 1536, 896), (200, 1536, 896)])
+def test_gemm_silu_mul_equals_unfused(ops, M, I, K):
+    """gate/up GEMM with SiLU*up in its epilogue == gemm() then
+    silu_mul(interleaved) byte for byte (unsplit 7B shape and the split-K
+    fallback of small shapes)."""
+    g = torch.Generator(device="cuda").manual_seed(M + I)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(2 * I, K, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    gu = torch.empty(M, 2 * I, dtype=torch.bfloat16, device="cuda")
+    ops.gemm(x, w, gu)
+    want = torch.empty(M, I, dtype=torch.bfloat16, device="cuda")
+    ops.silu_mul(gu, want, interleaved=True)
+    got = torch.empty_like(want)
+    ops.gemm_silu_mul(x, w, got)
+    assert torch.equal(got, want)
+    # the interleaved layout itself: features 64b..64b+63 use rows 128b.. (gate) and 128b+64.. (up)
+    gate = gu.view(M, I // 64, 2, 64)[:, :, 0].reshape(M, I).float()
+    up = gu.view(M, I // 64, 2, 64)[:, :, 1].reshape(M, I).float()
+    ref = (torch.nn.functional.silu(gate).to(torch.bfloat16).float() * up)
+    assert (ref - got.float()).abs().max().item() <= 0.02 * ref.abs().max().item() + 1e-3
+    _no_device_error(ops)
