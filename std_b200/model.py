@@ -149,7 +149,7 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
                    tok: torch.Tensor, tok_start: int, pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor,
                    slot_off: int, lens: torch.Tensor, len_offset: int, sparse: bool,
                    argmax_out: Optional[torch.Tensor], argmax_stride: int = 1, argmax_start: int = 0,
-                   dense_attn=None, sparse_index=None) -> None:
+                   dense_attn=None, sparse_index=None, collector=None) -> None:
     """One forward of n new tokens per request through all layers (graph-capturable).
 
     cache: [layers, 2, B, Hkv, cap, D].  sparse=True uses the draft kernel
@@ -163,6 +163,8 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     sparse_index = (dense cache, selection [layers, B, Hkv, n_idx] int32):
     the draft reads its prompt rows from the dense cache by position and
     `cache` holds only the generated tokens' draft-path K/V (the tail).
+    collector(li, q [B, n, Hq, D]) observes each layer's queries of a dense
+    forward (verification-guided re-selection).
     """
     c = model.config
     M = B * n
@@ -195,6 +197,8 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
         else:
             ops.verify_attention(ws.q[:M].view(B, n, Hq, D), kc, vc, lens, len_offset,
                                  out=ws.attn[:M].view(B, n, Hq, D))
+        if collector is not None and not sparse:
+            collector(li, ws.q[:M].view(B, n, Hq, D))
         ops.gemm_add_rmsnorm(ws.attn[:rows], lw.w_o, x, lw.w_post, c.rms_norm_eps, h)
         ops.gemm_silu_mul(h, lw.w_gu, ws.act[:rows])
         if li + 1 < n_layers:

@@ -36,6 +36,18 @@ SPARSE_ATTN_MODES = ("b200",)
 # (the reference's gather variant, :323-351) and only generated tokens get
 # sparse-path K/V rows.
 SPARSE_CACHE_MODES = ("compact", "indexed")
+# Visual selection across rounds (dynamic_selection.py:176-240): "static"
+# keeps S_0; "previous_verify_topk" sets S_{t+1} = TopK(A_t), A_t being round
+# t's dense-verification visual relevance (collector v1, :241-308).
+SELECTION_POLICIES = ("static", "previous_verify_topk")
+
+
+def topk_intersection_counts(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """|a ∩ b| over the last dim of two selections of unique, ascending
+    positions (dynamic_selection.py:85-101), on the selections' device."""
+    k = a.shape[-1]
+    pos = torch.searchsorted(b.contiguous(), a.contiguous()).clamp(max=k - 1)
+    return ((b.gather(-1, pos) == a)).sum(dim=-1)
 VERIFY_MODES = ("parallel", "sequential")
 
 
@@ -217,7 +229,8 @@ class STDRunner:
     def __init__(self, model: Qwen25VLDecoder, batch_size: int, layout: PromptLayout, max_new_tokens: int,
                  gamma: int = 9, k: int = 896, eos_token_id: int = -1, ignore_eos: bool = False,
                  use_graphs: bool = True, verify_mode: str = "parallel", shard=None,
-                 sparse_cache: str = "compact"):
+                 sparse_cache: str = "compact", selection_policy: str = "static",
+                 selection_update_interval: int = 1, min_selection_change_ratio: float = 0.0):
         c = model.config
         if gamma < 1 or 7 * (gamma + 1) > 126:
             raise ValueError("gamma must be in [1, 17]")
@@ -227,8 +240,17 @@ class STDRunner:
             raise ValueError(f"sparse_cache must be one of {SPARSE_CACHE_MODES}")
         if sparse_cache == "indexed" and shard is not None:
             raise ValueError("an indexed sparse cache reads the dense prompt rows, which a sharded owner does not hold")
+        if selection_policy not in SELECTION_POLICIES:
+            raise ValueError(f"selection_policy must be one of {SELECTION_POLICIES}")
+        if selection_policy != "static" and sparse_cache != "indexed":
+            raise ValueError("dynamic re-selection needs sparse_cache='indexed' (a selection change is an index update)")
+        if selection_update_interval < 1 or not 0.0 <= min_selection_change_ratio <= 1.0:
+            raise ValueError("selection_update_interval must be >= 1 and min_selection_change_ratio in [0, 1]")
         self.verify_mode = verify_mode
         self.sparse_cache = sparse_cache
+        self.dynamic = selection_policy == "previous_verify_topk"
+        self.update_interval = selection_update_interval
+        self.min_change = float(min_selection_change_ratio)
         self.model, self.B, self.layout = model, batch_size, layout
         self.gamma, self.k, self.max_new = gamma, k, max_new_tokens
         self.eos, self.ignore_eos, self.use_graphs = eos_token_id, ignore_eos, use_graphs
@@ -253,6 +275,9 @@ class STDRunner:
             self.sparse = allocate_kv_cache(model, batch_size, _round_up(max_new_tokens + gamma + 2, 64))
             self.sel_idx = torch.zeros(c.num_hidden_layers, batch_size, c.num_key_value_heads, self.compact_len,
                                        dtype=torch.int32, device=model.device)
+            sel_shape = (c.num_hidden_layers, batch_size, c.num_key_value_heads, k)
+            self.topk_init = torch.zeros(sel_shape, dtype=torch.int32, device=model.device)
+            self.topk_cur = torch.zeros_like(self.topk_init)
         else:
             self.sparse_shift = 0
             self.sparse = allocate_kv_cache(model, batch_size, self.cap_s)
@@ -283,6 +308,15 @@ class STDRunner:
         self.topk_per_request: List[torch.Tensor] = []
         self._graphs: Dict[str, torch.cuda.CUDAGraph] = {}
         self.prefill_done = False
+        if self.dynamic:
+            vp = layout.visual_pos
+            v0, nvis = int(vp[0].item()), int(vp.numel())
+            # relevance over prompt positions (only visual ones are ranked)
+            self.relevance = torch.zeros(c.num_hidden_layers, batch_size, c.num_key_value_heads, P,
+                                         dtype=torch.float32, device=dev)
+            self.vis_range = (v0, nvis) if int(vp[-1].item()) == v0 + nvis - 1 else None
+            self.sel_stats = torch.zeros(batch_size, 2, dtype=torch.float32, device=dev)  # updates, changed sum
+            self.update_flag = torch.zeros(batch_size, dtype=torch.bool, device=dev)
 
     @staticmethod
     def dense_capacity(prompt_len: int, max_new_tokens: int, gamma: int) -> int:
@@ -311,8 +345,9 @@ class STDRunner:
                 torch.cuda.synchronize()
                 t2 = time.time()
                 if self.sel_idx is not None:
-                    nv = self.layout.non_visual.view(1, 1, -1).expand(topk.shape[0], topk.shape[1], -1)
-                    self.sel_idx[:, b] = torch.cat([nv, topk], dim=-1).sort(dim=-1).values
+                    self.topk_init[:, b] = topk
+                    self.topk_cur[:, b] = topk
+                    self._rebuild_selection()
                 else:
                     compact_sparse_prompt_cache(full, self.sparse, b, self.layout, topk)
                 torch.cuda.synchronize()
@@ -346,6 +381,53 @@ class STDRunner:
         self.tok[:, 0] = self.dense_next   # AR: current token
         self.tok[:, 1] = self.dense_next   # STD: sparse_next = dense_next (copy_sparse_prefill)
         self.all_done.zero_()
+        if self.dynamic:  # every decode starts from the static selection S_0
+            self.topk_cur.copy_(self.topk_init)
+            self._rebuild_selection()
+            self.relevance.zero_()
+            self.sel_stats.zero_()
+
+    def _rebuild_selection(self) -> None:
+        """sel_idx = sorted(non_visual ∪ topk_cur) per (layer, request, KV head)."""
+        L, B, H, _ = self.topk_cur.shape
+        nv = self.layout.non_visual.view(1, 1, 1, -1).expand(L, B, H, -1)
+        self.sel_idx.copy_(torch.cat([nv, self.topk_cur], dim=-1).sort(dim=-1).values)
+
+    def _collect(self, li: int, q4: torch.Tensor) -> None:
+        """Collector v1 (dynamic_selection.py:290-308) for layer li of a verify
+        forward: A[b, h, v] = sum over the verify queries of softmax over the
+        visual keys of (group-mean query . k_v) / sqrt(D)."""
+        B, nq, Hq, D = q4.shape
+        Hkv = self.model.config.num_key_value_heads
+        qk = q4.view(B, nq, Hkv, Hq // Hkv, D).float().mean(dim=3).permute(0, 2, 1, 3).to(q4.dtype)
+        if self.vis_range is not None:
+            v0, nvis = self.vis_range
+            kv = self.dense[li, 0, :, :, v0:v0 + nvis]
+        else:
+            kv = self.dense[li, 0].index_select(2, self.layout.visual_pos.long())
+        logits = torch.matmul(qk, kv.transpose(-1, -2)).float() * (1.0 / math.sqrt(D))
+        rel = torch.softmax(logits, dim=-1).sum(dim=2)  # [B, Hkv, V]
+        if self.vis_range is not None:
+            self.relevance[li, :, :, v0:v0 + nvis] = rel
+        else:
+            self.relevance[li].index_copy_(2, self.layout.visual_pos.long(), rel)
+
+    def _update_selection(self) -> None:
+        """S_{t+1} = TopK(A_t) per (layer, request, KV head), applied to request
+        b when its selection changed by at least min_selection_change_ratio
+        (Jaccard distance averaged over layers and heads,
+        dynamic_selection.py:55-83)."""
+        L, B, H, k = self.topk_cur.shape
+        P = self.relevance.shape[-1]
+        new = ops.topk_select(self.relevance.view(L * B * H, P), self.layout.visual_pos, k).view(L, B, H, k)
+        inter = topk_intersection_counts(new, self.topk_cur).float()
+        jac = (inter / (2 * k - inter).clamp(min=1)).mean(dim=(0, 2))  # [B]
+        changed = 1.0 - jac
+        torch.ge(changed, self.min_change, out=self.update_flag)
+        self.topk_cur.copy_(torch.where(self.update_flag.view(1, B, 1, 1), new, self.topk_cur))
+        self._rebuild_selection()
+        self.sel_stats[:, 0] += self.update_flag.float()
+        self.sel_stats[:, 1] += changed
 
     # ------------------------------------------------------------------ steps
     def _sparse_index(self):
@@ -366,7 +448,7 @@ class STDRunner:
                        tok_start=1 - pending, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len,
                        slot_off=-sh, lens=self.dense_len, len_offset=nq - sh, sparse=False,
                        argmax_out=self.vpred.view(-1), argmax_stride=self.gamma + 1, argmax_start=0,
-                       dense_attn=self.shard)
+                       dense_attn=self.shard, collector=self._collect if self.dynamic else None)
 
     def _verify_sequential(self, pending: int) -> None:
         """verify_mode="sequential" (std_qwen25vl.py:504-528, :775-781, :885-893):
@@ -413,16 +495,18 @@ class STDRunner:
         else:
             self._verify(pending)
 
-    def _post(self, pending: int) -> None:
+    def _post(self, pending: int, update: bool = False) -> None:
         self._accept(pending)
+        if update:  # before the bonus append, which already uses S_{t+1}
+            self._update_selection()
         self._bonus_step()
         torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
 
-    def std_round(self, first: bool) -> None:
+    def std_round(self, first: bool, update: bool = False) -> None:
         pending = 0 if first else 1
         self._drafts()
         self._verify_phase(pending)
-        self._post(pending)
+        self._post(pending, update)
 
     def ar_step(self) -> None:
         from . import _lib
@@ -449,8 +533,11 @@ class STDRunner:
         if not self.use_graphs:
             return
         if self.shard is None:
-            steps = (("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False)),
-                     ("ar", self.ar_step))
+            steps = [("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False)),
+                     ("ar", self.ar_step)]
+            if self.dynamic:
+                steps += [("std_first_upd", lambda: self.std_round(True, True)),
+                          ("std_upd", lambda: self.std_round(False, True))]
         else:
             # collectives stay outside the graphs: the dense forwards (verify,
             # AR steps) run eagerly between captured local phases
@@ -486,13 +573,13 @@ class STDRunner:
         self.reset()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        self._round(True)
+        self._round(True, self._update_due(1))
         rounds = 1
         while not self._all_done():
             if rounds > self.max_new + 1:
                 raise RuntimeError("STD decode did not terminate")
-            self._round(False)
             rounds += 1
+            self._round(False, self._update_due(rounds))
         end.record()
         end.synchronize()
         return start.elapsed_time(end) / 1000.0
@@ -515,9 +602,14 @@ class STDRunner:
         end.synchronize()
         return start.elapsed_time(end) / 1000.0
 
-    def _round(self, first: bool) -> None:
+    def _update_due(self, round_id: int) -> bool:
+        """Selection updates run after rounds round_id % interval == 0 (one-based)."""
+        return self.dynamic and round_id % self.update_interval == 0
+
+    def _round(self, first: bool, update: bool = False) -> None:
         if self.shard is None:
-            self._replay_or_run("std_first" if first else "std", lambda: self.std_round(first))
+            name = ("std_first" if first else "std") + ("_upd" if update else "")
+            self._replay_or_run(name, lambda: self.std_round(first, update))
             return
         pending = 0 if first else 1
         self._replay_or_run("drafts", self._drafts)
@@ -534,6 +626,15 @@ class STDRunner:
     # ------------------------------------------------------------------ results
     def generated(self) -> torch.Tensor:
         return self.out_tokens[:, : int(self.n_gen.max().item())].to(torch.int64).cpu()
+
+    def selection_stats(self) -> Dict[str, object]:
+        """Dynamic re-selection bookkeeping of the last decode, per request."""
+        if not self.dynamic:
+            return {"policy": "static", "updates": [0] * self.B, "mean_changed_ratio": [0.0] * self.B}
+        st = self.sel_stats.cpu()
+        rounds = self.stats[:, 0].cpu().clamp(min=1).float()
+        return {"policy": "previous_verify_topk", "updates": st[:, 0].int().tolist(),
+                "mean_changed_ratio": (st[:, 1] / rounds).tolist()}
 
     def std_stats(self) -> Dict[str, object]:
         st = self.stats.cpu()
@@ -658,3 +759,65 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                                 visual_len=int(layout.visual_pos.numel()),
                                 text_len=max(1, layout.prompt_len - layout.text_start), k=k)
     return result, selection
+
+
+@torch.inference_mode()
+def dynamic_std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor], video_token_id: int,
+                                  eos_token_id: int, max_new_tokens: int = 256, gamma: int = 9,
+                                  target_k_plus_text: int = 1024, explicit_k: Optional[int] = None,
+                                  policy: str = "previous_verify_topk", profile_decode: bool = False,
+                                  profile_prefill: bool = False, sparse_attn_mode: str = "b200",
+                                  copy_sparse_prefill: bool = True, ignore_eos: bool = False,
+                                  collector_version: str = "v1", refresh_mode: str = "incremental",
+                                  selection_update_interval: int = 1, min_selection_change_ratio: float = 0.05,
+                                  bootstrap_mode: str = "attention", verify_fallback: str = "none",
+                                  runner: Optional[STDRunner] = None):
+    """Verification-guided STD (dynamic_std_qwen25vl.py:109-530): the static
+    prefill selection S_0, then after round t's verification S_{t+1} =
+    TopK(A_t) from collector v1.  With the index-based sparse cache a refresh
+    is an update of the position lists (both refresh_mode values), so the
+    selected K/V rows are never copied.  Returns (result, selection, stats).
+    Implemented: policy static / previous_verify_topk, collector_version
+    "v1", bootstrap_mode "attention"; other research knobs raise ValueError."""
+    if policy not in SELECTION_POLICIES:
+        raise ValueError(f"Unsupported policy={policy!r}; expected one of {SELECTION_POLICIES}.")
+    if collector_version != "v1":
+        raise ValueError("collector_version: this build implements 'v1' (RuntimeVerificationCollector).")
+    if refresh_mode not in ("full", "incremental"):
+        raise ValueError(f"Unsupported refresh_mode={refresh_mode!r}; expected 'full' or 'incremental'.")
+    if bootstrap_mode != "attention" or verify_fallback != "none":
+        raise ValueError("bootstrap_mode must be 'attention' and verify_fallback 'none' in the B200 path.")
+    if sparse_attn_mode not in SPARSE_ATTN_MODES or not copy_sparse_prefill:
+        raise ValueError("sparse_attn_mode must be 'b200' with copy_sparse_prefill=True.")
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ids, layout, embeds = _prepare(model, inputs, video_token_id)
+    k = selection_budget(layout.prompt_len, layout.text_start, int(layout.visual_pos.numel()), target_k_plus_text,
+                         explicit_k)
+    if runner is None:
+        runner = STDRunner(model, ids.shape[0], layout, max_new_tokens, gamma=gamma, k=k, eos_token_id=eos_token_id,
+                           ignore_eos=ignore_eos, sparse_cache="indexed", selection_policy=policy,
+                           selection_update_interval=selection_update_interval,
+                           min_selection_change_ratio=min_selection_change_ratio)
+    tp = runner.prefill(embeds, with_selection=True)
+    dec = runner.run_std()
+    torch.cuda.synchronize()
+    gen = runner.generated()
+    out = torch.cat([ids.cpu().long(), gen], dim=1) if ids.shape[0] == gen.shape[0] else gen
+    st = runner.std_stats()
+    acc = st["accept_lengths"][0]
+    result = GenerateResult(
+        output_ids=out, decoding_time=dec, inference_time=time.time() - t0, generate_len=int(runner.n_gen.sum().item()),
+        accepted_draft_tokens=int(sum(st["accepted"])), proposed_draft_tokens=int(sum(st["proposed"])),
+        mean_accept_length=(sum(acc) / len(acc)) if acc else 0.0, decode_rounds=int(max(st["rounds"])),
+        final_gamma=gamma, accept_lengths=acc, prefill_time=tp["prefill_time"], selection_time=tp["selection_time"],
+        sparse_cache_time=tp["sparse_cache_time"])
+    topk0 = runner.topk_cur[:, 0].cpu().long()
+    selection = SparseSelection(topk_positions=[topk0[l] for l in range(topk0.shape[0])],
+                                non_visual_positions=layout.non_visual.cpu().long(), prompt_len=layout.prompt_len,
+                                visual_len=int(layout.visual_pos.numel()),
+                                text_len=max(1, layout.prompt_len - layout.text_start), k=k)
+    stats = dict(runner.selection_stats(), collector_version="v1", refresh_mode=refresh_mode,
+                 selection_update_interval=selection_update_interval,
+                 min_selection_change_ratio=min_selection_change_ratio)
+    return result, selection, stats

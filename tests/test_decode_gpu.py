@@ -167,3 +167,50 @@ def test_indexed_sparse_cache_matches_compacted(B, gamma):
         assert res[("compact", k)][1] == res[("indexed", k)][1]
     assert torch.equal(res[("indexed", 150)][0], ar)
     assert sum(map(sum, res[("indexed", V)][1])) > 0   # full selection: long accepted prefixes exercised
+
+
+def test_dynamic_reselection_keeps_std_equal_to_ar():
+    """Verification-guided re-selection (previous_verify_topk, collector v1):
+    the draft's visual selection changes between rounds, the tokens still
+    equal AR, and the collector's relevance matches an fp32 restatement."""
+    from std_b200 import ops
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import STDRunner, _prepare, dynamic_std_generate_qwen25vl, selection_budget
+
+    model = Qwen25VLDecoder(TINY, seed=8)
+    B, V, T = 2, 600, 24
+    inp = _inputs(B, V, T, TINY.vocab_size, TINY.hidden_size, seed=77)
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    k = selection_budget(layout.prompt_len, layout.text_start, V, 120, None)
+    runner = STDRunner(model, B, layout, 32, gamma=5, k=k, ignore_eos=True, sparse_cache="indexed",
+                       selection_policy="previous_verify_topk", min_selection_change_ratio=0.0)
+    runner.prefill(embeds, with_selection=True)
+    runner.run_std()
+    std_tokens = runner.out_tokens.cpu().clone()
+    sel = runner.selection_stats()
+    assert min(sel["updates"]) >= 1
+    assert not torch.equal(runner.topk_cur, runner.topk_init)      # the selection moved
+    runner.run_ar()
+    assert torch.equal(std_tokens, runner.out_tokens.cpu())
+    assert ops.device_error() == 0
+
+    # collector v1 against an fp32 restatement for one layer
+    g = torch.Generator(device="cuda").manual_seed(3)
+    nq = 6
+    q4 = torch.randn(B, nq, TINY.num_attention_heads, TINY.head_dim, generator=g, device="cuda").to(torch.bfloat16)
+    runner._collect(1, q4)
+    Hkv = TINY.num_key_value_heads
+    qk = q4.float().view(B, nq, Hkv, 7, TINY.head_dim).mean(3).permute(0, 2, 1, 3)
+    kvis = runner.dense[1, 0][:, :, layout.visual_pos.long()].float()
+    ref = torch.softmax(qk @ kvis.transpose(-1, -2) / TINY.head_dim ** 0.5, dim=-1).sum(2)
+    got = runner.relevance[1][:, :, layout.visual_pos.long()]
+    assert (got - ref).abs().max().item() <= 0.02 * ref.max().item()
+    assert abs(got.sum().item() - B * Hkv * nq) < 1e-2 * B * Hkv * nq
+
+    res, selection, stats = dynamic_std_generate_qwen25vl(model, inp, VIDEO, -1, max_new_tokens=20, gamma=5,
+                                                          target_k_plus_text=120, ignore_eos=True,
+                                                          min_selection_change_ratio=0.0)
+    assert res.generate_len == B * 20 and stats["policy"] == "previous_verify_topk"
+    assert len(selection.topk_positions) == TINY.num_hidden_layers
+    with pytest.raises(ValueError):
+        STDRunner(model, B, layout, 8, gamma=5, k=k, selection_policy="previous_verify_topk")  # needs indexed

@@ -51,3 +51,17 @@ def test_initialize_past_key_values_defaults(monkeypatch):
     assert isinstance(pkv[0][0], KVCache)
     pkv, data_list, _ = initialize_past_key_values(m, batch_size=3, max_cache_len=16)
     assert data_list[0].shape[1] == 3 and data_list[0].shape[3] == 16
+
+
+def test_topk_intersection_counts_matches_sets():
+    from std_b200.std_qwen25vl import topk_intersection_counts
+
+    g = torch.Generator().manual_seed(0)
+    a = torch.stack([torch.randperm(300, generator=g)[:40].sort().values for _ in range(12)]).view(3, 4, 40)
+    b = torch.stack([torch.randperm(300, generator=g)[:40].sort().values for _ in range(12)]).view(3, 4, 40)
+    b[0, 0] = a[0, 0]                      # identical selections
+    got = topk_intersection_counts(a.to(torch.int32), b.to(torch.int32))
+    for i in range(3):
+        for j in range(4):
+            assert int(got[i, j]) == len(set(a[i, j].tolist()) & set(b[i, j].tolist()))
+    assert int(got[0, 0]) == 40
