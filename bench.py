@@ -286,13 +286,25 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     assert ops.device_error() == 0
 
     # ---- launches of our kernels in the timed region ----
+    # A forward: embed + first RMSNorm, then per layer QKV GEMM, RoPE/append
+    # epilogue (a GEMM on padded rows adds a split-K reduce), attention (+ the
+    # verify split merge), O GEMM, residual+norm epilogue, gate/up GEMM with
+    # SiLU, down GEMM, residual+norm epilogue; lm_head GEMM + argmax keys.
     Lyr = c.num_hidden_layers
-    fwd = 2 + 5 * Lyr           # embed, first rmsnorm; per layer rope_append, attention, 2 add_rmsnorm, silu_mul
-    head = 1                    # argmax (the final norm is fused into the last add_rmsnorm)
     g_ = w["gamma"]
-    # drafts, verify (+1 split-merge launch per layer), bonus, accept
-    per_round = g_ * fwd + (g_ - 1) * head + (fwd + Lyr + head) + (fwd + head) + 1
-    gpu_launches = a.steps * rounds_per_step * per_round
+    verify_merge = 1  # the verify kernel splits keys (and merges) whenever B*Hkv < 148 and cap >= 256
+
+    def forward_launches(dense: bool, padded: bool, head: bool) -> int:
+        per_layer = 8 + (1 if padded else 0) + (verify_merge if dense else 0)
+        return 2 + Lyr * per_layer + (2 if head else 0)
+
+    def round_launches(first: bool) -> int:
+        nq = g_ + (0 if first else 1)
+        verify = forward_launches(True, B * nq != runner.dense_rows, True)
+        drafts = (g_ - 1) * forward_launches(False, False, True) + forward_launches(False, False, False)
+        return drafts + verify + 1 + forward_launches(False, False, True)  # + accept, bonus step
+    per_step = round_launches(True) + (rounds_per_step - 1) * round_launches(False)
+    gpu_launches = a.steps * per_step
 
     # ---- e2e through the public API, host buffers ----
     e2e = None
