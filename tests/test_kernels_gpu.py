@@ -541,3 +541,49 @@ def test_gemm_silu_mul_equals_unfused(ops, M, I, K):
     ref = (torch.nn.functional.silu(gate).to(torch.bfloat16).float() * up)
     assert (ref - got.float()).abs().max().item() <= 0.02 * ref.abs().max().item() + 1e-3
     _no_device_error(ops)
+
+
+def test_configs3_sizes_verify_sharded_merge_and_draft(ops):
+    """configs[3] sizes: a 163,840-key preallocated cache holding 131,210 live
+    keys.  (1) verify (10 causal rows) vs fp32 math; (2) the same result from
+    two sequence shards (non-causal prefix shard + causal tail shard) merged
+    with std_merge_partials; (3) the draft over a 4,224-key sparse cache."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    cap, L, nq, S = 163840, 131210, 10, 65536
+    q = torch.randn(1, nq, 28, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(1, 4, cap, 128, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(1, 4, cap, 128, generator=g, device="cuda").to(torch.bfloat16)
+    lens = torch.tensor([L - nq], dtype=torch.int32, device="cuda")
+    out = ops.verify_attention(q, k, v, lens, nq)
+    qf = q.float()[0].permute(1, 0, 2)                          # [28, 10, 128]
+    ref = torch.empty(28, nq, 128, device="cuda")
+    for h in range(4):                                        # per KV group to bound memory
+        s = qf[7 * h:7 * h + 7] @ k[0, h, :L].float().t() / np.sqrt(128.0)   # [7, 10, L]
+        mask = torch.arange(L, device="cuda")[None, :] > (L - nq + torch.arange(nq, device="cuda"))[:, None]
+        s = s.masked_fill(mask[None], float("-inf"))
+        ref[7 * h:7 * h + 7] = torch.softmax(s, dim=-1) @ v[0, h, :L].float()
+    err = (out[0].float().permute(1, 0, 2) - ref).abs()
+    assert err.max().item() <= ATOL_MAX and err.mean().item() <= ATOL_MEAN
+    # two shards: keys [0, S) seen by every row, keys [S, L) causal at the tail
+    kp, vp = k[:, :, :S].contiguous(), v[:, :, :S].contiguous()
+    kt, vt = k[:, :, S:].contiguous(), v[:, :, S:].contiguous()
+    lse = torch.empty(2, nq, 28, dtype=torch.float32, device="cuda")
+    parts = torch.empty(2, 1, nq, 28, 128, dtype=torch.bfloat16, device="cuda")
+    ops.verify_attention(q, kp, vp, torch.tensor([S], dtype=torch.int32, device="cuda"), 0, causal=False,
+                         out=parts[0], lse=lse[0:1].view(1, nq, 28))
+    ops.verify_attention(q, kt, vt, torch.tensor([L - nq - S], dtype=torch.int32, device="cuda"), nq,
+                         out=parts[1], lse=lse[1:2].view(1, nq, 28))
+    merged = ops.merge_partials(parts.view(2, nq * 28, 128), lse.view(2, nq * 28))
+    err = (merged.view(nq, 28, 128).float().permute(1, 0, 2) - ref).abs()
+    assert err.max().item() <= ATOL_MAX and err.mean().item() <= ATOL_MEAN
+    # draft over the configs[3] sparse cache length
+    Ls = 4224
+    qd = torch.randn(1, 28, 128, generator=g, device="cuda").to(torch.bfloat16)
+    od = ops.draft_attention(qd, k[:, :, :4352].contiguous(), v[:, :, :4352].contiguous(),
+                             torch.tensor([Ls], dtype=torch.int32, device="cuda"), 0)
+    for h in range(4):
+        s = qd[0, 7 * h:7 * h + 7].float() @ k[0, h, :Ls].float().t() / np.sqrt(128.0)
+        r = torch.softmax(s, dim=-1) @ v[0, h, :Ls].float()
+        e = (od[0, 7 * h:7 * h + 7].float() - r).abs()
+        assert e.max().item() <= ATOL_MAX and e.mean().item() <= ATOL_MEAN
+    _no_device_error(ops)
