@@ -285,3 +285,18 @@ def test_decoder_matches_fp32_restatement():
         top2 = logits.topk(2).values
         if (top2[0] - top2[1]).item() > 0.05:      # skip near-ties, where bf16 may legitimately differ
             assert int(first[b]) == int(logits.argmax())
+
+
+def test_benchmark_cli_tiny(tmp_path):
+    """The per-sample AR vs STD CLI end to end on the tiny decoder."""
+    import json
+
+    from std_b200.benchmark_std import main
+
+    out = tmp_path / "m.jsonl"
+    assert main(["--config", "tiny", "--frame-num", "1", "--text-len", "16", "--max-new-tokens", "12",
+                 "--eval-num", "2", "--gamma", "4", "--target-k-plus-text", "96", "--ignore-eos",
+                 "--strict-equality", "--output", str(out)]) == 0
+    recs = [json.loads(l) for l in out.read_text().splitlines()]
+    assert len(recs) == 2 and all(r["token_equal"] and r["std_generate_len"] == 12 for r in recs)
+    assert recs[0]["prompt_len"] == 512 + 16 and recs[0]["k"] == 96 - 16

@@ -65,3 +65,20 @@ def test_topk_intersection_counts_matches_sets():
         for j in range(4):
             assert int(got[i, j]) == len(set(a[i, j].tolist()) & set(b[i, j].tolist()))
     assert int(got[0, 0]) == 40
+
+
+def test_benchmark_cli_flags():
+    """The reference CLI's decode flags parse; paths this build lacks are rejected."""
+    import pytest
+
+    from std_b200.benchmark_std import _agreement, _args
+
+    a = _args(["--gamma", "5", "--target-k-plus-text", "512", "--k", "100", "--verify-mode", "sequential",
+               "--ignore-eos", "--strict-equality", "--sparse-attn-mode", "b200"])
+    assert a.gamma == 5 and a.k == 100 and a.verify_mode == "sequential" and a.ignore_eos and a.strict_equality
+    for bad in (["--sparse-attn-mode", "triton_gqa"], ["--verify-fallback", "sequential_guard"],
+                ["--verify-attn-backend", "math"], ["--dataset", "Video-MME"]):
+        with pytest.raises(SystemExit):
+            _args(bad)
+    ag = _agreement(torch.tensor([1, 2, 3, 4]), torch.tensor([1, 2, 9, 4, 5]))
+    assert ag["common_prefix_length"] == 2 and abs(ag["token_level_agreement"] - (1 - 2 / 5)) < 1e-9
