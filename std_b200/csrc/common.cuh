@@ -55,6 +55,36 @@ STD_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
 }
+// Distributed shared memory: the shared::cluster address of the object at
+// shared::cta address `local` in cluster rank `rank`, and asynchronous stores
+// into it that complete transaction bytes on that rank's mbarrier (so the
+// receiver learns of their arrival by waiting on its own barrier).
+STD_DEV uint32_t mapa_rank(uint32_t local, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+STD_DEV void st_async_f32(uint32_t remote, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote),
+               "r"(__float_as_uint(v)), "r"(remote_bar)
+               : "memory");
+}
+STD_DEV void st_async_v2f32(uint32_t remote, float a, float b, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(remote),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(remote_bar)
+               : "memory");
+}
+STD_DEV void st_async_v4f32(uint32_t remote, float4 v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   remote),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w)), "r"(remote_bar)
+               : "memory");
+}
+STD_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+STD_DEV void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+STD_DEV void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
 STD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -275,6 +305,13 @@ STD_DEV void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& 
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr)
                : "memory");
+}
+// Transpose of an 8x8 b16 matrix held one 32-bit pair per lane (lane 4r+c
+// holds row r, columns 2c and 2c+1) into the same layout.
+STD_DEV uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
 }
 // c[16x8 fp32] += a[16x16 bf16, row-major] * b[16x16 -> 16x8 bf16, col-major]
 STD_DEV void mma_bf16_16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {

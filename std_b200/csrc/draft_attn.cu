@@ -10,25 +10,32 @@
 // is HBM-bound -- provided the math keeps up: at 6.5 TB/s the 7 query heads of
 // a KV group need ~45 TFLOP/s, more than fp32 CUDA cores sustain once the
 // conversions and reductions are counted.  So the two contractions run on the
-// tensor cores as warp-level m16n8k16 bf16 tiles (the 7 heads padded to the
-// 16-row tile), which leaves the kernel bound by the K/V stream alone.
+// tensor cores as warp-level m16n8k16 bf16 tiles, in transposed form so that
+// the 7 heads (plus one zero pad) are the N = 8 side of both tiles:
+// S^T = K Q^T puts 16 keys on M, and O^T += V^T P^T puts 16 dims on M, with P^T
+// moved from the accumulator layout to the operand layout by movmatrix.  A
+// 16-key unit then costs 8 + 8 MMAs and the output accumulator is 32 fp32
+// registers per thread (the untransposed form pads 7 heads to 16 rows: twice
+// the MMAs and registers).
 //
-//   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1), 4 warps/CTA.
+//   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1), 8 warps/CTA.
 //   CTA rank i owns keys [i*per, (i+1)*per) of the request's live length
 //   (per = ceil(L/8) rounded up to 16).  TMA (2-D tensor maps, 128-byte
 //   swizzle, 16-row boxes, no multicast) streams its K and V rows through a
 //   three-stage ring of 64-key sub-tiles; only the boxes that hold live keys are
-//   fetched.  Each warp takes 16 keys of every sub-tile: S = Q K^T from
-//   ldmatrix'd K fragments, an online softmax on the accumulator registers,
-//   then O += P V with P reused from registers as the A operand and V
-//   fragments from ldmatrix.trans.  Every K/V byte is read from HBM once (the
-//   Triton kernel re-reads each KV head for each of its 7 query heads).
-//   The 4 warp partials are combined in shared memory; each CTA then pushes
-//   its partial of output slice q into rank q's shared memory (DSMEM stores),
-//   one cluster barrier later every rank finishes its 112 of the 7 x 128
-//   outputs from local data -- one launch, no global scratch, no second
-//   kernel, one cluster barrier.  Lengths come from device memory, so the
-//   launch is graph-capturable while they change between replays.
+//   fetched.  The two warp groups take alternate sub-tiles (group g: sub-tiles
+//   g, g+2, ...) and each warp 16 keys of a sub-tile: S^T from ldmatrix'd K
+//   fragments and the q fragments held in registers, an online softmax on the
+//   accumulator registers, then O^T += V^T P^T with V^T from ldmatrix.trans.
+//   Every K/V byte is read from HBM once (the Triton kernel re-reads each KV
+//   head for each of its 7 query heads).  The 8 warp partials are combined in
+//   shared memory; each CTA then pushes its partial of output slice q into
+//   rank q's shared memory with st.async (asynchronous DSMEM stores that
+//   complete bytes on rank q's mbarrier), and every rank finishes its 112 of
+//   the 7 x 128 outputs from local data once its barrier completes -- one
+//   launch, no global scratch, no second kernel, and no cluster barrier after
+//   the pushes.  Lengths come from device memory, so the launch is
+//   graph-capturable while they change between replays.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -37,9 +44,9 @@ namespace stdb {
 
 constexpr int DR_D = 128;
 constexpr int DR_G = 7;
-constexpr int DR_WARPS = 4;
+constexpr int DR_WARPS = 8;    // two groups of 4, alternate sub-tiles
 constexpr int DR_THREADS = DR_WARPS * 32;
-constexpr int DR_SUB = 64;     // keys per pipeline stage, 16 per warp
+constexpr int DR_SUB = 64;     // keys per pipeline stage, 16 per warp of a group
 constexpr int DR_BOX = 16;     // rows per TMA box
 constexpr int DR_STAGES = 3;
 constexpr int DR_CLUSTER = 8;  // CTAs per (request, KV head)
@@ -48,8 +55,9 @@ constexpr uint32_t DR_STAGE_BYTES = 4 * DR_HALF_BYTES;             // K lo, K hi
 constexpr uint32_t DR_SMEM = DR_STAGES * DR_STAGE_BYTES + 1024;    // + alignment slack (swizzle atoms: 1 KB)
 constexpr int DR_OSTRIDE = DR_D + 4;                               // fp32 row of a warp partial (bank skew)
 constexpr int DR_OUT_PER_RANK = DR_G * DR_D / DR_CLUSTER;          // 112
-static_assert(DR_WARPS * 8 * DR_OSTRIDE * 4 + 2 * DR_WARPS * 8 * 4 <= DR_STAGES * DR_STAGE_BYTES,
+static_assert(DR_WARPS * 8 * DR_OSTRIDE * 4 + 3 * DR_WARPS * 8 * 4 + 16 * 4 <= DR_STAGES * DR_STAGE_BYTES,
               "warp partials alias the stage buffers");
+static_assert(DR_OUT_PER_RANK % 4 == 0 && DR_D % 4 == 0, "pushes are 4-output vectors of one rank and one head");
 
 struct DraftParams {
   const __nv_bfloat16* q;   // [B, Hq, D]
@@ -68,146 +76,199 @@ STD_DEV uint32_t dr_sw(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// Q of KV group kvh as the m16n8k16 A operand: row gid = query head kvh*7 +
-// gid (row 7 and rows 8..15 are zero padding), k-step ks covers dims
-// [16ks, 16ks+16).
-STD_DEV void draft_load_q(const DraftParams& p, int b, int kvh, int gid, int tig, uint32_t (&qa)[8][2]) {
+// Q^T of KV group kvh as the m16n8k16 B operand (k = dim, n = head): lane
+// (gid, tig) holds head kvh*7 + gid, dims 16ks + 2tig (+1) and 16ks + 8 + 2tig
+// (+1); head 7 of the tile is zero padding.
+STD_DEV void draft_load_q(const DraftParams& p, int b, int kvh, int gid, int tig, uint32_t (&qb)[8][2]) {
   const bool hv = gid < DR_G;
   const __nv_bfloat16* qrow = p.q + (static_cast<size_t>(b) * p.Hq + kvh * DR_G + (hv ? gid : 0)) * DR_D;
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks) {
-    qa[ks][0] = hv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * tig) : 0u;
-    qa[ks][1] = hv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * tig) : 0u;
+    qb[ks][0] = hv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 2 * tig) : 0u;
+    qb[ks][1] = hv ? *reinterpret_cast<const uint32_t*>(qrow + 16 * ks + 8 + 2 * tig) : 0u;
   }
 }
 
-// One warp's 16 keys (kw .. kw+15 of the sub-tile in sK / sV, nvalid of them
-// live) folded into its online softmax state (o, m_run, l_run of row gid).
-STD_DEV void draft_subtile(const uint8_t* sK, const uint8_t* sV, int kw, int nvalid, const uint32_t (&qa)[8][2],
-                           float sc, int lane, float (&o)[16][4], float& m_run, float& l_run) {
-  const int tig = lane & 3;
-  // S[16 x 16 keys] = Q K^T, even and odd k-steps in separate
-  // accumulators (four independent MMA chains instead of two)
-  float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  float s2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  const int mi = lane >> 3;
+// One warp's 16 keys (rows kw .. kw+15 of the sub-tile in sK / sV, nvalid of
+// them live) folded into its online softmax state.  Lane (gid, tig) keeps
+// heads 2tig and 2tig+1: m_run / l_run per head (l_run over this lane's keys
+// only; the lanes of a head are summed at the end) and o[mt] = O^T rows
+// (dims) 16mt + gid and 16mt + gid + 8 of those two heads.
+STD_DEV void draft_unit(const uint8_t* sK, const uint8_t* sV, int kw, int nvalid, const uint32_t (&qb)[8][2],
+                        float sc, int lane, float (&o)[8][4], float (&m_run)[2], float (&l_run)[2]) {
+  const int gid = lane >> 2, mi = lane >> 3;
+  // S^T[16 keys x 8 heads] = K Q^T; A = K rows (matrices: keys lo/hi x dims lo/hi)
+  uint32_t ka[8][4];
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks) {
-    const int key = kw + (mi >> 1) * 8 + (lane & 7);
-    const int ch = (ks & 3) * 2 + (mi & 1);
-    uint32_t b0, b1, b2, b3;
-    ldsm_x4(smem_u32(sK + (ks >> 2) * DR_HALF_BYTES + dr_sw(key, ch)), b0, b1, b2, b3);
-    float* d0 = (ks & 1) ? s2[0] : s[0];
-    float* d1 = (ks & 1) ? s2[1] : s[1];
-    mma_bf16_16816(d0, qa[ks][0], 0u, qa[ks][1], 0u, b0, b1);
-    mma_bf16_16816(d1, qa[ks][0], 0u, qa[ks][1], 0u, b2, b3);
-  }
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    s[0][e] += s2[0][e];
-    s[1][e] += s2[1][e];
-  }
-  // online softmax on row gid (keys 2tig, 2tig+1, 8+2tig, 9+2tig)
-  float x[4];
-  x[0] = (2 * tig < nvalid) ? s[0][0] * sc : -INFINITY;
-  x[1] = (2 * tig + 1 < nvalid) ? s[0][1] * sc : -INFINITY;
-  x[2] = (8 + 2 * tig < nvalid) ? s[1][0] * sc : -INFINITY;
-  x[3] = (9 + 2 * tig < nvalid) ? s[1][1] * sc : -INFINITY;
-  float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-  const float mn = fmaxf(m_run, mx);  // finite: key kw is live
-  const float alpha = ex2_approx(m_run - mn);
-  float pr[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) pr[e] = ex2_approx(x[e] - mn);
-  l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
-  m_run = mn;
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    o[j][0] *= alpha;
-    o[j][1] *= alpha;
-  }
-  const uint32_t pa0 = pack_bf16x2(pr[0], pr[1]), pa2 = pack_bf16x2(pr[2], pr[3]);
-  // O[16 x 128] += P[16 x 16 keys] V[16 keys x 128]
-#pragma unroll
-  for (int jj = 0; jj < 8; ++jj) {
     const int key = kw + (mi & 1) * 8 + (lane & 7);
-    const int ch = (2 * jj & 7) + (mi >> 1);
-    uint32_t v0, v1, v2, v3;
-    ldsm_x4_trans(smem_u32(sV + (jj >> 2) * DR_HALF_BYTES + dr_sw(key, ch)), v0, v1, v2, v3);
-    mma_bf16_16816(o[2 * jj], pa0, 0u, pa2, 0u, v0, v1);
-    mma_bf16_16816(o[2 * jj + 1], pa0, 0u, pa2, 0u, v2, v3);
+    const int c = 2 * ks + (mi >> 1);
+    ldsm_x4(smem_u32(sK + (c >> 3) * DR_HALF_BYTES + dr_sw(key, c & 7)), ka[ks][0], ka[ks][1], ka[ks][2],
+            ka[ks][3]);
   }
+  float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd k-steps: two MMA chains
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+    mma_bf16_16816((ks & 1) ? s2 : s, ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3], qb[ks][0], qb[ks][1]);
+  // V^T fragments (A operand of O^T += V^T P^T: dims x keys), loaded before
+  // the softmax so their latency overlaps it
+  uint32_t va[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int key = kw + (mi >> 1) * 8 + (lane & 7);
+    const int c = 2 * mt + (mi & 1);
+    ldsm_x4_trans(smem_u32(sV + (c >> 3) * DR_HALF_BYTES + dr_sw(key, c & 7)), va[mt][0], va[mt][1], va[mt][2],
+                  va[mt][3]);
+  }
+  // online softmax: x[0], x[1] = keys kw+gid, heads 2tig, 2tig+1; x[2], x[3] = key kw+gid+8
+  float x[4];
+  x[0] = gid < nvalid ? (s[0] + s2[0]) * sc : -INFINITY;
+  x[1] = gid < nvalid ? (s[1] + s2[1]) * sc : -INFINITY;
+  x[2] = gid + 8 < nvalid ? (s[2] + s2[2]) * sc : -INFINITY;
+  x[3] = gid + 8 < nvalid ? (s[3] + s2[3]) * sc : -INFINITY;
+  float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);  // finite: key kw is live
+  const float al0 = ex2_approx(m_run[0] - mn0), al1 = ex2_approx(m_run[1] - mn1);
+  const float p0 = ex2_approx(x[0] - mn0), p1 = ex2_approx(x[1] - mn1);
+  const float p2 = ex2_approx(x[2] - mn0), p3 = ex2_approx(x[3] - mn1);
+  l_run[0] = l_run[0] * al0 + (p0 + p2);
+  l_run[1] = l_run[1] * al1 + (p1 + p3);
+  m_run[0] = mn0;
+  m_run[1] = mn1;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    o[mt][0] *= al0;
+    o[mt][1] *= al1;
+    o[mt][2] *= al0;
+    o[mt][3] *= al1;
+  }
+  // P^T (k = key, n = head) as the B operand: transpose the accumulator-layout
+  // 8x8 blocks (keys lo, keys hi)
+  const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
+  const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) mma_bf16_16816(o[mt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb0, pb1);
 }
 
-// Combine the 4 warp partials of this CTA, push them to the ranks that finish
-// each output slice, and finish this rank's slice (one cluster barrier).
-STD_DEV void draft_finish(cooperative_groups::cluster_group& cluster, int rank, int b, int kvh, uint8_t* sbase,
-                          const DraftParams& p, float (&o)[16][4], float m_run, float l_run, bool ok,
-                          float (&r_o)[DR_CLUSTER][DR_OUT_PER_RANK], float (&r_m)[DR_CLUSTER][DR_G],
-                          float (&r_l)[DR_CLUSTER][DR_G]) {
+// What every rank of a cluster receives from the others: its output slice of
+// each rank's CTA partial, and (m, l) of the heads that slice covers.  The
+// senders write it with st.async, which completes transaction bytes on `bar`,
+// so the receiver learns of its arrival by waiting on its own barrier.
+struct DraftRecv {
+  float o[DR_CLUSTER][DR_OUT_PER_RANK];
+  float ml[DR_CLUSTER][DR_G][2];
+  uint64_t bar;
+};
+
+// heads whose 128 outputs overlap output slice q ([112 q, 112 q + 112))
+STD_DEV int draft_slice_head0(int q) { return (q * DR_OUT_PER_RANK) / DR_D; }
+STD_DEV int draft_slice_head1(int q) { return (q * DR_OUT_PER_RANK + DR_OUT_PER_RANK - 1) / DR_D; }
+
+// Thread 0, before the cluster's first barrier arrive: the receive barrier
+// expects one slice and its heads' (m, l) from each of the DR_CLUSTER ranks.
+STD_DEV void draft_recv_init(DraftRecv& rv, int rank) {
+  const int nh = draft_slice_head1(rank) - draft_slice_head0(rank) + 1;
+  mbar_init(&rv.bar, 1);
+  mbar_arrive_expect_tx(&rv.bar, static_cast<uint32_t>(DR_CLUSTER * (DR_OUT_PER_RANK * 4 + nh * 8)));
+}
+
+// Combine the 8 warp partials of this CTA, push them to the ranks that finish
+// each output slice (asynchronous DSMEM stores), and finish this rank's slice
+// once every rank's push has landed.
+STD_DEV void draft_finish(int rank, int b, int kvh, uint8_t* sbase, const DraftParams& p, float (&o)[8][4],
+                          float (&m_run)[2], float (&l_run)[2], bool ok, DraftRecv& rv) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   // warp partials -> shared memory (the stage buffers are free now)
-  float* wo = reinterpret_cast<float*>(sbase);  // [warp][8 rows][DR_OSTRIDE]
+  float* wo = reinterpret_cast<float*>(sbase);  // [warp][8 heads][DR_OSTRIDE]
   float* wm = wo + DR_WARPS * 8 * DR_OSTRIDE;   // [warp][8]
   float* wl = wm + DR_WARPS * 8;                // [warp][8]
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-  if (gid < DR_G) {
-    float* row = wo + (warp * 8 + gid) * DR_OSTRIDE;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) *reinterpret_cast<float2*>(row + 8 * j + 2 * tig) = make_float2(o[j][0], o[j][1]);
-    if (tig == 0) {
-      wm[warp * 8 + gid] = (l_run > 0.f && ok) ? m_run : -INFINITY;
-      wl[warp * 8 + gid] = ok ? l_run : 0.f;
+  for (int e = 0; e < 2; ++e) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) l_run[e] += __shfl_xor_sync(0xffffffffu, l_run[e], off);
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int h = 2 * tig + e;
+    if (h < DR_G) {
+      float* row = wo + (warp * 8 + h) * DR_OSTRIDE;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        row[16 * mt + gid] = o[mt][e];
+        row[16 * mt + gid + 8] = o[mt][2 + e];
+      }
+      if (gid == 0) {
+        wm[warp * 8 + h] = (l_run[e] > 0.f && ok) ? m_run[e] : -INFINITY;
+        wl[warp * 8 + h] = ok ? l_run[e] : 0.f;
+      }
     }
   }
   __syncthreads();
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-  // CTA partial: thread tid owns dim tid of all 7 heads
-#pragma unroll
-  for (int h = 0; h < DR_G; ++h) {
+  // per head: M = max over warps, the warps' weights exp2(m_w - M) and the
+  // weighted sum of their l
+  float* wt = wl + DR_WARPS * 8;  // [warp][8]
+  float* hm = wt + DR_WARPS * 8;  // [0, 8): M, [8, 16): l
+  if (tid < DR_G) {
+    const int h = tid;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < DR_WARPS; ++w) M = fmaxf(M, wm[w * 8 + h]);
-    float acc = 0.f, lsum = 0.f;
-    if (M != -INFINITY) {
+    float lsum = 0.f;
 #pragma unroll
-      for (int w = 0; w < DR_WARPS; ++w) {
-        const float mw = wm[w * 8 + h];
-        if (mw == -INFINITY) continue;
-        const float wt = ex2_approx(mw - M);
-        acc += wt * wo[(w * 8 + h) * DR_OSTRIDE + tid];
-        lsum += wt * wl[w * 8 + h];
-      }
+    for (int w = 0; w < DR_WARPS; ++w) {
+      const float x = M == -INFINITY ? 0.f : ex2_approx(wm[w * 8 + h] - M);  // 0 for a warp without keys
+      wt[w * 8 + h] = x;
+      lsum += x * wl[w * 8 + h];
     }
-    // push output h*128 + tid to the rank that finishes it (DSMEM store)
-    const int idx = h * DR_D + tid;
-    *cluster.map_shared_rank(&r_o[rank][idx % DR_OUT_PER_RANK], idx / DR_OUT_PER_RANK) = acc;
-    if (tid == 0) {
-      for (int q = (h * DR_D) / DR_OUT_PER_RANK; q <= (h * DR_D + DR_D - 1) / DR_OUT_PER_RANK; ++q) {
-        *cluster.map_shared_rank(&r_m[rank][h], q) = M;
-        *cluster.map_shared_rank(&r_l[rank][h], q) = lsum;
-      }
-    }
+    hm[h] = M;
+    hm[8 + h] = lsum;
   }
-  // One cluster barrier: every push has landed (release/acquire), and after it
-  // no CTA touches another's shared memory, so none has to wait for the
-  // others before exiting.
-  cluster.sync();
+  __syncthreads();
+  // every rank has initialised its receive barrier (it arrived after that)
+  cluster_wait_acquire();
+  const uint32_t bar_local = smem_u32(&rv.bar);
+  // CTA partial of outputs idx .. idx+3 (idx = 4 tid = h*128 + d), pushed as
+  // one vector to the rank that finishes them; (M, l) of head h to each rank
+  // whose slice covers part of h (at most two)
+  if (tid < DR_G * DR_D / 4) {
+    const int idx = 4 * tid, h = idx / DR_D, d = idx % DR_D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < DR_WARPS; ++w) {
+      const float x = wt[w * 8 + h];
+      const float4 v = *reinterpret_cast<const float4*>(wo + (w * 8 + h) * DR_OSTRIDE + d);
+      acc.x += x * v.x;
+      acc.y += x * v.y;
+      acc.z += x * v.z;
+      acc.w += x * v.w;
+    }
+    const int q = idx / DR_OUT_PER_RANK;
+    st_async_v4f32(mapa_rank(smem_u32(&rv.o[rank][idx % DR_OUT_PER_RANK]), q), acc, mapa_rank(bar_local, q));
+  } else if (tid < DR_G * DR_D / 4 + 2 * DR_G) {
+    const int h = (tid - DR_G * DR_D / 4) >> 1;
+    const int t = h * DR_D / DR_OUT_PER_RANK + ((tid - DR_G * DR_D / 4) & 1);
+    if (t <= (h * DR_D + DR_D - 1) / DR_OUT_PER_RANK)
+      st_async_v2f32(mapa_rank(smem_u32(&rv.ml[rank][h][0]), t), hm[h], hm[8 + h], mapa_rank(bar_local, t));
+  }
   // Rank r finishes outputs [112 r, 112 r + 112) of the group's 7 x 128 from
-  // the 8 partials in its own shared memory.
+  // the 8 partials in its own shared memory.  No rank exits before its own
+  // barrier completes, i.e. before every store into its memory has landed.
   if (tid < DR_OUT_PER_RANK) {
+    mbar_wait(&rv.bar, 0);
     const int idx = rank * DR_OUT_PER_RANK + tid;
     const int g = idx / DR_D, d = idx % DR_D;
     float mr[DR_CLUSTER], lr[DR_CLUSTER], orr[DR_CLUSTER];
 #pragma unroll
     for (int r = 0; r < DR_CLUSTER; ++r) {
-      mr[r] = r_m[r][g];
-      lr[r] = r_l[r][g];
-      orr[r] = r_o[r][tid];
+      mr[r] = rv.ml[r][g][0];
+      lr[r] = rv.ml[r][g][1];
+      orr[r] = rv.o[r][tid];
     }
     float m = -INFINITY;
 #pragma unroll
@@ -228,7 +289,8 @@ STD_DEV void draft_finish(cooperative_groups::cluster_group& cluster, int rank, 
 }
 
 __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS, 2)
-    draft_attn_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+    draft_attn_kernel(const __grid_constant__ CUtensorMap tk64, const __grid_constant__ CUtensorMap tv64,
+                      const __grid_constant__ CUtensorMap tk16, const __grid_constant__ CUtensorMap tv16,
                       const DraftParams p) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
@@ -236,10 +298,25 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  // Every CTA of the cluster must be running before another writes into its
-  // shared memory: arrive now, wait just before the first push (by then the
-  // wait returns at once).
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  extern __shared__ uint8_t dsmem_raw[];
+  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar[DR_STAGES];
+  __shared__ __align__(16) DraftRecv rv;
+  if (tid == 0) {
+    prefetch_tensormap(&tk64);
+    prefetch_tensormap(&tv64);
+    prefetch_tensormap(&tk16);
+    prefetch_tensormap(&tv16);
+#pragma unroll
+    for (int s = 0; s < DR_STAGES; ++s) mbar_init(&bar[s], 1);
+    draft_recv_init(rv, rank);
+    fence_barrier_init();
+  }
+  // Every CTA of the cluster must have initialised its receive barrier before
+  // another pushes into it: arrive now (relaxed: the init fence above orders
+  // the initialisation), wait just before the first push (by then the wait
+  // returns at once).
+  cluster_arrive_relaxed();
   // After an append (the decode step's RoPE + KV-append kernel, which writes
   // only q and the K/V row at position L-1): the lengths and every older K/V
   // row are read while that kernel may still run; q and row L-1 only after
@@ -249,14 +326,6 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     pdl_wait();
     pdl_launch_dependents();
   }
-
-  extern __shared__ uint8_t dsmem_raw[];
-  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bar[DR_STAGES];
-  // partials pushed here by every rank r of the cluster for the 112 outputs
-  // this CTA finishes (and, per head it covers, their m and l)
-  __shared__ __align__(16) float r_o[DR_CLUSTER][DR_OUT_PER_RANK];
-  __shared__ float r_m[DR_CLUSTER][DR_G], r_l[DR_CLUSTER][DR_G];
 
   int L = p.lens[b] + p.len_offset;
   if (L > p.cap || L < 0) {
@@ -277,93 +346,115 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     defer_j = ((L - 1 - k0) % DR_SUB) / DR_BOX;
   }
 
-  if (tid == 0) {
-    prefetch_tensormap(&tk);
-    prefetch_tensormap(&tv);
-#pragma unroll
-    for (int s = 0; s < DR_STAGES; ++s) mbar_init(&bar[s], 1);
-    fence_barrier_init();
-  }
-  __syncthreads();
-  // Sub-tile i is issued by the 32 lanes of warp 0 together: lane 4j+part
-  // copies box j (16 rows) of K lo/hi (part 0/1) or V lo/hi (part 2/3).
+  __syncthreads();  // the stage barriers are initialised
+  // Sub-tile i is issued by thread 0: a full sub-tile (64 live keys) as one
+  // 64-row box per K/V half, a partial one -- or the one holding the deferred
+  // row -- as 16-row boxes (both give the same shared-memory layout).  One
+  // thread with few large boxes: a copy instruction with per-lane coordinates
+  // issues its lanes one after another.
   // mode 0: the whole sub-tile; 1: all but the deferred box; 2: only that box
   auto issue = [&](int i, int mode) {
     const int st = i % DR_STAGES;
     const int a = i * DR_SUB;
-    const int nbox = (min(DR_SUB, nkeys - a) + DR_BOX - 1) / DR_BOX;
+    const int nk = min(DR_SUB, nkeys - a);
+    const int nbox = (nk + DR_BOX - 1) / DR_BOX;
     uint8_t* s = sbase + st * DR_STAGE_BYTES;
-    if (mode != 2) {
-      if (lane == 0) mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nbox) * 4u * DR_BOX * 128u);
-      __syncwarp();
+    if (mode != 2) mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nbox) * 4u * DR_BOX * 128u);
+    if (nk == DR_SUB && i != defer_i) {
+      if (mode != 2) {
+#pragma unroll
+        for (int part = 0; part < 4; ++part)
+          tma_load_2d(s + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES, part < 2 ? &tk64 : &tv64,
+                      &bar[st], (part & 1) * 64, row0 + a);
+      }
+      return;
     }
-    const int j = lane >> 2, part = lane & 3;
-    const bool is_deferred = i == defer_i && j == defer_j;
-    if (lane < 4 * nbox && (mode == 0 || (mode == 1) != is_deferred)) {
-      const uint32_t off = j * DR_BOX * 128 + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES;
-      tma_load_2d(s + off, part < 2 ? &tk : &tv, &bar[st], (part & 1) * 64, row0 + a + j * DR_BOX);
+    for (int j = 0; j < nbox; ++j) {
+      const bool is_deferred = i == defer_i && j == defer_j;
+      if (mode == 0 || (mode == 1) != is_deferred) {
+#pragma unroll
+        for (int part = 0; part < 4; ++part)
+          tma_load_2d(s + j * DR_BOX * 128 + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES,
+                      part < 2 ? &tk16 : &tv16, &bar[st], (part & 1) * 64, row0 + a + j * DR_BOX);
+      }
     }
   };
-  // sub-tiles issued so far: the same value in every thread (warp 0 issues),
-  // so the block-wide barriers below that depend on it are uniform
+  // sub-tiles issued so far: the same value in every thread (thread 0
+  // issues), so the block-wide barriers below that depend on it are uniform
   int issued = min(DR_STAGES, nsub);
-  if (warp == 0) {
+  int issued_real = issued;  // what thread 0 really issued (differs only after a wait gave up)
+  if (tid == 0) {
     for (int i = 0; i < issued; ++i) issue(i, early ? 1 : 0);
   }
   if (early) {
     pdl_wait();
     pdl_launch_dependents();
-    if (warp == 0 && defer_i >= 0 && defer_i < issued) issue(defer_i, 2);
+    if (tid == 0 && defer_i >= 0 && defer_i < issued) issue(defer_i, 2);
   }
 
-  uint32_t qa[8][2];
-  draft_load_q(p, b, kvh, gid, tig, qa);
+  uint32_t qb[8][2];
+  draft_load_q(p, b, kvh, gid, tig, qb);
 
-  float o[16][4];
+  float o[8][4];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;  // row gid of this warp, identical across the quad
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   bool ok = true;
   const float sc = p.scale_log2;
+  const int grp = warp >> 2, kw = (warp & 3) * 16;
 
-  for (int i = 0; i < nsub; ++i) {
-    const int st = i % DR_STAGES;
-    const int nk = min(DR_SUB, nkeys - i * DR_SUB);
-    if (ok) ok = mbar_wait(&bar[st], (i / DR_STAGES) & 1);
-    ok = __all_sync(0xffffffffu, ok);  // warp-uniform: guards warp-collective code below
-    uint8_t* sK = sbase + st * DR_STAGE_BYTES;
-    uint8_t* sV = sK + 2 * DR_HALF_BYTES;
-    const int kw = warp * 16;
-    const int nvalid = min(16, nk - kw);
-    if (nvalid > 0 && ok) {
-      if (nvalid < 16) {
-        // Rows past the live length inside the last box hold whatever the
-        // cache holds there; zero their V so that P = 0 times them stays 0.
-        for (int e = lane; e < (16 - nvalid) * 16; e += 32) {
-          const int r = kw + nvalid + (e >> 4), c = e & 15;
-          *reinterpret_cast<uint4*>(sV + (c >> 3) * DR_HALF_BYTES + r * 128 + ((c & 7) << 4)) =
-              make_uint4(0u, 0u, 0u, 0u);
+  // Iteration j: group 0 takes sub-tile 2j, group 1 sub-tile 2j+1; then the
+  // two stages they free are refilled with the next two sub-tiles.  A stage's
+  // previous phase was consumed in an earlier iteration, so a wait can never
+  // see the parity of a phase older than the one it waits for.
+  for (int i0 = 0; i0 < nsub; i0 += 2) {
+    const int i = i0 + grp;
+    if (i < nsub) {
+      const int st = i % DR_STAGES;
+      if (ok) ok = mbar_wait(&bar[st], (i / DR_STAGES) & 1);
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform: guards warp-collective code below
+      uint8_t* sK = sbase + st * DR_STAGE_BYTES;
+      uint8_t* sV = sK + 2 * DR_HALF_BYTES;
+      const int nvalid = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
+      if (nvalid > 0 && ok) {
+        if (nvalid < 16) {
+          // Rows past the live length inside the last box hold whatever the
+          // cache holds there; zero their V so that P = 0 times them stays 0.
+          for (int e = lane; e < (16 - nvalid) * 16; e += 32) {
+            const int r = kw + nvalid + (e >> 4), c = e & 15;
+            *reinterpret_cast<uint4*>(sV + (c >> 3) * DR_HALF_BYTES + r * 128 + ((c & 7) << 4)) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          fence_async_smem();
+          __syncwarp();
         }
-        fence_async_smem();
-        __syncwarp();
+        draft_unit(sK, sV, kw, nvalid, qb, sc, lane, o, m_run, l_run);
       }
-      draft_subtile(sK, sV, kw, nvalid, qa, sc, lane, o, m_run, l_run);
     }
     if (issued < nsub) {  // uniform: a refill follows
-      __syncthreads();    // every warp is done with stage st
-      if (warp == 0 && __all_sync(0xffffffffu, ok)) issue(issued, 0);
-      ++issued;
+      __syncthreads();    // both groups are done with their stages
+      if (warp == 0) {
+        const bool warp_ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0 && warp_ok) {
+          issue(issued, 0);
+          if (issued + 1 < nsub) issue(issued + 1, 0);
+          issued_real = min(nsub, issued + 2);
+        }
+      }
+      issued = min(nsub, issued + 2);
     }
   }
-  if (tid == 0) {
-    // Normally a no-op (every issued phase has completed).  If a wait gave up,
-    // let the loads still in flight land before the stage buffers are reused
-    // or the CTA exits; these waits are bounded too.
-    for (int i = max(0, issued - DR_STAGES); i < issued; ++i) mbar_wait(&bar[i % DR_STAGES], (i / DR_STAGES) & 1);
+  if (!__syncthreads_and(ok)) {
+    // A wait gave up: let the loads still in flight land before the stage
+    // buffers are reused or the CTA exits; these waits are bounded too.
+    if (tid == 0) {
+      for (int i = max(0, issued_real - DR_STAGES); i < issued_real; ++i)
+        mbar_wait(&bar[i % DR_STAGES], (i / DR_STAGES) & 1);
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
-  draft_finish(cluster, rank, b, kvh, sbase, p, o, m_run, l_run, ok, r_o, r_m, r_l);
+  draft_finish(rank, b, kvh, sbase, p, o, m_run, l_run, ok, rv);
 }
 // ---------------------------------------------------------------------------
 // Index-based sparse cache: the draft reads the selected prompt rows straight
@@ -406,14 +497,16 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-  pdl_wait();
-  pdl_launch_dependents();
-
   extern __shared__ uint8_t dsmem_raw[];
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(16) float r_o[DR_CLUSTER][DR_OUT_PER_RANK];
-  __shared__ float r_m[DR_CLUSTER][DR_G], r_l[DR_CLUSTER][DR_G];
+  __shared__ __align__(16) DraftRecv rv;
+  if (tid == 0) {
+    draft_recv_init(rv, rank);
+    fence_barrier_init();
+  }
+  cluster_arrive_relaxed();
+  pdl_wait();
+  pdl_launch_dependents();
 
   int L = p.lens[b] + p.len_offset;
   if (L > p.cap || L < 0) {
@@ -428,11 +521,12 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   const int nsub = (nkeys + DR_SUB - 1) / DR_SUB;
   const size_t head = static_cast<size_t>(b) * p.Hkv + kvh;
 
-  // thread t gathers half (t & 1) of row t >> 1 of a 64-row sub-tile, K and V
+  // thread t gathers chunks 4(t&3) .. 4(t&3)+3 (of the 16 per 256-byte row) of
+  // row t >> 2 of a 64-row sub-tile, K and V
   auto issue = [&](int i) {
     if (i >= nsub) return;
     const int st = i % DR_STAGES;
-    const int r = tid >> 1, hf = tid & 1;
+    const int r = tid >> 2, qd = tid & 3;
     const int rel = i * DR_SUB + r;
     const __nv_bfloat16* srcK = ix.dk;  // any valid address when zero-filling
     const __nv_bfloat16* srcV = ix.dv;
@@ -457,10 +551,11 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     uint8_t* sK = sbase + st * DR_STAGE_BYTES;
     uint8_t* sV = sK + 2 * DR_HALF_BYTES;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const uint32_t off = hf * DR_HALF_BYTES + dr_sw(r, c);
-      cp_async16(sK + off, srcK + hf * 64 + c * 8, nbytes);
-      cp_async16(sV + off, srcV + hf * 64 + c * 8, nbytes);
+    for (int e = 0; e < 4; ++e) {
+      const int c = 4 * qd + e;  // 16-byte chunk of the row: half c >> 3
+      const uint32_t off = (c >> 3) * DR_HALF_BYTES + dr_sw(r, c & 7);
+      cp_async16(sK + off, srcK + c * 8, nbytes);
+      cp_async16(sV + off, srcV + c * 8, nbytes);
     }
   };
 #pragma unroll
@@ -469,29 +564,38 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     cp_async_commit();
   }
 
-  uint32_t qa[8][2];
-  draft_load_q(p, b, kvh, gid, tig, qa);
-  float o[16][4];
+  uint32_t qb[8][2];
+  draft_load_q(p, b, kvh, gid, tig, qb);
+  float o[8][4];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const int grp = warp >> 2, kw = (warp & 3) * 16;
 
-  for (int i = 0; i < nsub; ++i) {
-    cp_async_wait<DR_STAGES - 1>();  // this thread's copies of sub-tile i have landed
-    __syncthreads();                 // ... and every other thread's
-    const int st = i % DR_STAGES;
-    const uint8_t* sK = sbase + st * DR_STAGE_BYTES;
-    const uint8_t* sV = sK + 2 * DR_HALF_BYTES;
-    const int kw = warp * 16;
-    const int nvalid = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
-    if (nvalid > 0) draft_subtile(sK, sV, kw, nvalid, qa, p.scale_log2, lane, o, m_run, l_run);
-    __syncthreads();  // stage st is free
-    issue(i + DR_STAGES);
+  // Iteration j: group 0 takes sub-tile 2j, group 1 sub-tile 2j+1 (the
+  // assignment of the TMA kernel, so both give the same bytes).  Groups of
+  // copies are committed one per sub-tile: before iteration j, sub-tiles up
+  // to 2j+2 are committed and 2j, 2j+1 must have landed.
+  for (int i0 = 0; i0 < nsub; i0 += 2) {
+    cp_async_wait<1>();  // this thread's copies of sub-tiles i0, i0+1 have landed
+    __syncthreads();     // ... and every other thread's
+    const int i = i0 + grp;
+    if (i < nsub) {
+      const int st = i % DR_STAGES;
+      const uint8_t* sK = sbase + st * DR_STAGE_BYTES;
+      const uint8_t* sV = sK + 2 * DR_HALF_BYTES;
+      const int nvalid = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
+      if (nvalid > 0) draft_unit(sK, sV, kw, nvalid, qb, p.scale_log2, lane, o, m_run, l_run);
+    }
+    __syncthreads();  // stages of i0, i0+1 are free
+    issue(i0 + DR_STAGES);
+    cp_async_commit();
+    issue(i0 + DR_STAGES + 1);
     cp_async_commit();
   }
   cp_async_wait<0>();  // nothing in flight into the stage buffers
   __syncthreads();
-  draft_finish(cluster, rank, b, kvh, sbase, p, o, m_run, l_run, true, r_o, r_m, r_l);
+  draft_finish(rank, b, kvh, sbase, p, o, m_run, l_run, true, rv);
 }
 
 }  // namespace stdb
@@ -528,9 +632,11 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
       return 3;
     attr_set = true;
   }
-  CUtensorMap tk, tv;
-  int rc = make_tmap_bf16_2d(&tk, k_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_BOX);
-  if (rc == 0) rc = make_tmap_bf16_2d(&tv, v_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_BOX);
+  CUtensorMap tk64, tv64, tk16, tv16;
+  int rc = make_tmap_bf16_2d(&tk64, k_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_SUB);
+  if (rc == 0) rc = make_tmap_bf16_2d(&tv64, v_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_SUB);
+  if (rc == 0) rc = make_tmap_bf16_2d(&tk16, k_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_BOX);
+  if (rc == 0) rc = make_tmap_bf16_2d(&tv16, v_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_BOX);
   if (rc != 0) return rc;
   stdb::DraftParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -545,7 +651,7 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   p.flags = flags & 1;
   dim3 grid(stdb::DR_CLUSTER, Hkv, B);
   return launch_pdl(stdb::draft_attn_kernel, grid, dim3(stdb::DR_THREADS), stdb::DR_SMEM,
-                    static_cast<cudaStream_t>(stream), tk, tv, p) == cudaSuccess
+                    static_cast<cudaStream_t>(stream), tk64, tv64, tk16, tv16, p) == cudaSuccess
              ? 0
              : 4;
 }
