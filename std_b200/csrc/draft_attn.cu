@@ -89,55 +89,94 @@ STD_DEV void draft_load_q(const DraftParams& p, int b, int kvh, int gid, int tig
   }
 }
 
-// One warp's 16 keys (rows kw .. kw+15 of the sub-tile in sK / sV, nvalid of
-// them live) folded into its online softmax state.  Lane (gid, tig) keeps
-// heads 2tig and 2tig+1: m_run / l_run per head (l_run over this lane's keys
-// only; the lanes of a head are summed at the end) and o[mt] = O^T rows
-// (dims) 16mt + gid and 16mt + gid + 8 of those two heads.
-STD_DEV void draft_unit(const uint8_t* sK, const uint8_t* sV, int kw, int nvalid, const uint32_t (&qb)[8][2],
-                        float sc, int lane, float (&o)[8][4], float (&m_run)[2], float (&l_run)[2]) {
+// NU (1 or 2) 16-key units of one warp -- rows kw .. kw+15 of the sub-tiles in
+// sK[u] / sV[u], nvalid[u] of them live -- folded into the warp's online
+// softmax state in one step (two units share one max, one rescale and
+// interleaved MMA chains, so a pair costs little more latency than one).  Lane
+// (gid, tig) keeps heads 2tig and 2tig+1: m_run / l_run per head (l_run over
+// this lane's keys only; the lanes of a head are summed at the end) and
+// o[mt] = O^T rows (dims) 16mt + gid and 16mt + gid + 8 of those two heads.
+template <int NU>
+STD_DEV void draft_units(const uint8_t* const (&sK)[NU], const uint8_t* const (&sV)[NU], const int (&nvalid)[NU],
+                         int kw, const uint32_t (&qb)[8][2], float sc, int lane, float (&o)[8][4], float (&m_run)[2],
+                         float (&l_run)[2]) {
+  constexpr int NCH = 4 / NU;  // independent MMA chains per unit for S
   const int gid = lane >> 2, mi = lane >> 3;
-  // S^T[16 keys x 8 heads] = K Q^T; A = K rows (matrices: keys lo/hi x dims lo/hi)
-  uint32_t ka[8][4];
+  // S^T[16 keys x 8 heads] = K Q^T per unit; A = K rows (matrices: keys lo/hi x dims lo/hi)
+  float s[NU][NCH][4];
 #pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    const int key = kw + (mi & 1) * 8 + (lane & 7);
-    const int c = 2 * ks + (mi >> 1);
-    ldsm_x4(smem_u32(sK + (c >> 3) * DR_HALF_BYTES + dr_sw(key, c & 7)), ka[ks][0], ka[ks][1], ka[ks][2],
-            ka[ks][3]);
+  for (int u = 0; u < NU; ++u)
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) s[u][c][0] = s[u][c][1] = s[u][c][2] = s[u][c][3] = 0.f;
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    uint32_t ka[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int key = kw + (mi & 1) * 8 + (lane & 7);
+      const int c = 2 * ks + (mi >> 1);
+      ldsm_x4(smem_u32(sK[u] + (c >> 3) * DR_HALF_BYTES + dr_sw(key, c & 7)), ka[ks][0], ka[ks][1], ka[ks][2],
+              ka[ks][3]);
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks)
+      mma_bf16_16816(s[u][ks % NCH], ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3], qb[ks][0], qb[ks][1]);
   }
-  float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd k-steps: two MMA chains
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks)
-    mma_bf16_16816((ks & 1) ? s2 : s, ka[ks][0], ka[ks][1], ka[ks][2], ka[ks][3], qb[ks][0], qb[ks][1]);
-  // V^T fragments (A operand of O^T += V^T P^T: dims x keys), loaded before
-  // the softmax so their latency overlaps it
+  // V^T fragments of unit 0 (A operand of O^T += V^T P^T: dims x keys), loaded
+  // before the softmax so their latency overlaps it
   uint32_t va[8][4];
+  auto load_v = [&](int u) {
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) {
-    const int key = kw + (mi >> 1) * 8 + (lane & 7);
-    const int c = 2 * mt + (mi & 1);
-    ldsm_x4_trans(smem_u32(sV + (c >> 3) * DR_HALF_BYTES + dr_sw(key, c & 7)), va[mt][0], va[mt][1], va[mt][2],
-                  va[mt][3]);
+    for (int mt = 0; mt < 8; ++mt) {
+      const int key = kw + (mi >> 1) * 8 + (lane & 7);
+      const int c = 2 * mt + (mi & 1);
+      ldsm_x4_trans(smem_u32(sV[u] + (c >> 3) * DR_HALF_BYTES + dr_sw(key, c & 7)), va[mt][0], va[mt][1],
+                    va[mt][2], va[mt][3]);
+    }
+  };
+  load_v(0);
+  // online softmax: x[u][0], x[u][1] = key kw+gid of unit u, heads 2tig, 2tig+1;
+  // x[u][2], x[u][3] = key kw+gid+8
+  float x[NU][4];
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    float t[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      t[e] = s[u][0][e];
+#pragma unroll
+      for (int c = 1; c < NCH; ++c) t[e] += s[u][c][e];
+    }
+    x[u][0] = gid < nvalid[u] ? t[0] * sc : -INFINITY;
+    x[u][1] = gid < nvalid[u] ? t[1] * sc : -INFINITY;
+    x[u][2] = gid + 8 < nvalid[u] ? t[2] * sc : -INFINITY;
+    x[u][3] = gid + 8 < nvalid[u] ? t[3] * sc : -INFINITY;
+    mx0 = fmaxf(mx0, fmaxf(x[u][0], x[u][2]));
+    mx1 = fmaxf(mx1, fmaxf(x[u][1], x[u][3]));
   }
-  // online softmax: x[0], x[1] = keys kw+gid, heads 2tig, 2tig+1; x[2], x[3] = key kw+gid+8
-  float x[4];
-  x[0] = gid < nvalid ? (s[0] + s2[0]) * sc : -INFINITY;
-  x[1] = gid < nvalid ? (s[1] + s2[1]) * sc : -INFINITY;
-  x[2] = gid + 8 < nvalid ? (s[2] + s2[2]) * sc : -INFINITY;
-  x[3] = gid + 8 < nvalid ? (s[3] + s2[3]) * sc : -INFINITY;
-  float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
 #pragma unroll
   for (int off = 4; off < 32; off <<= 1) {
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
   }
-  const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);  // finite: key kw is live
+  const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);  // finite: key kw of unit 0 is live
   const float al0 = ex2_approx(m_run[0] - mn0), al1 = ex2_approx(m_run[1] - mn1);
-  const float p0 = ex2_approx(x[0] - mn0), p1 = ex2_approx(x[1] - mn1);
-  const float p2 = ex2_approx(x[2] - mn0), p3 = ex2_approx(x[3] - mn1);
-  l_run[0] = l_run[0] * al0 + (p0 + p2);
-  l_run[1] = l_run[1] * al1 + (p1 + p3);
+  float ps0 = 0.f, ps1 = 0.f;
+  uint32_t pb[NU][2];
+#pragma unroll
+  for (int u = 0; u < NU; ++u) {
+    const float p0 = ex2_approx(x[u][0] - mn0), p1 = ex2_approx(x[u][1] - mn1);
+    const float p2 = ex2_approx(x[u][2] - mn0), p3 = ex2_approx(x[u][3] - mn1);
+    ps0 += p0 + p2;
+    ps1 += p1 + p3;
+    // P^T (k = key, n = head) as the B operand: transpose the
+    // accumulator-layout 8x8 blocks (keys lo, keys hi)
+    pb[u][0] = movmatrix_trans(pack_bf16x2(p0, p1));
+    pb[u][1] = movmatrix_trans(pack_bf16x2(p2, p3));
+  }
+  l_run[0] = l_run[0] * al0 + ps0;
+  l_run[1] = l_run[1] * al1 + ps1;
   m_run[0] = mn0;
   m_run[1] = mn1;
 #pragma unroll
@@ -147,13 +186,33 @@ STD_DEV void draft_unit(const uint8_t* sK, const uint8_t* sV, int kw, int nvalid
     o[mt][2] *= al0;
     o[mt][3] *= al1;
   }
-  // P^T (k = key, n = head) as the B operand: transpose the accumulator-layout
-  // 8x8 blocks (keys lo, keys hi)
-  const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
-  const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
+  // O^T += V^T P^T
 #pragma unroll
-  for (int mt = 0; mt < 8; ++mt) mma_bf16_16816(o[mt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb0, pb1);
+  for (int u = 0; u < NU; ++u) {
+    if (u > 0) load_v(u);
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+      mma_bf16_16816(o[mt], va[mt][0], va[mt][1], va[mt][2], va[mt][3], pb[u][0], pb[u][1]);
+  }
 }
+
+// Rows past the live length inside a sub-tile's last box hold whatever the
+// cache holds there: zero V rows kw+nvalid .. kw+15 so that P = 0 times them
+// stays 0.
+STD_DEV void draft_zero_tail_v(uint8_t* sV, int kw, int nvalid, int lane) {
+  for (int e = lane; e < (16 - nvalid) * 16; e += 32) {
+    const int r = kw + nvalid + (e >> 4), c = e & 15;
+    *reinterpret_cast<uint4*>(sV + (c >> 3) * DR_HALF_BYTES + r * 128 + ((c & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_async_smem();
+  __syncwarp();
+}
+
+// The units a warp of group grp folds in at loop step i0 (sub-tiles are taken
+// in pairs: group g takes i0 + g), except that an odd count of sub-tiles ends
+// with three, of which group 0 takes the first and the third together.
+// Returns the second sub-tile of that pair, or -1.
+STD_DEV int draft_pair_of(int nsub, int i0, int grp) { return (nsub - i0 == 3 && grp == 0) ? i0 + 2 : -1; }
 
 // What every rank of a cluster receives from the others: its output slice of
 // each rank's CTA partial, and (m, l) of the heads that slice covers.  The
@@ -302,6 +361,12 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bar[DR_STAGES];
   __shared__ __align__(16) DraftRecv rv;
+  // After an append (the decode step's RoPE + KV-append kernel, which writes
+  // only q and the K/V row at position L-1): the lengths and every older K/V
+  // row are read while that kernel may still run; q and row L-1 only after
+  // griddepcontrol.wait.  Otherwise nothing is read before the wait.
+  const bool early = (p.flags & 1) != 0;
+  int L = early ? p.lens[b] + p.len_offset : 0;
   if (tid == 0) {
     prefetch_tensormap(&tk64);
     prefetch_tensormap(&tv64);
@@ -317,17 +382,11 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   // the initialisation), wait just before the first push (by then the wait
   // returns at once).
   cluster_arrive_relaxed();
-  // After an append (the decode step's RoPE + KV-append kernel, which writes
-  // only q and the K/V row at position L-1): the lengths and every older K/V
-  // row are read while that kernel may still run; q and row L-1 only after
-  // griddepcontrol.wait.  Otherwise nothing is read before the wait.
-  const bool early = (p.flags & 1) != 0;
   if (!early) {
     pdl_wait();
     pdl_launch_dependents();
+    L = p.lens[b] + p.len_offset;
   }
-
-  int L = p.lens[b] + p.len_offset;
   if (L > p.cap || L < 0) {
     if (rank == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
     L = L < 0 ? 0 : p.cap;
@@ -405,34 +464,39 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
 
   // Iteration j: group 0 takes sub-tile 2j, group 1 sub-tile 2j+1; then the
   // two stages they free are refilled with the next two sub-tiles.  A stage's
-  // previous phase was consumed in an earlier iteration, so a wait can never
-  // see the parity of a phase older than the one it waits for.
+  // previous phase was consumed before the refill that reuses it, so a wait can
+  // never see the parity of a phase older than the one it waits for.  An odd
+  // count ends with three sub-tiles in one iteration (draft_pair_of).
   for (int i0 = 0; i0 < nsub; i0 += 2) {
     const int i = i0 + grp;
     if (i < nsub) {
-      const int st = i % DR_STAGES;
-      if (ok) ok = mbar_wait(&bar[st], (i / DR_STAGES) & 1);
+      const int ib = draft_pair_of(nsub, i0, grp);
+      if (ok) ok = mbar_wait(&bar[i % DR_STAGES], (i / DR_STAGES) & 1);
+      if (ok && ib >= 0) ok = mbar_wait(&bar[ib % DR_STAGES], (ib / DR_STAGES) & 1);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform: guards warp-collective code below
-      uint8_t* sK = sbase + st * DR_STAGE_BYTES;
-      uint8_t* sV = sK + 2 * DR_HALF_BYTES;
-      const int nvalid = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
-      if (nvalid > 0 && ok) {
-        if (nvalid < 16) {
-          // Rows past the live length inside the last box hold whatever the
-          // cache holds there; zero their V so that P = 0 times them stays 0.
-          for (int e = lane; e < (16 - nvalid) * 16; e += 32) {
-            const int r = kw + nvalid + (e >> 4), c = e & 15;
-            *reinterpret_cast<uint4*>(sV + (c >> 3) * DR_HALF_BYTES + r * 128 + ((c & 7) << 4)) =
-                make_uint4(0u, 0u, 0u, 0u);
-          }
-          fence_async_smem();
-          __syncwarp();
+      uint8_t* sK0 = sbase + (i % DR_STAGES) * DR_STAGE_BYTES;
+      const int nv0 = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
+      const int nv1 = ib >= 0 ? min(16, min(DR_SUB, nkeys - ib * DR_SUB) - kw) : 0;
+      if (nv0 > 0 && ok) {
+        if (nv0 < 16) draft_zero_tail_v(sK0 + 2 * DR_HALF_BYTES, kw, nv0, lane);
+        if (nv1 > 0) {
+          uint8_t* sK1 = sbase + (ib % DR_STAGES) * DR_STAGE_BYTES;
+          if (nv1 < 16) draft_zero_tail_v(sK1 + 2 * DR_HALF_BYTES, kw, nv1, lane);
+          const uint8_t* const k2[2] = {sK0, sK1};
+          const uint8_t* const v2[2] = {sK0 + 2 * DR_HALF_BYTES, sK1 + 2 * DR_HALF_BYTES};
+          const int n2[2] = {nv0, nv1};
+          draft_units<2>(k2, v2, n2, kw, qb, sc, lane, o, m_run, l_run);
+        } else {
+          const uint8_t* const k1[1] = {sK0};
+          const uint8_t* const v1[1] = {sK0 + 2 * DR_HALF_BYTES};
+          const int n1[1] = {nv0};
+          draft_units<1>(k1, v1, n1, kw, qb, sc, lane, o, m_run, l_run);
         }
-        draft_unit(sK, sV, kw, nvalid, qb, sc, lane, o, m_run, l_run);
       }
     }
-    if (issued < nsub) {  // uniform: a refill follows
-      __syncthreads();    // both groups are done with their stages
+    if (nsub - i0 == 3) break;  // uniform: the last three sub-tiles are consumed
+    if (issued < nsub) {        // uniform: a refill follows
+      __syncthreads();          // both groups are done with their stages
       if (warp == 0) {
         const bool warp_ok = __all_sync(0xffffffffu, ok);
         if (lane == 0 && warp_ok) {
@@ -577,16 +641,32 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   // copies are committed one per sub-tile: before iteration j, sub-tiles up
   // to 2j+2 are committed and 2j, 2j+1 must have landed.
   for (int i0 = 0; i0 < nsub; i0 += 2) {
-    cp_async_wait<1>();  // this thread's copies of sub-tiles i0, i0+1 have landed
-    __syncthreads();     // ... and every other thread's
+    const bool last3 = nsub - i0 == 3;  // uniform
+    if (last3)
+      cp_async_wait<0>();  // this thread's copies of sub-tiles i0 .. i0+2 have landed
+    else
+      cp_async_wait<1>();  // this thread's copies of sub-tiles i0, i0+1 have landed
+    __syncthreads();       // ... and every other thread's
     const int i = i0 + grp;
     if (i < nsub) {
-      const int st = i % DR_STAGES;
-      const uint8_t* sK = sbase + st * DR_STAGE_BYTES;
-      const uint8_t* sV = sK + 2 * DR_HALF_BYTES;
-      const int nvalid = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
-      if (nvalid > 0) draft_unit(sK, sV, kw, nvalid, qb, p.scale_log2, lane, o, m_run, l_run);
+      const int ib = draft_pair_of(nsub, i0, grp);
+      const uint8_t* sK0 = sbase + (i % DR_STAGES) * DR_STAGE_BYTES;
+      const int nv0 = min(16, min(DR_SUB, nkeys - i * DR_SUB) - kw);
+      const int nv1 = ib >= 0 ? min(16, min(DR_SUB, nkeys - ib * DR_SUB) - kw) : 0;
+      if (nv0 > 0 && nv1 > 0) {
+        const uint8_t* sK1 = sbase + (ib % DR_STAGES) * DR_STAGE_BYTES;
+        const uint8_t* const k2[2] = {sK0, sK1};
+        const uint8_t* const v2[2] = {sK0 + 2 * DR_HALF_BYTES, sK1 + 2 * DR_HALF_BYTES};
+        const int n2[2] = {nv0, nv1};
+        draft_units<2>(k2, v2, n2, kw, qb, p.scale_log2, lane, o, m_run, l_run);
+      } else if (nv0 > 0) {
+        const uint8_t* const k1[1] = {sK0};
+        const uint8_t* const v1[1] = {sK0 + 2 * DR_HALF_BYTES};
+        const int n1[1] = {nv0};
+        draft_units<1>(k1, v1, n1, kw, qb, p.scale_log2, lane, o, m_run, l_run);
+      }
     }
+    if (last3) break;
     __syncthreads();  // stages of i0, i0+1 are free
     issue(i0 + DR_STAGES);
     cp_async_commit();
