@@ -274,6 +274,13 @@ STD_DEV float ex2_approx(float x) {
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue (launch_dependents), and wait for the previous kernel's completion
 // and memory (wait; a no-op when the launch had no programmatic dependency).
+// The next kernel is scheduled once every CTA of this one has triggered (or
+// exited), so an early trigger never keeps this kernel's own CTAs from
+// starting.  A kernel triggers before its own wait only where each kernel
+// that can follow it reads nothing before its own wait but data no decode
+// kernel writes (the GEMMs prefetch weights there); kernels followed by a
+// reader of earlier results before its wait (RoPE + KV append before the
+// draft's early reads; the accept and AR bookkeeping) trigger after it.
 STD_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 STD_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

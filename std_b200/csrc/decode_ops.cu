@@ -26,8 +26,8 @@ namespace stdb {
 // out[b*n + j] = table[tok[b*tok_stride + tok_start + j]]
 __global__ void embed_kernel(const __nv_bfloat16* table, int vocab, int H, const int32_t* tok, int tok_stride,
                              int tok_start, int n, __nv_bfloat16* out) {
+  pdl_launch_dependents();  // followed by the first RMSNorm, which reads after its wait
   pdl_wait();
-  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int b = row / n, j = row % n;
   int id = tok[b * tok_stride + tok_start + j];
@@ -99,8 +99,8 @@ __global__ void __launch_bounds__(512) rmsnorm_kernel(__nv_bfloat16* __restrict_
                                                        const __nv_bfloat16* __restrict__ w, float eps, int H,
                                                        __nv_bfloat16* __restrict__ out) {
   __shared__ float s_part[32];
-  pdl_wait();
   pdl_launch_dependents();  // the following GEMM may start streaming its weights
+  pdl_wait();
   const size_t row = blockIdx.x;
   const int c = threadIdx.x * 8;
   const bool act = c < H;

@@ -446,8 +446,8 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     for (int i = 0; i < issued; ++i) issue(i, early ? 1 : 0);
   }
   if (early) {
+    pdl_launch_dependents();  // the decode step's O projection GEMM: weights before its wait
     pdl_wait();
-    pdl_launch_dependents();
     if (tid == 0 && defer_i >= 0 && defer_i < issued) issue(defer_i, 2);
   }
 

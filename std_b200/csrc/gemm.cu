@@ -87,6 +87,11 @@ __global__ void __launch_bounds__(GM_THREADS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
+  // Every kernel that follows a GEMM reads its inputs after its own wait (or,
+  // a GEMM, only weights before it): let it be scheduled now, so it is
+  // resident when this one completes.  After the TMEM allocation, so a
+  // successor can never hold columns this CTA still needs.
+  pdl_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
@@ -130,8 +135,7 @@ __global__ void __launch_bounds__(GM_THREADS)
 
   // ---- epilogue: thread = output feature, columns = tokens ----
   mbar_wait(&bar_done, 0);
-  pdl_wait();                 // every thread: the previous kernel is complete before any store
-  pdl_launch_dependents();    // the next kernel may start its prologue
+  pdl_wait();  // every thread: the previous kernel is complete before any store
   __syncwarp();
   tc_fence_after();
   const int f = n0 + warp * 32 + lane;
@@ -217,8 +221,8 @@ __global__ void __launch_bounds__(GM_THREADS)
 // y[t, f] = bf16( sum_s partial[s, t, f] + bias[f] ), splits in order
 __global__ void gemm_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N,
                                    const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y) {
+  pdl_launch_dependents();  // followed by RoPE + append or a norm: both read after their wait
   pdl_wait();
-  pdl_launch_dependents();
   const size_t total = static_cast<size_t>(M) * N / 4;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -290,8 +294,8 @@ struct GemmOut {
 // keys are cleared for the next call.
 __global__ void argmax_keys_kernel(unsigned long long* keys, int rows, int n, int out_stride, int out_start,
                                    int32_t* out) {
+  pdl_launch_dependents();  // followed by the embedding, the accept or the AR bookkeeping: read after their wait
   pdl_wait();
-  pdl_launch_dependents();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= rows) return;
   const unsigned long long k = keys[t];

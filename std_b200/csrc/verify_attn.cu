@@ -370,8 +370,8 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
 // One thread per (row, 4 dims); requests whose keys fit one split are skipped
 // (the split kernel wrote them).
 __global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p) {
+  pdl_launch_dependents();  // followed by the O projection GEMM (weights before its wait)
   pdl_wait();
-  pdl_launch_dependents();
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int L = verify_len(p, b);
   const int n_splits = (L + p.split_keys - 1) / p.split_keys;
