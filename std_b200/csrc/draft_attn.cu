@@ -418,13 +418,14 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     const int nk = min(DR_SUB, nkeys - a);
     const int nbox = (nk + DR_BOX - 1) / DR_BOX;
     uint8_t* s = sbase + st * DR_STAGE_BYTES;
+    const uint64_t pol = l2_policy_evict_first();  // each K/V row is read once per forward
     if (mode != 2) mbar_arrive_expect_tx(&bar[st], static_cast<uint32_t>(nbox) * 4u * DR_BOX * 128u);
     if (nk == DR_SUB && i != defer_i) {
       if (mode != 2) {
 #pragma unroll
         for (int part = 0; part < 4; ++part)
-          tma_load_2d(s + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES, part < 2 ? &tk64 : &tv64,
-                      &bar[st], (part & 1) * 64, row0 + a);
+          tma_load_2d_hint(s + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES,
+                           part < 2 ? &tk64 : &tv64, &bar[st], (part & 1) * 64, row0 + a, pol);
       }
       return;
     }
@@ -433,8 +434,8 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
       if (mode == 0 || (mode == 1) != is_deferred) {
 #pragma unroll
         for (int part = 0; part < 4; ++part)
-          tma_load_2d(s + j * DR_BOX * 128 + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES,
-                      part < 2 ? &tk16 : &tv16, &bar[st], (part & 1) * 64, row0 + a + j * DR_BOX);
+          tma_load_2d_hint(s + j * DR_BOX * 128 + (part & 1) * DR_HALF_BYTES + (part >> 1) * 2 * DR_HALF_BYTES,
+                           part < 2 ? &tk16 : &tv16, &bar[st], (part & 1) * 64, row0 + a + j * DR_BOX, pol);
       }
     }
   };

@@ -98,10 +98,11 @@ __global__ void __launch_bounds__(GM_THREADS)
     // The weights do not depend on the previous kernel: the first stages'
     // weight tiles are requested before waiting for it (programmatic
     // dependent launch), the token tiles only after.
+    const uint64_t stream_policy = l2_policy_evict_first();  // each weight byte is read once per step
     const int pre = nkb < S ? nkb : S;
     for (int i = 0; i < pre; ++i) {
       mbar_arrive_expect_tx(&bar_full[i], GM_WTILE + xtile);
-      tma_load_2d(sW + i * GM_WTILE, &tmW, &bar_full[i], (kb0 + i) * GM_BK, n0);
+      tma_load_2d_hint(sW + i * GM_WTILE, &tmW, &bar_full[i], (kb0 + i) * GM_BK, n0, stream_policy);
     }
     pdl_wait();
     for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * xtile, &tmX, &bar_full[i], (kb0 + i) * GM_BK, 0);
@@ -111,7 +112,7 @@ __global__ void __launch_bounds__(GM_THREADS)
       if (!mbar_wait(&bar_empty[st], ((i / S) - 1) & 1)) break;
       mbar_arrive_expect_tx(&bar_full[st], GM_WTILE + xtile);
       const int kx = (kb0 + i) * GM_BK;
-      tma_load_2d(sW + st * GM_WTILE, &tmW, &bar_full[st], kx, n0);
+      tma_load_2d_hint(sW + st * GM_WTILE, &tmW, &bar_full[st], kx, n0, stream_policy);
       tma_load_2d(sX + st * xtile, &tmX, &bar_full[st], kx, 0);
       issued = i + 1;
     }

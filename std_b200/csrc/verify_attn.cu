@@ -142,6 +142,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();  // each K/V row is read once per forward
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
         const int st = c % VF_STAGES;
@@ -150,10 +151,10 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         const int y = row0 + k0 + c * VF_CHUNK;
         uint8_t* kd = sK + st * VF_KV;
         uint8_t* vd = sV + st * VF_KV;
-        tma_load_2d(kd, &tmK, &bar_kv_full[st], 0, y);
-        tma_load_2d(kd + VF_KV / 2, &tmK, &bar_kv_full[st], 64, y);
-        tma_load_2d(vd, &tmV, &bar_kv_full[st], 0, y);
-        tma_load_2d(vd + VF_KV / 2, &tmV, &bar_kv_full[st], 64, y);
+        tma_load_2d_hint(kd, &tmK, &bar_kv_full[st], 0, y, pol);
+        tma_load_2d_hint(kd + VF_KV / 2, &tmK, &bar_kv_full[st], 64, y, pol);
+        tma_load_2d_hint(vd, &tmV, &bar_kv_full[st], 0, y, pol);
+        tma_load_2d_hint(vd + VF_KV / 2, &tmV, &bar_kv_full[st], 64, y, pol);
         issued = c + 1;
       }
       // never leave a copy in flight: wait for the last load of each stage
