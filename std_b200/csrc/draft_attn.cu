@@ -50,6 +50,10 @@ constexpr int DR_SUB = 64;     // keys per pipeline stage, 16 per warp of a grou
 constexpr int DR_BOX = 16;     // rows per TMA box
 constexpr int DR_STAGES = 3;
 constexpr int DR_CLUSTER = 8;  // CTAs per (request, KV head)
+// The thread that issues every K/V copy: lane 0 of the last warp, which never
+// takes the extra unit of an odd sub-tile count (group 0's first warp does),
+// so that the busiest warp is not held back loading q while copies are issued.
+constexpr int DR_ISSUER = (DR_WARPS - 1) * 32;
 constexpr uint32_t DR_HALF_BYTES = DR_SUB * 64 * 2;                // 64 keys x 64 dims (one 128-B swizzle span)
 constexpr uint32_t DR_STAGE_BYTES = 4 * DR_HALF_BYTES;             // K lo, K hi, V lo, V hi
 constexpr uint32_t DR_SMEM = DR_STAGES * DR_STAGE_BYTES + 1024;    // + alignment slack (swizzle atoms: 1 KB)
@@ -406,7 +410,7 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   }
 
   __syncthreads();  // the stage barriers are initialised
-  // Sub-tile i is issued by thread 0: a full sub-tile (64 live keys) as one
+  // Sub-tile i is issued by thread DR_ISSUER: a full sub-tile (64 live keys) as one
   // 64-row box per K/V half, a partial one -- or the one holding the deferred
   // row -- as 16-row boxes (both give the same shared-memory layout).  One
   // thread with few large boxes: a copy instruction with per-lane coordinates
@@ -439,17 +443,17 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
       }
     }
   };
-  // sub-tiles issued so far: the same value in every thread (thread 0
+  // sub-tiles issued so far: the same value in every thread (the issuer
   // issues), so the block-wide barriers below that depend on it are uniform
   int issued = min(DR_STAGES, nsub);
-  int issued_real = issued;  // what thread 0 really issued (differs only after a wait gave up)
-  if (tid == 0) {
+  int issued_real = issued;  // what the issuer really issued (differs only after a wait gave up)
+  if (tid == DR_ISSUER) {
     for (int i = 0; i < issued; ++i) issue(i, early ? 1 : 0);
   }
   if (early) {
     pdl_launch_dependents();  // the decode step's O projection GEMM: weights before its wait
     pdl_wait();
-    if (tid == 0 && defer_i >= 0 && defer_i < issued) issue(defer_i, 2);
+    if (tid == DR_ISSUER && defer_i >= 0 && defer_i < issued) issue(defer_i, 2);
   }
 
   uint32_t qb[8][2];
@@ -498,7 +502,7 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     if (nsub - i0 == 3) break;  // uniform: the last three sub-tiles are consumed
     if (issued < nsub) {        // uniform: a refill follows
       __syncthreads();          // both groups are done with their stages
-      if (warp == 0) {
+      if (warp == DR_ISSUER / 32) {
         const bool warp_ok = __all_sync(0xffffffffu, ok);
         if (lane == 0 && warp_ok) {
           issue(issued, 0);
@@ -512,7 +516,7 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
   if (!__syncthreads_and(ok)) {
     // A wait gave up: let the loads still in flight land before the stage
     // buffers are reused or the CTA exits; these waits are bounded too.
-    if (tid == 0) {
+    if (tid == DR_ISSUER) {
       for (int i = max(0, issued_real - DR_STAGES); i < issued_real; ++i)
         mbar_wait(&bar[i % DR_STAGES], (i / DR_STAGES) & 1);
     }

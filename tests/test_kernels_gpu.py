@@ -60,6 +60,28 @@ def test_draft_attention_vs_oracle(ops, B, lens, cap):
     _no_device_error(ops)
 
 
+def test_draft_attention_length_sweep(ops):
+    """Live lengths that give every CTA of the cluster 1..5 sub-tiles of 64 keys
+    (odd counts end with two sub-tiles folded in one step), partial last boxes,
+    empty ranks, and the newest row inside a full sub-tile (loaded as 16-row
+    boxes in after-append mode): both launch modes against the oracle."""
+    lens = [1, 15, 17, 64, 65, 127, 129, 511, 512, 513, 1023, 1024, 1025, 1097, 1536, 1537, 2047, 2560, 2561]
+    B, cap = len(lens), 2624
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(B, 28, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, 4, cap, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, 4, cap, 128, generator=g).to(torch.bfloat16)
+    lens_t = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    ref, ref_lse = oracle.draft_attention(q.float().numpy(), k.float().numpy(), v.float().numpy(), lens)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    for early in (False, True):
+        lse = torch.empty(B, 28, dtype=torch.float32, device="cuda")
+        out = ops.draft_attention(qd, kd, vd, lens_t, 0, lse=lse, after_append=early)
+        _check_attn(out.float().cpu().numpy(), ref, f"draft sweep (after_append={early})")
+        assert np.abs(lse.cpu().numpy() - ref_lse).max() < 1e-3
+    _no_device_error(ops)
+
+
 def test_draft_attention_len_offset(ops):
     g = torch.Generator().manual_seed(2)
     q = torch.randn(2, 28, 128, generator=g).to(torch.bfloat16).cuda()
