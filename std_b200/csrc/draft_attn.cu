@@ -21,10 +21,12 @@
 //   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1), 8 warps/CTA.
 //   CTA rank i owns keys [i*per, (i+1)*per) of the request's live length
 //   (per = ceil(L/8) rounded up to 16).  TMA (2-D tensor maps, 128-byte
-//   swizzle, 16-row boxes, no multicast) streams its K and V rows through a
-//   three-stage ring of 64-key sub-tiles; only the boxes that hold live keys are
-//   fetched.  The two warp groups take alternate sub-tiles (group g: sub-tiles
-//   g, g+2, ...) and each warp 16 keys of a sub-tile: S^T from ldmatrix'd K
+//   swizzle, no multicast; 64-row boxes for a full sub-tile, 16-row boxes for
+//   a partial one) streams its K and V rows through a three-stage ring of
+//   64-key sub-tiles; only rows of boxes that hold live keys are fetched.  The
+//   two warp groups take alternate sub-tiles (group g: sub-tiles g, g+2, ...;
+//   an odd count ends with group 0 folding two in one step) and each warp 16
+//   keys of a sub-tile: S^T from ldmatrix'd K
 //   fragments and the q fragments held in registers, an online softmax on the
 //   accumulator registers, then O^T += V^T P^T with V^T from ldmatrix.trans.
 //   Every K/V byte is read from HBM once (the Triton kernel re-reads each KV
