@@ -41,6 +41,12 @@ VIDEO_TOKEN_ID = 151656
 # `python -m std_b200.kernel_bench --kernel verify --B 8 --L 32906`.  Used only
 # when the bench runs exactly that shape.
 VERIFY_TRAFFIC = {(8, 32906, 10): 550.2e6}
+# sm__pipe_tensor_cycles_active (fraction of peak sustained) of the same capture
+VERIFY_TENSOR_ACTIVE = {(8, 32906, 10): 0.27}
+# DRAM read+write bytes of one sparse forward's GEMM launches at M = 8 (the
+# five shapes' per-launch ncu figures x their launches per forward); None
+# until captured for the current kernels.
+GEMM_TRAFFIC = {8: None}
 
 WORKLOADS = {
     "config4": dict(batch=8, visual=32768, text=128, k_plus_text=1024, gamma=9, max_new=128,
@@ -128,6 +134,41 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ----------------------------------------------------------------------------- ranks
+class RankSync:
+    """Barrier and whole-job reductions over the ranks of one bench run.
+
+    Every rank calls the same methods in the same order.  `dist` is None for a
+    single process; otherwise an initialised torch.distributed module whose
+    backend reduces tensors on `device` (NCCL: the rank's GPU; gloo: cpu)."""
+
+    def __init__(self, dist=None, device="cpu", device_ids=None):
+        self.dist, self.device, self.device_ids = dist, device, device_ids
+
+    def barrier(self) -> None:
+        if self.dist is None:
+            return
+        if self.device_ids is not None:
+            self.dist.barrier(device_ids=self.device_ids)
+        else:
+            self.dist.barrier()
+
+    def reduce(self, x: float, op: str) -> float:
+        if self.dist is None:
+            return float(x)
+        import torch
+
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX if op == "max" else self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def throughput(self, seconds_local: float, tokens_local: float):
+        """(tokens summed over ranks, seconds = max over ranks, tokens / seconds)."""
+        t_max = self.reduce(seconds_local, "max")
+        tokens = self.reduce(tokens_local, "sum")
+        return tokens, t_max, tokens / t_max
+
+
 # ----------------------------------------------------------------------------- reference arm
 def reference_arm(a, w, rank: int, world: int) -> None:
     if rank != 0:
@@ -152,6 +193,87 @@ def reference_arm(a, w, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- roofline helpers
+def gemm_shapes(c):
+    """(name, N, K, launches per sparse forward) of the decode GEMMs."""
+    H, I = c.hidden_size, c.intermediate_size
+    Lyr = c.num_hidden_layers
+    return [("qkv", c.qkv_size, H, Lyr), ("o", H, H, Lyr), ("gate_up", 2 * I, H, Lyr), ("down", H, I, Lyr),
+            ("lm_head", c.vocab_size, H, 1)]
+
+
+def gemm_roofline(runner, model, M: int, hbm_peak: float):
+    """Graph-time each decode GEMM as the sparse forward launches it (with its
+    fused epilogue), M token rows, cycling through the layers' weights."""
+    import torch
+
+    from std_b200 import ops
+    from std_b200.timing import graph_time_us
+
+    c = model.config
+    dev = model.device
+    Hq, Hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+    bf = torch.bfloat16
+    h = (torch.randn(M, c.hidden_size, device=dev) * 0.5).to(bf)
+    x = torch.zeros(M, c.hidden_size, device=dev, dtype=bf)
+    attn = (torch.randn(M, c.hidden_size, device=dev) * 0.5).to(bf)
+    act = (torch.randn(M, c.intermediate_size, device=dev) * 0.5).to(bf)
+    q = torch.empty(M, Hq, D, device=dev, dtype=bf)
+    kc = torch.zeros(M, Hkv, 64, D, device=dev, dtype=bf)
+    vc = torch.zeros_like(kc)
+    zero = torch.zeros(M, dtype=torch.int32, device=dev)
+    tok = torch.zeros(M, dtype=torch.int32, device=dev)
+    cos_t, sin_t = model.cos_t, model.sin_t
+    eps = c.rms_norm_eps
+    calls = {
+        "qkv": lambda lw: ops.gemm_rope_append(h, lw.w_qkv, lw.b_qkv, M, 1, Hq, Hkv, D, zero, 0, zero, 0, cos_t, sin_t,
+                                               q, kc, vc),
+        "o": lambda lw: ops.gemm_add_rmsnorm(attn, lw.w_o, x, lw.w_post, eps, h),
+        "gate_up": lambda lw: ops.gemm_silu_mul(h, lw.w_gu, act),
+        "down": lambda lw: ops.gemm_add_rmsnorm(act, lw.w_down, x, lw.w_in, eps, h),
+        "lm_head": lambda lw: ops.gemm_argmax(h, model.lm_head, tok),
+    }
+    shapes, tot_b, tot_s, tot_n = {}, 0.0, 0.0, 0
+    for name, N, K, per_fwd in gemm_shapes(c):
+        fn = calls[name]
+        us = graph_time_us([lambda lw=lw: fn(lw) for lw in model.layers], rounds=2)
+        nbytes = 2 * N * K + 2 * M * K + 2 * M * (N if name != "gate_up" else N // 2)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        shapes[name] = {"N": N, "K": K, "launch_us": us, "algorithmic_bytes": nbytes, "achieved": gbs,
+                        "frac": gbs / hbm_peak, "per_forward": per_fwd}
+        tot_b += nbytes * per_fwd
+        tot_s += us * 1e-6 * per_fwd
+        tot_n += per_fwd
+    runner.reset()
+    return {"achieved": tot_b / tot_s / 1e9, "bytes": tot_b, "seconds": tot_s, "launches": tot_n, "shapes": shapes,
+            "traffic": GEMM_TRAFFIC.get(M)}
+
+
+def step_algorithmic_bytes(c, B: int, P: int, compact: int, gamma: int, accept_lengths, max_new: int) -> float:
+    """Algorithmic HBM bytes of one timed step (one STD decode of max_new
+    tokens for the B requests): every forward streams the decoder weights
+    (the lm_head too, except the last draft of a round, whose prediction is
+    unused), every draft forward reads its request's sparse K/V (2048 B per
+    key per layer) and every verify forward its dense K/V, at the lengths of
+    request 0's recorded rounds (the requests' rounds are alike).  KV appends
+    and activations (< 1 %) are left out."""
+    H, I, V = c.hidden_size, c.intermediate_size, c.vocab_size
+    Lyr = c.num_hidden_layers
+    w_layers = Lyr * 2 * (c.qkv_size * H + H * H + 2 * I * H + H * I)
+    w_head = 2 * V * H
+    total, n_gen = 0.0, 0
+    for r, acc in enumerate(accept_lengths[0]):
+        pending = 0 if r == 0 else 1
+        ls = compact + n_gen  # sparse keys before the round's first draft
+        ld = P + n_gen - pending  # dense keys before the verify block
+        for i in range(gamma):  # drafts
+            total += w_layers + (w_head if i < gamma - 1 else 0) + Lyr * B * 2048 * (ls + i + 1)
+        total += w_layers + w_head + Lyr * B * 2048 * (ld + gamma + pending)  # verify
+        total += w_layers + w_head + Lyr * B * 2048 * (ls + acc + 1)  # bonus step
+        n_gen += min(acc + 1, max_new - n_gen)
+    return total
+
+
 # ----------------------------------------------------------------------------- B200 arm
 def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     import torch
@@ -171,16 +293,8 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
 
-    def barrier():
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
-
-    def allreduce(x: float, op: str) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
-        return float(t.item())
+    sync = RankSync(dist, dev, [local_rank])
+    barrier, allreduce = sync.barrier, sync.reduce
 
     B, P, V, T = w["batch"], w["prompt"], w["visual"], w["text"]
     c = QWEN25_VL_7B
@@ -232,15 +346,14 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     clocks = sampler.stop()
     t_local = ev0.elapsed_time(ev1) / 1000.0
     tokens_local = a.steps * int(runner.n_gen.sum().item())
-    t_max = allreduce(t_local, "max")
-    tokens_all = allreduce(float(tokens_local), "sum")
-    value = tokens_all / t_max
+    tokens_all, t_max, value = sync.throughput(t_local, float(tokens_local))
     st = runner.std_stats()
     std_tokens = runner.out_tokens.clone()
     acc_all = sum(st["accepted"])
     prop_all = sum(st["proposed"])
     rounds_all = [len(x) for x in st["accept_lengths"]]
     mean_accept = acc_all / max(1, sum(rounds_all))
+    g_ = w["gamma"]
 
     # ---- AR on the same prefilled state: tokens/s and token-exactness ----
     ar_tps, token_exact = None, None
@@ -251,8 +364,18 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
         token_exact = bool(torch.equal(std_tokens, runner.out_tokens))
         token_exact = bool(allreduce(0.0 if token_exact else 1.0, "sum") == 0.0)
 
-    # ---- roofline: verify kernel (dominant of ours) and draft kernel, timed alone ----
+    # ---- roofline ----
+    peaks = {}
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
     runner.reset()
+    gemm = gemm_roofline(runner, model, B, hbm_peak)
     nq = w["gamma"] + 1
     qv = torch.randn(B, nq, c.num_attention_heads, c.head_dim, device=dev).to(torch.bfloat16)
     ov = torch.empty_like(qv)
@@ -272,65 +395,55 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
                              for li in range(c.num_hidden_layers)], rounds=4) / 1e6
     Ls = w["compact"] + 1
     draft_bytes = B * (2048 * Ls + 14336)
-    peaks = {}
-    try:
-        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except Exception:
-        pass
-    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
-    achieved = verify_bytes / t_verify / 1e9
     draft_gbs = draft_bytes / t_draft / 1e9
+    verify_gbs = verify_bytes / t_verify / 1e9
+    step_bytes = step_algorithmic_bytes(c, B, P, w["compact"], g_, st["accept_lengths"], w["max_new"])
     assert ops.device_error() == 0
 
-    # ---- launches of our kernels in the timed region ----
-    # A forward: embed + first RMSNorm, then per layer QKV GEMM, RoPE/append
-    # epilogue (a GEMM on padded rows adds a split-K reduce), attention (+ the
-    # verify split merge), O GEMM, residual+norm epilogue, gate/up GEMM with
-    # SiLU, down GEMM, residual+norm epilogue; lm_head GEMM + argmax keys.
-    Lyr = c.num_hidden_layers
-    g_ = w["gamma"]
-    verify_merge = 1  # the verify kernel splits keys (and merges) whenever B*Hkv < 148 and cap >= 256
-
-    def forward_launches(dense: bool, padded: bool, head: bool) -> int:
-        per_layer = 8 + (1 if padded else 0) + (verify_merge if dense else 0)
-        return 2 + Lyr * per_layer + (2 if head else 0)
-
-    def round_launches(first: bool) -> int:
-        nq = g_ + (0 if first else 1)
-        verify = forward_launches(True, B * nq != runner.dense_rows, True)
-        drafts = (g_ - 1) * forward_launches(False, False, True) + forward_launches(False, False, False)
-        return drafts + verify + 1 + forward_launches(False, False, True)  # + accept, bonus step
-    per_step = round_launches(True) + (rounds_per_step - 1) * round_launches(False)
+    # ---- launches of our kernels in the timed region, counted from the captured loop graph ----
+    lc = runner.launch_counts("std_loop")
+    per_step = lc["outer_ours"] + (rounds_per_step - 1) * lc["body_ours"]
     gpu_launches = a.steps * per_step
 
     # ---- e2e through the public API, host buffers ----
-    e2e = None
+    # `e2e`: a fresh std_generate_qwen25vl call as a user makes it (runner=None):
+    # cache allocation, graph capture, H2D of the inputs from pinned host
+    # memory, two-stage prefill, selection, compaction, STD decode and the D2H
+    # read of the tokens.  `e2e_prepared_runner`: the same call on the bench's
+    # already-built runner, which skips the allocation and the capture.
+    e2e, e2e_warm = None, None
     if not a.no_e2e:
         ids_h = ids.pin_memory()
         vis_h = vis.cpu().pin_memory()
         h2d = ids_h.numel() * ids_h.element_size() + vis_h.numel() * vis_h.element_size()
-        d2h = B * w["max_new"] * 8
-        torch.cuda.synchronize()
-        barrier()
-        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        x0.record()
-        res, _ = std_generate_qwen25vl(model, {"input_ids": ids_h, "visual_embeds": vis_h}, VIDEO_TOKEN_ID, -1,
-                                       max_new_tokens=w["max_new"], gamma=w["gamma"],
-                                       target_k_plus_text=w["k_plus_text"], ignore_eos=True, runner=runner)
-        gen_host = res.output_ids  # host tensor (device -> host read inside the call)
-        x1.record()
-        torch.cuda.synchronize()
-        barrier()
-        te = allreduce(x0.elapsed_time(x1) / 1000.0, "max")
-        toks = allreduce(float(res.generate_len), "sum")
-        e2e = {"value": toks / te, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "seconds": te, "includes": "H2D of ids+visual embeddings, two-stage prefill, selection, compaction, "
-                                         "STD decode, D2H of tokens",
-               "token_exact_vs_timed_run": bool(torch.equal(gen_host[:, P:].to(torch.int32),
-                                                             std_tokens.cpu()[:, : gen_host.shape[1] - P]))}
+        d2h = B * (P + w["max_new"]) * 8
+        kw = dict(max_new_tokens=w["max_new"], gamma=g_, target_k_plus_text=w["k_plus_text"], ignore_eos=True)
+        results = {}
+        for key, rn in (("prepared", runner), ("fresh", None)):
+            torch.cuda.synchronize()
+            barrier()
+            x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            x0.record()
+            res, _ = std_generate_qwen25vl(model, {"input_ids": ids_h, "visual_embeds": vis_h}, VIDEO_TOKEN_ID, -1,
+                                           runner=rn, **kw)
+            gen_host = res.output_ids  # host tensor (device -> host read inside the call)
+            x1.record()
+            torch.cuda.synchronize()
+            barrier()
+            te = allreduce(x0.elapsed_time(x1) / 1000.0, "max")
+            toks = allreduce(float(res.generate_len), "sum")
+            results[key] = {
+                "value": toks / te, "unit": "tokens/s", "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "seconds": te,
+                "token_exact_vs_timed_run": bool(torch.equal(gen_host[:, P:].to(torch.int32),
+                                                              std_tokens.cpu()[:, : gen_host.shape[1] - P]))}
+            del res, gen_host
+            torch.cuda.empty_cache()
+        e2e = dict(results["fresh"], includes="std_generate_qwen25vl(runner=None): KV-cache allocation, CUDA-graph "
+                   "capture, H2D of ids+visual embeddings (pinned), two-stage prefill, selection, compaction, "
+                   "STD decode, D2H of the output ids")
+        e2e_warm = dict(results["prepared"], includes="the same call with the bench's prepared runner (allocation "
+                        "and capture excluded)")
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -354,15 +467,29 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
                    "max_new_tokens": w["max_new"], "parallelism": f"dp{world} (independent request groups)",
                    "l2": "inputs larger than L2 (15.2 GB weights + KV caches read per step)"},
         "e2e": e2e,
-        "roofline": {"bound": "hbm", "kernel": "verify_attn_kernel (tcgen05)", "achieved": achieved,
-                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
-                     "traffic": VERIFY_TRAFFIC.get((B, L, nq)), "traffic_unit": "bytes per launch",
-                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, burst)",
-                     "algorithmic_bytes_per_launch": verify_bytes, "launch_us": t_verify * 1e6,
-                     "tensor_tflops": verify_flops / t_verify / 1e12,
-                     "tensor_frac": verify_flops / t_verify / 1e12 / tc_peak},
-        "draft_attn": {"achieved": draft_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": draft_gbs / hbm_peak,
-                       "algorithmic_bytes_per_launch": draft_bytes, "launch_us": t_draft * 1e6},
+        "e2e_prepared_runner": e2e_warm,
+        "roofline": {
+            "bound": "hbm", "kernel": "gemm_kernel (tcgen05 weight stream; the decode forwards' projections, MLP "
+                                      "and lm_head with their fused epilogues)",
+            "achieved": gemm["achieved"], "peak": hbm_peak, "unit": "GB/s", "frac": gemm["achieved"] / hbm_peak,
+            "traffic": gemm["traffic"], "traffic_unit": "bytes per sparse forward's GEMM launches",
+            "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs, burst)",
+            "algorithmic_bytes_per_launch": gemm["bytes"] / gemm["launches"],
+            "launch_us": gemm["seconds"] * 1e6 / gemm["launches"],
+            "basis": "the GEMM launches of one sparse (draft) forward at M = requests per GPU, each shape timed "
+                     "over the 28 layers' distinct weights from one CUDA graph; achieved = their algorithmic bytes "
+                     "(weights + activations) / their summed time",
+            "shapes": gemm["shapes"],
+            "step_frac": step_bytes / (t_max / a.steps) / 1e9 / hbm_peak,
+            "step_algorithmic_bytes": step_bytes,
+            "verify_attn": {"kernel": "verify_attn_kernel (tcgen05)", "achieved": verify_gbs, "frac": verify_gbs / hbm_peak,
+                            "traffic": VERIFY_TRAFFIC.get((B, L, nq)), "algorithmic_bytes_per_launch": verify_bytes,
+                            "launch_us": t_verify * 1e6, "tensor_tflops": verify_flops / t_verify / 1e12,
+                            "tensor_frac": verify_flops / t_verify / 1e12 / tc_peak,
+                            "tensor_pipe_active_ncu": VERIFY_TENSOR_ACTIVE.get((B, L, nq))},
+            "draft_attn": {"kernel": "draft_attn_kernel", "achieved": draft_gbs, "frac": draft_gbs / hbm_peak,
+                           "algorithmic_bytes_per_launch": draft_bytes, "launch_us": t_draft * 1e6},
+        },
         "cpu_baseline": cpu_baseline,
         "clocks": clocks,
         "gpu_launches": gpu_launches,

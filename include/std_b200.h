@@ -251,6 +251,29 @@ int std_ar_commit(int B, int tok_stride, int max_new, int eos, int ignore_eos, c
 int std_ar_advance(int B, const int32_t* active, const int32_t* next_tok, int32_t* tok, int tok_stride,
                    int32_t* dense_len, int32_t* ctx_len, void* stream);
 
+/* ---- (d) device-side decode loop (CUDA graph WHILE node) --------------- */
+
+/* Replaces: the host-driven decode loops of std_qwen25vl.py:766-939 (STD
+ * rounds, `while len(generated) < max_new_tokens`, with .tolist() host reads
+ * each round) and :575-606 (AR steps).  Called while `stream` is capturing a
+ * CUDA graph: enqueues a kernel that zeroes *counter and sets the loop
+ * condition to "some done[b] == 0" (b < B), appends a WHILE conditional node,
+ * and begins capturing `body_stream` (a different stream, not capturing) into
+ * the node's body graph.  The caller then enqueues one loop iteration on
+ * body_stream and calls std_capture_while_end, which enqueues the condition
+ * update (counter += 1; continue while some request runs and counter <
+ * max_iters) and ends the body capture.  handle_out receives the conditional
+ * handle for std_capture_while_end, body_graph_out (optional) the body graph
+ * (owned by the WHILE node).  done and counter are device int32. */
+int std_capture_while_begin(void* stream, void* body_stream, const int32_t* done, int B, int32_t* counter,
+                            unsigned long long* handle_out, void** body_graph_out);
+int std_capture_while_end(void* body_stream, unsigned long long handle, const int32_t* done, int B, int32_t* counter,
+                          int max_iters);
+/* Launch accounting for a captured cudaGraph_t (no reference counterpart):
+ * counts[0] kernel nodes, counts[1] of them this library's.  Child graphs are
+ * followed; conditional bodies are not (count a body graph on its own). */
+int std_graph_kernel_counts(void* graph, int* counts);
+
 #ifdef __cplusplus
 }
 #endif

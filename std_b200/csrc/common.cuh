@@ -15,6 +15,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <utility>
 
 #define STD_DEV __device__ __forceinline__
@@ -383,6 +385,43 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ---------------------------------------------------------------------------
+// host: dynamic shared-memory limits, per device.  cudaFuncSetAttribute
+// applies to the current device only, so the grant is recorded per device
+// ordinal: a process that drives several GPUs sets it on each of them.  The
+// fast path is one atomic load; setting it takes a lock, so host threads
+// launching on the same device concurrently are safe.
+// ---------------------------------------------------------------------------
+constexpr int STD_MAX_DEVICES = 128;
+
+struct SmemGrant {
+  std::atomic<size_t> bytes[STD_MAX_DEVICES];
+  std::mutex mu;
+  SmemGrant() {
+    for (auto& b : bytes) b.store(0, std::memory_order_relaxed);
+  }
+};
+
+// Ensure `kernel` may use `smem` bytes of dynamic shared memory on the current
+// device (and, with max_carveout, prefers the largest shared-memory carveout).
+// Returns 0, or 3 when the device or the attribute call fails.
+template <typename Kernel>
+static int ensure_smem(Kernel kernel, SmemGrant& grant, size_t smem, bool max_carveout = false) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= STD_MAX_DEVICES) return 3;
+  if (grant.bytes[dev].load(std::memory_order_acquire) >= smem) return 0;
+  std::lock_guard<std::mutex> lock(grant.mu);
+  if (grant.bytes[dev].load(std::memory_order_relaxed) >= smem) return 0;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return 3;
+  if (max_carveout &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+          cudaSuccess)
+    return 3;
+  grant.bytes[dev].store(smem, std::memory_order_release);
+  return 0;
 }
 
 // ---------------------------------------------------------------------------

@@ -710,15 +710,8 @@ extern "C" int std_draft_attn(const void* q, const void* k_cache, const void* v_
   if ((reinterpret_cast<uintptr_t>(q) & 3) != 0) return 1;
   const long long rows = static_cast<long long>(B) * Hkv * cap;
   if (rows + stdb::DR_SUB >= (1ll << 31)) return 1;  // tensor-map row coordinates are 32-bit
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(stdb::draft_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, stdb::DR_SMEM) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(stdb::draft_attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-      return 3;
-    attr_set = true;
-  }
+  static SmemGrant grant;
+  if (ensure_smem(stdb::draft_attn_kernel, grant, stdb::DR_SMEM, true) != 0) return 3;
   CUtensorMap tk64, tv64, tk16, tv16;
   int rc = make_tmap_bf16_2d(&tk64, k_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_SUB);
   if (rc == 0) rc = make_tmap_bf16_2d(&tv64, v_cache, static_cast<uint64_t>(rows), 128, 256, 64, stdb::DR_SUB);
@@ -755,15 +748,8 @@ extern "C" int std_draft_attn_indexed(const void* q, const void* dense_k, const 
         reinterpret_cast<uintptr_t>(tail_k) | reinterpret_cast<uintptr_t>(tail_v)) & 15) != 0)
     return 1;
   if ((reinterpret_cast<uintptr_t>(q) & 3) != 0) return 1;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(stdb::draft_attn_indexed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             stdb::DR_SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(stdb::draft_attn_indexed_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
-      return 3;
-    attr_set = true;
-  }
+  static SmemGrant grant;
+  if (ensure_smem(stdb::draft_attn_indexed_kernel, grant, stdb::DR_SMEM, true) != 0) return 3;
   stdb::DraftParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.lens = lens;

@@ -347,13 +347,8 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
   stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
   const size_t smem = static_cast<size_t>(stages) * stage_bytes + 1024;
-  static size_t attr_smem = 0;
-  if (smem > attr_smem) {
-    if (cudaFuncSetAttribute(stdb::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-        cudaSuccess)
-      return 3;
-    attr_smem = smem;
-  }
+  static SmemGrant grant;
+  if (ensure_smem(stdb::gemm_kernel, grant, smem) != 0) return 3;
   CUtensorMap tw, tx;
   int rc = make_tmap_bf16_2d(&tw, w, static_cast<uint64_t>(N), static_cast<uint64_t>(K),
                              static_cast<uint64_t>(K) * 2, stdb::GM_BK, stdb::GM_BM);

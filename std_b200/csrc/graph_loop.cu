@@ -1,0 +1,141 @@
+// graph_loop.cu -- device-side decode loops inside one CUDA graph.
+//
+// The reference drives decoding from Python: every STD round ends with host
+// reads of the verify argmax and of the accepted length (std_qwen25vl.py:806
+// `.tolist()`, the `while len(generated) < max_new_tokens` loop at :766), so the
+// GPU idles while the host decides whether to run another round.  Here the loop
+// itself lives in the graph: a WHILE conditional node whose body is one decode
+// round (or one AR step) and whose condition a one-warp kernel sets from the
+// device-resident `done` flags at the end of every iteration.  The host
+// launches the whole decode once and synchronises once.
+//
+// Capture protocol (the stream is already capturing, e.g. under
+// torch.cuda.graph):
+//   std_capture_while_begin(stream, body_stream, done, B, counter)
+//     enqueues loop_init_kernel on `stream` (counter = 0; condition = "some
+//     request is still running"), appends the WHILE node after it, and starts
+//     capturing `body_stream` into the node's body graph;
+//   ... the caller enqueues one round on body_stream ...
+//   std_capture_while_end(body_stream, done, B, counter, max_iters)
+//     enqueues loop_continue_kernel on body_stream (counter += 1; condition =
+//     "some request running and counter < max_iters") and ends the body
+//     capture.
+// The iteration bound makes every loop finite whatever the done flags say.
+#include "common.cuh"
+
+namespace stdb {
+
+// 1 when some request b < B has done[b] == 0.
+STD_DEV unsigned any_running(const int32_t* done, int B) {
+  unsigned run = 0;
+  for (int b = threadIdx.x; b < B; b += 32) run |= (done[b] == 0) ? 1u : 0u;
+  return __any_sync(0xffffffffu, run != 0) ? 1u : 0u;
+}
+
+__global__ void loop_init_kernel(cudaGraphConditionalHandle h, const int32_t* done, int B, int32_t* counter) {
+  const unsigned run = any_running(done, B);
+  if (threadIdx.x == 0) {
+    *counter = 0;
+    cudaGraphSetConditional(h, run);
+  }
+}
+
+__global__ void loop_continue_kernel(cudaGraphConditionalHandle h, const int32_t* done, int B, int32_t* counter,
+                                     int max_iters) {
+  const unsigned run = any_running(done, B);
+  if (threadIdx.x == 0) {
+    const int32_t c = *counter + 1;
+    *counter = c;
+    cudaGraphSetConditional(h, (run != 0u && c < max_iters) ? 1u : 0u);
+  }
+}
+
+}  // namespace stdb
+
+extern "C" int std_capture_while_begin(void* stream, void* body_stream, const int32_t* done, int B, int32_t* counter,
+                                       unsigned long long* handle_out, void** body_graph_out) {
+  if (stream == nullptr || body_stream == nullptr || stream == body_stream || done == nullptr || counter == nullptr ||
+      B <= 0 || handle_out == nullptr)
+    return 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  cudaGraph_t graph = nullptr;
+  if (cudaStreamGetCaptureInfo(s, &st, nullptr, &graph, nullptr, nullptr) != cudaSuccess) return 4;
+  if (st != cudaStreamCaptureStatusActive || graph == nullptr) return 1;  // must be called while capturing
+  cudaGraphConditionalHandle h;
+  // default 0: if the init kernel never ran, the body does not run either
+  if (cudaGraphConditionalHandleCreate(&h, graph, 0, cudaGraphCondAssignDefault) != cudaSuccess) return 4;
+  stdb::loop_init_kernel<<<1, 32, 0, s>>>(h, done, B, counter);
+  if (cudaGetLastError() != cudaSuccess) return 4;
+  const cudaGraphNode_t* deps = nullptr;
+  size_t ndeps = 0;
+  if (cudaStreamGetCaptureInfo(s, &st, nullptr, &graph, &deps, &ndeps) != cudaSuccess) return 4;
+  cudaGraphNodeParams np = {};
+  np.type = cudaGraphNodeTypeConditional;
+  np.conditional.handle = h;
+  np.conditional.type = cudaGraphCondTypeWhile;
+  np.conditional.size = 1;
+  cudaGraphNode_t node;
+  if (cudaGraphAddNode(&node, graph, deps, ndeps, &np) != cudaSuccess) return 4;
+  if (cudaStreamUpdateCaptureDependencies(s, &node, 1, cudaStreamSetCaptureDependencies) != cudaSuccess) return 4;
+  cudaGraph_t body = np.conditional.phGraph_out[0];
+  if (cudaStreamBeginCaptureToGraph(static_cast<cudaStream_t>(body_stream), body, nullptr, nullptr, 0,
+                                    cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+    return 4;
+  *handle_out = static_cast<unsigned long long>(h);
+  if (body_graph_out != nullptr) *body_graph_out = body;
+  return 0;
+}
+
+extern "C" int std_capture_while_end(void* body_stream, unsigned long long handle, const int32_t* done, int B,
+                                     int32_t* counter, int max_iters) {
+  if (body_stream == nullptr || done == nullptr || counter == nullptr || B <= 0 || max_iters <= 0) return 1;
+  cudaStream_t s = static_cast<cudaStream_t>(body_stream);
+  stdb::loop_continue_kernel<<<1, 32, 0, s>>>(static_cast<cudaGraphConditionalHandle>(handle), done, B, counter,
+                                               max_iters);
+  const cudaError_t launch = cudaGetLastError();
+  cudaGraph_t g = nullptr;
+  const cudaError_t end = cudaStreamEndCapture(s, &g);  // the body graph is owned by the WHILE node
+  return (launch == cudaSuccess && end == cudaSuccess) ? 0 : 4;
+}
+
+// ---------------------------------------------------------------------------
+// Launch accounting: kernel nodes of a captured graph, and how many of them
+// are this library's own kernels (namespace stdb).  Child graphs are followed;
+// conditional bodies are counted separately (std_capture_while_begin returns
+// the body graph), since they run once per loop iteration.
+// ---------------------------------------------------------------------------
+#include <cstring>
+#include <vector>
+
+static int count_graph_kernels(cudaGraph_t g, int* counts) {
+  size_t n = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess) return 4;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n > 0 && cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return 4;
+  for (cudaGraphNode_t node : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(node, &t) != cudaSuccess) return 4;
+    if (t == cudaGraphNodeTypeKernel) {
+      counts[0] += 1;
+      cudaKernelNodeParams kp = {};
+      const char* name = nullptr;
+      if (cudaGraphKernelNodeGetParams(node, &kp) == cudaSuccess && kp.func != nullptr &&
+          cudaFuncGetName(&name, kp.func) == cudaSuccess && name != nullptr && std::strncmp(name, "_ZN4stdb", 8) == 0)
+        counts[1] += 1;
+      cudaGetLastError();  // a foreign kernel may leave a lookup error behind
+    } else if (t == cudaGraphNodeTypeGraph) {
+      cudaGraph_t child = nullptr;
+      if (cudaGraphChildGraphNodeGetGraph(node, &child) != cudaSuccess) return 4;
+      const int rc = count_graph_kernels(child, counts);
+      if (rc != 0) return rc;
+    }
+  }
+  return 0;
+}
+
+extern "C" int std_graph_kernel_counts(void* graph, int* counts) {
+  if (graph == nullptr || counts == nullptr) return 1;
+  counts[0] = counts[1] = 0;
+  return count_graph_kernels(static_cast<cudaGraph_t>(graph), counts);
+}

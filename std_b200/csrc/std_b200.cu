@@ -12,6 +12,7 @@
 #include "select.cu"
 #include "verify_attn.cu"
 #include "gemm.cu"
+#include "graph_loop.cu"
 
 extern "C" int std_version(void) { return 100; }
 

@@ -463,13 +463,8 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
        15) != 0)
     return 1;
   if (workspace == nullptr || workspace_bytes < std_verify_attn_workspace_bytes(B, Hkv, cap)) return 5;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(stdb::verify_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, stdb::VF_SMEM) !=
-        cudaSuccess)
-      return 3;
-    attr_set = true;
-  }
+  static SmemGrant grant;
+  if (ensure_smem(stdb::verify_attn_kernel, grant, stdb::VF_SMEM) != 0) return 3;
   CUtensorMap tk, tv;
   const uint64_t rows = static_cast<uint64_t>(B) * Hkv * cap;
   int rc = make_tmap_bf16_2d(&tk, k_cache, rows, 128, 256, 64, stdb::VF_CHUNK);
@@ -520,21 +515,19 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
 // caller workspace.  Every GPU that loads this library holds that array
 // (STD_VERIFY_NOALLOC_SCRATCH_BYTES) until the process exits.
 // ---------------------------------------------------------------------------
-#include <mutex>
-
 namespace {
 constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(32) << 20;  // == STD_VERIFY_NOALLOC_SCRATCH_BYTES
 __device__ __align__(256) unsigned char g_verify_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[128] = {};  // device address of the array, per device ordinal
+void* g_noalloc_ptr[STD_MAX_DEVICES] = {};  // device address of the array, per device ordinal
 
 // On the host, g_verify_noalloc_scratch only stands in for the symbol; its
 // device address is looked up once per device, with that device current.
 int noalloc_scratch_for_current_device(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 4;
-  if (dev < 0 || dev >= 128) return 3;
+  if (dev < 0 || dev >= STD_MAX_DEVICES) return 3;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
@@ -549,7 +542,9 @@ int noalloc_scratch_for_current_device(void** out) {
 extern "C" int std_verify_attn_noalloc(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
                                        int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap,
                                        void* out, float* lse, void* stream) {
-  if (B <= 0 || Hkv <= 0 || cap <= 0) return 1;
+  // argument errors (status 1) take precedence over the capacity check (status 2)
+  if (D != stdb::VF_D || Hkv <= 0 || Hq != Hkv * stdb::VF_G || nq < 1 || stdb::VF_G * nq > 128 || B <= 0 || cap <= 0)
+    return 1;
   if (std_verify_attn_workspace_bytes(B, Hkv, cap) > kNoAllocScratchBytes) return 2;
   void* scratch = nullptr;
   const int rc = noalloc_scratch_for_current_device(&scratch);

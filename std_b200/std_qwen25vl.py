@@ -94,6 +94,10 @@ class GenerateResult:
     selection_time: float = 0.0
     dense_prefill_time: float = 0.0
     sparse_cache_time: float = 0.0
+    # B200 batch extension: the per-round lists above concatenate every
+    # request's rounds in request order; these keep them per request
+    request_accept_lengths: List[List[int]] = field(default_factory=list)
+    request_generate_lens: List[int] = field(default_factory=list)
 
     @property
     def acceptance_rate(self) -> float:
@@ -230,7 +234,8 @@ class STDRunner:
                  gamma: int = 9, k: int = 896, eos_token_id: int = -1, ignore_eos: bool = False,
                  use_graphs: bool = True, verify_mode: str = "parallel", shard=None,
                  sparse_cache: str = "compact", selection_policy: str = "static",
-                 selection_update_interval: int = 1, min_selection_change_ratio: float = 0.0):
+                 selection_update_interval: int = 1, min_selection_change_ratio: float = 0.0,
+                 device_loop: bool = True):
         c = model.config
         if gamma < 1 or 7 * (gamma + 1) > 126:
             raise ValueError("gamma must be in [1, 17]")
@@ -307,6 +312,14 @@ class STDRunner:
         self.topk = torch.zeros(c.num_hidden_layers, c.num_key_value_heads, k, **i32)
         self.topk_per_request: List[torch.Tensor] = []
         self._graphs: Dict[str, torch.cuda.CUDAGraph] = {}
+        self.loop_counter = torch.zeros(1, **i32)
+        self._loop_bodies: Dict[str, int] = {}
+        self._body_stream: Optional[torch.cuda.Stream] = None
+        # decode loops as one graph each (a WHILE node around a round / AR
+        # step): no host round trip between rounds.  The host-driven loop
+        # remains for dynamic re-selection (its update allocates) and for a
+        # sequence-sharded owner (its collectives run outside graphs).
+        self.device_loop = device_loop and use_graphs and shard is None and not self.dynamic
         self.prefill_done = False
         if self.dynamic:
             vp = layout.visual_pos
@@ -525,23 +538,37 @@ class STDRunner:
         torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
 
     # ------------------------------------------------------------------ graphs
-    def capture(self) -> None:
-        """Capture the round-1, steady-state and AR-step graphs.
+    def capture(self, mode: str = "all") -> None:
+        """Capture the CUDA graphs a decode of `mode` ("std", "ar" or "all") replays.
 
-        Each step runs once eagerly first (allocating workspaces and setting
-        kernel attributes outside capture); state is reset afterwards."""
+        Device loop: one graph per mode (std_loop / ar_loop).  Host-driven
+        loop: the round-1, steady-state (and selection-update) round graphs
+        and the AR-step graph; a sequence-sharded owner captures only its
+        local phases.  Each step runs once eagerly first (allocating
+        workspaces and setting kernel attributes outside capture); state is
+        reset afterwards."""
         if not self.use_graphs:
             return
-        if self.shard is None:
-            steps = [("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False)),
-                     ("ar", self.ar_step)]
-            if self.dynamic:
-                steps += [("std_first_upd", lambda: self.std_round(True, True)),
-                          ("std_upd", lambda: self.std_round(False, True))]
-        else:
+        want_std, want_ar = mode in ("std", "all"), mode in ("ar", "all")
+        if self.shard is not None:
             # collectives stay outside the graphs: the dense forwards (verify,
             # AR steps) run eagerly between captured local phases
-            steps = (("drafts", self._drafts), ("post_first", lambda: self._post(0)), ("post", lambda: self._post(1)))
+            steps = [("drafts", self._drafts), ("post_first", lambda: self._post(0)), ("post", lambda: self._post(1))]
+        elif self.device_loop:
+            steps = []
+            if want_std and "std_loop" not in self._graphs:
+                steps += [("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False))]
+            if want_ar and "ar_loop" not in self._graphs:
+                steps += [("ar", self.ar_step)]
+        else:
+            steps = []
+            if want_std:
+                steps += [("std_first", lambda: self.std_round(True)), ("std", lambda: self.std_round(False))]
+                if self.dynamic:
+                    steps += [("std_first_upd", lambda: self.std_round(True, True)),
+                              ("std_upd", lambda: self.std_round(False, True))]
+            if want_ar:
+                steps += [("ar", self.ar_step)]
         for name, fn in steps:
             if name in self._graphs:
                 continue
@@ -552,14 +579,78 @@ class STDRunner:
                 fn()
             torch.cuda.current_stream().wait_stream(side)
             torch.cuda.synchronize()
+            if self.device_loop:
+                continue  # eager warm-up only: the loop graphs below hold these steps
             self.reset()
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
             self._graphs[name] = g
+        if self.device_loop:
+            self._capture_loops(want_std, want_ar)
         self.reset()
         torch.cuda.synchronize()
+
+    def _capture_loops(self, want_std: bool, want_ar: bool) -> None:
+        """std_loop: round 1, then a WHILE node around steady-state rounds;
+        ar_loop: a WHILE node around AR steps.  The loop condition is set on
+        the device from the done flags (libstd_b200 graph_loop.cu), bounded by
+        max_new_tokens + 1 iterations.  Every step already ran eagerly in
+        capture(), so nothing allocates while the body is captured."""
+        import ctypes
+
+        from . import _lib
+
+        if self._body_stream is None:
+            self._body_stream = torch.cuda.Stream()
+        body_stream = self._body_stream
+        limit = self.max_new + 1
+
+        def loop(body) -> None:
+            h = ctypes.c_ulonglong(0)
+            bg = ctypes.c_void_p(0)
+            _lib.call("std_capture_while_begin", torch.cuda.current_stream().cuda_stream, body_stream.cuda_stream,
+                      self.done.data_ptr(), self.B, self.loop_counter.data_ptr(), ctypes.byref(h), ctypes.byref(bg))
+            bodies.append(bg.value)
+            with torch.cuda.stream(body_stream):
+                body()
+            _lib.call("std_capture_while_end", body_stream.cuda_stream, h.value, self.done.data_ptr(), self.B,
+                      self.loop_counter.data_ptr(), limit)
+
+        loops = []
+        if want_std:
+            loops.append(("std_loop", lambda: (self.std_round(True), loop(lambda: self.std_round(False)))))
+        if want_ar:
+            loops.append(("ar_loop", lambda: loop(self.ar_step)))
+        for name, fn in loops:
+            if name in self._graphs:
+                continue
+            self.reset()
+            torch.cuda.synchronize()
+            bodies: List[int] = []
+            g = torch.cuda.CUDAGraph(keep_graph=True)  # kept for launch accounting (launch_counts)
+            with torch.cuda.graph(g):
+                fn()
+            g.instantiate()
+            self._graphs[name] = g
+            self._loop_bodies[name] = bodies[0]
+
+    def launch_counts(self, name: str) -> Dict[str, int]:
+        """Kernel launches of one replay of loop graph `name` ("std_loop" /
+        "ar_loop"): once-per-decode kernels outside the loop body and
+        per-iteration kernels in the body, counted from the captured graph
+        nodes; "*_ours" are this library's kernels."""
+        import ctypes
+
+        from . import _lib
+
+        out = {}
+        for part, graph in (("outer", self._graphs[name].raw_cuda_graph()), ("body", self._loop_bodies[name])):
+            c = (ctypes.c_int * 2)()
+            _lib.call("std_graph_kernel_counts", ctypes.c_void_p(graph), c)
+            out[part], out[part + "_ours"] = int(c[0]), int(c[1])
+        return out
 
     def _all_done(self) -> bool:
         self.all_done_host.copy_(self.all_done, non_blocking=True)
@@ -568,10 +659,23 @@ class STDRunner:
 
     # ------------------------------------------------------------------ loops
     def run_std(self) -> float:
-        """STD decode of every request from the post-prefill state; returns seconds (device time)."""
-        self.capture()
+        """STD decode of every request from the post-prefill state; returns seconds (device time).
+
+        With the device loop the whole decode is one graph launch and one
+        synchronisation; otherwise the host launches a round graph and reads
+        the 4-byte all-done flag after each round."""
+        self.capture("std")
         self.reset()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        loop = self._graphs.get("std_loop")
+        if loop is not None:
+            start.record()
+            loop.replay()
+            end.record()
+            end.synchronize()
+            if not bool(self.done.all().item()):
+                raise RuntimeError("STD decode did not terminate within max_new_tokens + 1 rounds")
+            return start.elapsed_time(end) / 1000.0
         start.record()
         self._round(True, self._update_due(1))
         rounds = 1
@@ -585,9 +689,18 @@ class STDRunner:
         return start.elapsed_time(end) / 1000.0
 
     def run_ar(self) -> float:
-        self.capture()
+        self.capture("ar")
         self.reset()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        loop = self._graphs.get("ar_loop")
+        if loop is not None:
+            start.record()
+            loop.replay()
+            end.record()
+            end.synchronize()
+            if not bool(self.done.all().item()):
+                raise RuntimeError("AR decode did not terminate within max_new_tokens + 1 steps")
+            return start.elapsed_time(end) / 1000.0
         start.record()
         steps = 0
         while True:
@@ -601,6 +714,80 @@ class STDRunner:
         end.record()
         end.synchronize()
         return start.elapsed_time(end) / 1000.0
+
+    def run_std_profiled(self) -> Dict[str, float]:
+        """STD decode with per-phase device timers (profile_decode=True; the
+        reference's _profile_mark stages, std_qwen25vl.py:771-939, and
+        decode_profiler.py:85-145).  Each round runs as four graphs -- the
+        gamma draft steps, the dense verify, the fused accept/rollback, the
+        bonus sparse step -- with CUDA events between them, and the host
+        reads the all-done flag after every round as the reference does.
+        Returns seconds per phase: draft_time, verify_time, cache_adjust_time
+        (accept + cache-length rollback), bonus_time, and decoding_time."""
+        if self.shard is not None or self.dynamic:
+            raise ValueError("profiled decode covers the single-GPU static-selection runner")
+        phases = {"drafts": self._drafts, "verify_first": lambda: self._verify_phase(0),
+                  "verify": lambda: self._verify_phase(1), "accept_first": lambda: self._accept_and_flag(0),
+                  "accept": lambda: self._accept_and_flag(1), "bonus": self._bonus_step}
+        if self.use_graphs:
+            for name, fn in phases.items():
+                key = "phase_" + name
+                if key in self._graphs:
+                    continue
+                self.reset()
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    fn()
+                torch.cuda.current_stream().wait_stream(side)
+                torch.cuda.synchronize()
+                self.reset()
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn()
+                self._graphs[key] = g
+        self.reset()
+        torch.cuda.synchronize()
+        marks = []
+        rounds = 0
+        t0 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        while True:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            first = rounds == 0
+            ev[0].record()
+            self._replay_or_run("phase_drafts", phases["drafts"])
+            ev[1].record()
+            name = "verify_first" if first else "verify"
+            self._replay_or_run("phase_" + name, phases[name])
+            ev[2].record()
+            name = "accept_first" if first else "accept"
+            self._replay_or_run("phase_" + name, phases[name])
+            ev[3].record()
+            self._replay_or_run("phase_bonus", phases["bonus"])
+            ev[4].record()
+            marks.append(ev)
+            rounds += 1
+            if self._all_done():
+                break
+            if rounds > self.max_new + 1:
+                raise RuntimeError("STD decode did not terminate")
+        t1 = torch.cuda.Event(enable_timing=True)
+        t1.record()
+        t1.synchronize()
+        out = {"draft_time": 0.0, "verify_time": 0.0, "cache_adjust_time": 0.0, "bonus_time": 0.0}
+        for ev in marks:
+            out["draft_time"] += ev[0].elapsed_time(ev[1]) / 1000.0
+            out["verify_time"] += ev[1].elapsed_time(ev[2]) / 1000.0
+            out["cache_adjust_time"] += ev[2].elapsed_time(ev[3]) / 1000.0
+            out["bonus_time"] += ev[3].elapsed_time(ev[4]) / 1000.0
+        out["decoding_time"] = t0.elapsed_time(t1) / 1000.0
+        return out
+
+    def _accept_and_flag(self, pending: int) -> None:
+        self._accept(pending)
+        torch.amin(self.done, dim=0, keepdim=True, out=self.all_done)
 
     def _update_due(self, round_id: int) -> bool:
         """Selection updates run after rounds round_id % interval == 0 (one-based)."""
@@ -637,20 +824,61 @@ class STDRunner:
                 "mean_changed_ratio": (st[:, 1] / rounds).tolist()}
 
     def std_stats(self) -> Dict[str, object]:
+        """Per-request round records of the last STD decode.  proposed_lengths
+        and pending_lengths follow the reference's per-round bookkeeping
+        (std_qwen25vl.py:783-793): a round proposes min(gamma, remaining)
+        drafts, and every round after the first carries one pending bonus."""
         st = self.stats.cpu()
         hist = self.accept_hist.cpu()
         rounds = st[:, 0].tolist()
+        accept = [hist[b, : rounds[b]].tolist() for b in range(self.B)]
+        proposed = []
+        for b in range(self.B):
+            n_gen, props = 0, []
+            for a in accept[b]:
+                remaining = self.max_new - n_gen
+                props.append(min(self.gamma, remaining))
+                n_gen += min(a + 1, remaining)
+            proposed.append(props)
         return {
             "rounds": rounds,
             "accepted": st[:, 1].tolist(),
             "proposed": st[:, 2].tolist(),
-            "accept_lengths": [hist[b, : rounds[b]].tolist() for b in range(self.B)],
+            "accept_lengths": accept,
+            "proposed_lengths": proposed,
+            "pending_lengths": [[0] + [1] * (r - 1) if r > 0 else [] for r in rounds],
         }
 
 
 # ----------------------------------------------------------------------------
 # reference-shaped entry points
 # ----------------------------------------------------------------------------
+
+def _std_result(runner: STDRunner, ids: torch.Tensor, decoding_time: float, t0: float, tp: Dict[str, float],
+                gamma: int, prof: Optional[Dict[str, float]] = None) -> GenerateResult:
+    """GenerateResult of an STD decode over every request of the batch: counts
+    are summed, the per-round lists concatenate the requests' rounds in
+    request order, and mean_accept_length is accepted drafts per round over
+    all requests' rounds (for one request: the reference's definition,
+    std_qwen25vl.py:943)."""
+    gen = runner.generated()
+    out = torch.cat([ids.cpu().long(), gen], dim=1) if ids.shape[0] == gen.shape[0] else gen
+    st = runner.std_stats()
+    acc = [a for r in st["accept_lengths"] for a in r]
+    prof = prof or {}
+    return GenerateResult(
+        output_ids=out, decoding_time=decoding_time, inference_time=time.time() - t0,
+        generate_len=int(runner.n_gen.sum().item()), accepted_draft_tokens=int(sum(st["accepted"])),
+        proposed_draft_tokens=int(sum(st["proposed"])), mean_accept_length=(sum(acc) / len(acc)) if acc else 0.0,
+        decode_rounds=int(max(st["rounds"])), final_gamma=gamma, gamma_history=[gamma] * int(max(st["rounds"])),
+        accept_lengths=acc, proposed_lengths=[p for r in st["proposed_lengths"] for p in r],
+        pending_lengths=[p for r in st["pending_lengths"] for p in r],
+        draft_time=prof.get("draft_time", 0.0), verify_time=prof.get("verify_time", 0.0),
+        bonus_time=prof.get("bonus_time", 0.0), cache_adjust_time=prof.get("cache_adjust_time", 0.0),
+        prefill_time=tp["prefill_time"], selection_time=tp["selection_time"],
+        sparse_cache_time=tp["sparse_cache_time"], request_accept_lengths=st["accept_lengths"],
+        request_generate_lens=runner.n_gen.cpu().tolist())
+
 
 def _prepare(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor], video_token_id: int):
     ids = inputs["input_ids"]
@@ -741,18 +969,14 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
     elif runner.verify_mode != verify_mode:
         raise ValueError("the runner was built for a different verify_mode")
     tp = runner.prefill(embeds, with_selection=True)
-    dec = runner.run_std()
+    prof = None
+    if profile_decode and runner.shard is None:
+        prof = runner.run_std_profiled()
+        dec = prof["decoding_time"]
+    else:
+        dec = runner.run_std()
     torch.cuda.synchronize()
-    gen = runner.generated()
-    out = torch.cat([ids.cpu().long(), gen], dim=1) if ids.shape[0] == gen.shape[0] else gen
-    st = runner.std_stats()
-    acc = st["accept_lengths"][0]
-    result = GenerateResult(
-        output_ids=out, decoding_time=dec, inference_time=time.time() - t0, generate_len=int(runner.n_gen.sum().item()),
-        accepted_draft_tokens=int(sum(st["accepted"])), proposed_draft_tokens=int(sum(st["proposed"])),
-        mean_accept_length=(sum(acc) / len(acc)) if acc else 0.0, decode_rounds=int(max(st["rounds"])),
-        final_gamma=gamma, accept_lengths=acc, prefill_time=tp["prefill_time"], selection_time=tp["selection_time"],
-        sparse_cache_time=tp["sparse_cache_time"])
+    result = _std_result(runner, ids, dec, t0, tp, gamma, prof)
     topk0 = runner.topk_per_request[0].cpu().long()
     selection = SparseSelection(topk_positions=[topk0[l] for l in range(topk0.shape[0])],
                                 non_visual_positions=layout.non_visual.cpu().long(), prompt_len=layout.prompt_len,
@@ -802,16 +1026,7 @@ def dynamic_std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torc
     tp = runner.prefill(embeds, with_selection=True)
     dec = runner.run_std()
     torch.cuda.synchronize()
-    gen = runner.generated()
-    out = torch.cat([ids.cpu().long(), gen], dim=1) if ids.shape[0] == gen.shape[0] else gen
-    st = runner.std_stats()
-    acc = st["accept_lengths"][0]
-    result = GenerateResult(
-        output_ids=out, decoding_time=dec, inference_time=time.time() - t0, generate_len=int(runner.n_gen.sum().item()),
-        accepted_draft_tokens=int(sum(st["accepted"])), proposed_draft_tokens=int(sum(st["proposed"])),
-        mean_accept_length=(sum(acc) / len(acc)) if acc else 0.0, decode_rounds=int(max(st["rounds"])),
-        final_gamma=gamma, accept_lengths=acc, prefill_time=tp["prefill_time"], selection_time=tp["selection_time"],
-        sparse_cache_time=tp["sparse_cache_time"])
+    result = _std_result(runner, ids, dec, t0, tp, gamma)
     topk0 = runner.topk_cur[:, 0].cpu().long()
     selection = SparseSelection(topk_positions=[topk0[l] for l in range(topk0.shape[0])],
                                 non_visual_positions=layout.non_visual.cpu().long(), prompt_len=layout.prompt_len,

@@ -300,3 +300,77 @@ def test_benchmark_cli_tiny(tmp_path):
     recs = [json.loads(l) for l in out.read_text().splitlines()]
     assert len(recs) == 2 and all(r["token_equal"] and r["std_generate_len"] == 12 for r in recs)
     assert recs[0]["prompt_len"] == 512 + 16 and recs[0]["k"] == 96 - 16
+
+
+def test_device_loop_matches_host_loop_and_profiled_rounds():
+    """The decode loop inside one CUDA graph (WHILE node, condition set on the
+    device) gives the same tokens and round records as the host-driven loop
+    and as the per-phase profiled loop; the profiled phase times add up."""
+    from std_b200 import ops
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import STDRunner, _prepare, selection_budget
+
+    model = Qwen25VLDecoder(TINY, seed=6)
+    B, V, T = 3, 500, 24
+    inp = _inputs(B, V, T, TINY.vocab_size, TINY.hidden_size, seed=31)
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    k = selection_budget(layout.prompt_len, layout.text_start, V, 120, None)
+    eos = int(ids[0, -1])
+    out = {}
+    for loop in (True, False):
+        runner = STDRunner(model, B, layout, 30, gamma=5, k=k, eos_token_id=eos, device_loop=loop)
+        runner.prefill(embeds)
+        runner.run_std()
+        out[loop] = (runner.out_tokens.cpu().clone(), runner.n_gen.cpu().clone(), runner.std_stats())
+        if loop:
+            lc = runner.launch_counts("std_loop")
+            assert lc["body_ours"] > 0 and lc["outer_ours"] > lc["body_ours"]
+            runner.run_ar()
+            ar = (runner.out_tokens.cpu().clone(), runner.n_gen.cpu().clone())
+            prof = runner.run_std_profiled()
+            out["prof"] = (runner.out_tokens.cpu().clone(), runner.n_gen.cpu().clone(), runner.std_stats())
+            parts = prof["draft_time"] + prof["verify_time"] + prof["cache_adjust_time"] + prof["bonus_time"]
+            assert 0 < parts <= prof["decoding_time"] * 1.001
+            assert prof["draft_time"] > 0 and prof["verify_time"] > 0
+    assert ops.device_error() == 0
+    for key in (False, "prof"):
+        assert torch.equal(out[True][0], out[key][0]) and torch.equal(out[True][1], out[key][1])
+        assert out[True][2] == out[key][2]
+    assert torch.equal(out[True][1], ar[1])
+    for b in range(B):
+        n = int(ar[1][b])
+        assert out[True][0][b, :n].tolist() == ar[0][b, :n].tolist()
+
+
+def test_batch_result_metrics_cover_every_request():
+    """GenerateResult of a batch: accept_lengths concatenates every request's
+    rounds, mean_accept_length averages over all of them, and the per-round
+    proposed / pending lists follow the reference's bookkeeping."""
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import std_generate_qwen25vl
+
+    model = Qwen25VLDecoder(TINY, seed=7)
+    B, max_new, gamma = 3, 20, 4
+    inp = _inputs(B, 400, 20, TINY.vocab_size, TINY.hidden_size, seed=41)
+    res, _ = std_generate_qwen25vl(model, inp, video_token_id=VIDEO, eos_token_id=-1, max_new_tokens=max_new,
+                                   gamma=gamma, target_k_plus_text=100, ignore_eos=True, profile_decode=True)
+    per = res.request_accept_lengths
+    assert len(per) == B
+    assert res.accept_lengths == [a for r in per for a in r]
+    assert res.accepted_draft_tokens == sum(res.accept_lengths)
+    assert abs(res.mean_accept_length - sum(res.accept_lengths) / len(res.accept_lengths)) < 1e-12
+    assert res.decode_rounds == max(len(r) for r in per)
+    assert res.generate_len == B * max_new and res.request_generate_lens == [max_new] * B
+    assert len(res.proposed_lengths) == len(res.pending_lengths) == len(res.accept_lengths)
+    off = 0
+    for r in per:
+        props = res.proposed_lengths[off:off + len(r)]
+        assert res.pending_lengths[off:off + len(r)] == [0] + [1] * (len(r) - 1)
+        n = 0
+        for a, p in zip(r, props):
+            assert p == min(gamma, max_new - n) and a <= p
+            n += min(a + 1, max_new - n)
+        assert n == max_new
+        off += len(r)
+    assert res.proposed_draft_tokens == sum(res.proposed_lengths)
+    assert res.draft_time > 0 and res.verify_time > 0 and res.bonus_time > 0
