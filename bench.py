@@ -402,7 +402,7 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
 
     # ---- launches of our kernels in the timed region, counted from the captured loop graph ----
     lc = runner.launch_counts("std_loop")
-    per_step = lc["outer_ours"] + (rounds_per_step - 1) * lc["body_ours"]
+    per_step = lc["outer"] + (rounds_per_step - 1) * lc["body"]
     gpu_launches = a.steps * per_step
 
     # ---- e2e through the public API, host buffers ----

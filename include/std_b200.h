@@ -269,10 +269,10 @@ int std_capture_while_begin(void* stream, void* body_stream, const int32_t* done
                             unsigned long long* handle_out, void** body_graph_out);
 int std_capture_while_end(void* body_stream, unsigned long long handle, const int32_t* done, int B, int32_t* counter,
                           int max_iters);
-/* Launch accounting for a captured cudaGraph_t (no reference counterpart):
- * counts[0] kernel nodes, counts[1] of them this library's.  Child graphs are
- * followed; conditional bodies are not (count a body graph on its own). */
-int std_graph_kernel_counts(void* graph, int* counts);
+/* Launch accounting (no reference counterpart): how many kernel launches
+ * this library has enqueued in this process so far, counting launches
+ * recorded into CUDA graphs under stream capture.  Host-side counter. */
+long long std_launch_count(void);
 
 #ifdef __cplusplus
 }

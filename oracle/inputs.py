@@ -49,6 +49,9 @@ class LayerCase:
 
 CONFIG0 = LayerCase("config0", V=8192, text=256, T=64, k_plus_text=1024)
 SMALL = LayerCase("small", V=512, text=32, T=16, k_plus_text=128)
+# configs[3] selection sizes for one layer: 131072 visual + 128 text keys,
+# 64 text query rows (the last prompt rows), K = 4096 - 128 = 3968
+CONFIG3_LAYER = LayerCase("config3", V=131072, text=128, T=64, k_plus_text=4096)
 
 
 def make_layer_inputs(case: LayerCase, seed: int = 0, Hq: int = 28, Hkv: int = 4, D: int = 128):

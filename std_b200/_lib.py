@@ -61,7 +61,7 @@ SIGNATURES: Dict[str, tuple] = {
     "std_ar_advance": (I, [I, PI32, PI32, PI32, I, PI32, PI32, P]),
     "std_capture_while_begin": (I, [P, P, PI32, I, PI32, P, P]),
     "std_capture_while_end": (I, [P, ctypes.c_ulonglong, PI32, I, PI32, I]),
-    "std_graph_kernel_counts": (I, [P, P]),
+    "std_launch_count": (I64, []),
 }
 
 _STATUS = {1: "bad shape or argument", 2: "capacity exceeded", 3: "unsupported device or driver entry point",

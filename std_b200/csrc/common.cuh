@@ -371,9 +371,16 @@ STD_DEV float warp_sum(float v) {
 // anything the stream wrote before it, so the result is that of a plain
 // stream-ordered launch, minus the launch gap.
 // ---------------------------------------------------------------------------
+// Host-side count of kernel launches this library has enqueued (including
+// launches recorded into a CUDA graph under stream capture): launch
+// accounting for callers, read with std_launch_count().
+static std::atomic<long long> g_std_launches{0};
+static inline void count_launch() { g_std_launches.fetch_add(1, std::memory_order_relaxed); }
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                               Args&&... args) {
+  count_launch();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;

@@ -65,6 +65,7 @@ extern "C" int std_capture_while_begin(void* stream, void* body_stream, const in
   cudaGraphConditionalHandle h;
   // default 0: if the init kernel never ran, the body does not run either
   if (cudaGraphConditionalHandleCreate(&h, graph, 0, cudaGraphCondAssignDefault) != cudaSuccess) return 4;
+  count_launch();
   stdb::loop_init_kernel<<<1, 32, 0, s>>>(h, done, B, counter);
   if (cudaGetLastError() != cudaSuccess) return 4;
   const cudaGraphNode_t* deps = nullptr;
@@ -91,6 +92,7 @@ extern "C" int std_capture_while_end(void* body_stream, unsigned long long handl
                                      int32_t* counter, int max_iters) {
   if (body_stream == nullptr || done == nullptr || counter == nullptr || B <= 0 || max_iters <= 0) return 1;
   cudaStream_t s = static_cast<cudaStream_t>(body_stream);
+  count_launch();
   stdb::loop_continue_kernel<<<1, 32, 0, s>>>(static_cast<cudaGraphConditionalHandle>(handle), done, B, counter,
                                                max_iters);
   const cudaError_t launch = cudaGetLastError();
@@ -99,43 +101,4 @@ extern "C" int std_capture_while_end(void* body_stream, unsigned long long handl
   return (launch == cudaSuccess && end == cudaSuccess) ? 0 : 4;
 }
 
-// ---------------------------------------------------------------------------
-// Launch accounting: kernel nodes of a captured graph, and how many of them
-// are this library's own kernels (namespace stdb).  Child graphs are followed;
-// conditional bodies are counted separately (std_capture_while_begin returns
-// the body graph), since they run once per loop iteration.
-// ---------------------------------------------------------------------------
-#include <cstring>
-#include <vector>
-
-static int count_graph_kernels(cudaGraph_t g, int* counts) {
-  size_t n = 0;
-  if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess) return 4;
-  std::vector<cudaGraphNode_t> nodes(n);
-  if (n > 0 && cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return 4;
-  for (cudaGraphNode_t node : nodes) {
-    cudaGraphNodeType t;
-    if (cudaGraphNodeGetType(node, &t) != cudaSuccess) return 4;
-    if (t == cudaGraphNodeTypeKernel) {
-      counts[0] += 1;
-      cudaKernelNodeParams kp = {};
-      const char* name = nullptr;
-      if (cudaGraphKernelNodeGetParams(node, &kp) == cudaSuccess && kp.func != nullptr &&
-          cudaFuncGetName(&name, kp.func) == cudaSuccess && name != nullptr && std::strncmp(name, "_ZN4stdb", 8) == 0)
-        counts[1] += 1;
-      cudaGetLastError();  // a foreign kernel may leave a lookup error behind
-    } else if (t == cudaGraphNodeTypeGraph) {
-      cudaGraph_t child = nullptr;
-      if (cudaGraphChildGraphNodeGetGraph(node, &child) != cudaSuccess) return 4;
-      const int rc = count_graph_kernels(child, counts);
-      if (rc != 0) return rc;
-    }
-  }
-  return 0;
-}
-
-extern "C" int std_graph_kernel_counts(void* graph, int* counts) {
-  if (graph == nullptr || counts == nullptr) return 1;
-  counts[0] = counts[1] = 0;
-  return count_graph_kernels(static_cast<cudaGraph_t>(graph), counts);
-}
+extern "C" long long std_launch_count(void) { return g_std_launches.load(std::memory_order_relaxed); }

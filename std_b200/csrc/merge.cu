@@ -39,6 +39,7 @@ __global__ void merge_partials_kernel(const __nv_bfloat16* o_parts, const float*
 extern "C" int std_merge_partials(const void* o_parts, const float* lse_parts, int n_parts, int rows, int D, void* out,
                                   float* lse_out, void* stream) {
   if (n_parts <= 0 || rows <= 0 || D <= 0) return 1;
+  count_launch();
   stdb::merge_partials_kernel<<<(rows * 32 + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(o_parts), lse_parts, n_parts, rows, D, static_cast<__nv_bfloat16*>(out),
       lse_out);

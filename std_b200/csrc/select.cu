@@ -345,10 +345,13 @@ extern "C" int std_select_scores(const void* q_text, const void* k_cache, long l
   lp.logits = logits;
   const int G = Hq / Hkv;
   dim3 g1((P + stdb::SL_KT - 1) / stdb::SL_KT, (G * T + stdb::SL_RT - 1) / stdb::SL_RT, Hkv);
+  count_launch();
   stdb::select_logits_kernel<<<g1, 256, 0, s>>>(lp);
+  count_launch();
   stdb::select_row_stats_kernel<<<(static_cast<unsigned>(rows) * 32 + 255) / 256, 256, 0, s>>>(logits, rows, P,
                                                                                               pstride, row_m, row_l);
   dim3 g3((P + 255) / 256, Hkv);
+  count_launch();
   stdb::select_colsum_kernel<<<g3, 256, 0, s>>>(logits, row_m, row_l, T, Hq, Hkv, P, pstride, scores, write_probs);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }
@@ -362,6 +365,7 @@ extern "C" int std_select_probs_view(int T, int Hq, int P, long long* pstride_ou
 extern "C" int std_topk_select(const float* scores, long long seg_stride, int n_seg, const int32_t* visual_pos, int V,
                                int K, int32_t* out, void* stream) {
   if (n_seg <= 0 || V <= 0 || K <= 0 || K > V || scores == nullptr || visual_pos == nullptr || out == nullptr) return 1;
+  count_launch();
   stdb::topk_lowest_kernel<<<n_seg, stdb::TK_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(scores, seg_stride,
                                                                                              visual_pos, V, K, out);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
@@ -388,6 +392,7 @@ extern "C" int std_compact_gather(const void* dense_cache, void* sparse_cache, i
   p.layers = layers;
   const int n = NV + K;
   dim3 grid((n * 32 + 255) / 256, Hkv, layers);
+  count_launch();
   stdb::compact_gather_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

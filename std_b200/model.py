@@ -260,6 +260,8 @@ def prefill_segment(model: Qwen25VLDecoder, cache: torch.Tensor, b: int, x: torc
         if selection is not None:
             sc, probs = ops.select_scores(q, cache[li, 0, b], L, start, scores=selection["scores"][li],
                                           write_probs=True)
+            if selection.get("observe") is not None:  # (layer, post-RoPE text queries, K rows, keys, first query pos)
+                selection["observe"](li, q, cache[li, 0, b], L, start)
             G = Hq // Hkv
             attn = torch.empty(S, Hq, D, device=dev, dtype=model.dtype)
             for kv in range(Hkv):
@@ -291,19 +293,22 @@ def prefill_segment(model: Qwen25VLDecoder, cache: torch.Tensor, b: int, x: torc
 
 
 def prefill_request(model: Qwen25VLDecoder, cache: torch.Tensor, b: int, embeds: torch.Tensor, text_start: int,
-                    scores_out: Optional[torch.Tensor] = None) -> int:
+                    scores_out: Optional[torch.Tensor] = None, observe=None) -> int:
     """Two-stage prefill of one request (std_qwen25vl.py:670-707).
 
     1. video prefix rows [0, text_start) -> cache;
     2. if scores_out [layers, Hkv, P] is given: the selection branch over the
        text suffix (its K/V are written to the cache and then overwritten);
     3. the dense branch over the text suffix (the canonical verifier KV).
+    observe(layer, q_text, k_rows, P, q_start), if given, sees each layer's
+    selection inputs right after its scores are computed (for parity checks).
     Returns the prefill's greedy next token (dense_next).
     """
     P = embeds.shape[0]
     prefill_segment(model, cache, b, embeds[:text_start].clone(), 0)
     if scores_out is not None:
-        prefill_segment(model, cache, b, embeds[text_start:].clone(), text_start, selection={"scores": scores_out})
+        prefill_segment(model, cache, b, embeds[text_start:].clone(), text_start,
+                        selection={"scores": scores_out, "observe": observe})
     last = prefill_segment(model, cache, b, embeds[text_start:].clone(), text_start)
     logits = last @ model.lm_head.t()
     out = torch.empty(1, dtype=torch.int32, device=model.device)

@@ -313,7 +313,7 @@ class STDRunner:
         self.topk_per_request: List[torch.Tensor] = []
         self._graphs: Dict[str, torch.cuda.CUDAGraph] = {}
         self.loop_counter = torch.zeros(1, **i32)
-        self._loop_bodies: Dict[str, int] = {}
+        self._loop_launches: Dict[str, Dict[str, int]] = {}
         self._body_stream: Optional[torch.cuda.Stream] = None
         # decode loops as one graph each (a WHILE node around a round / AR
         # step): no host round trip between rounds.  The host-driven loop
@@ -336,8 +336,11 @@ class STDRunner:
         return _round_up(prompt_len + max_new_tokens + gamma + 2, 128)
 
     # ------------------------------------------------------------------ prefill
-    def prefill(self, embeds: Sequence[torch.Tensor], with_selection: bool = True) -> Dict[str, float]:
-        """Prefill every request (embeds[b]: [P, H] bf16) and, for STD, select and compact."""
+    def prefill(self, embeds: Sequence[torch.Tensor], with_selection: bool = True, observe=None) -> Dict[str, float]:
+        """Prefill every request (embeds[b]: [P, H] bf16) and, for STD, select and compact.
+
+        observe(b, layer, q_text, k_rows, P, q_start, scores) sees every
+        layer's selection inputs and scores (parity checks)."""
         c = self.model.config
         L, Hkv, P = c.num_hidden_layers, c.num_key_value_heads, self.layout.prompt_len
         t = {"prefill_time": 0.0, "selection_time": 0.0, "sparse_cache_time": 0.0}
@@ -349,7 +352,10 @@ class STDRunner:
         for b in range(self.B):
             torch.cuda.synchronize()
             t0 = time.time()
-            dn.append(prefill_request(self.model, full, b, embeds[b], self.layout.text_start, scores))
+            obs = None
+            if observe is not None and with_selection:
+                obs = (lambda li, q, k, P_, s0, b=b: observe(b, li, q, k, P_, s0, scores[li]))
+            dn.append(prefill_request(self.model, full, b, embeds[b], self.layout.text_start, scores, obs))
             torch.cuda.synchronize()
             t1 = time.time()
             t["prefill_time"] += t1 - t0
@@ -607,14 +613,18 @@ class STDRunner:
         body_stream = self._body_stream
         limit = self.max_new + 1
 
+        def launches() -> int:
+            return int(_lib.query("std_launch_count"))
+
         def loop(body) -> None:
             h = ctypes.c_ulonglong(0)
-            bg = ctypes.c_void_p(0)
+            counts["outer"] = launches() - counts["start"] + 1  # + the loop's init kernel
             _lib.call("std_capture_while_begin", torch.cuda.current_stream().cuda_stream, body_stream.cuda_stream,
-                      self.done.data_ptr(), self.B, self.loop_counter.data_ptr(), ctypes.byref(h), ctypes.byref(bg))
-            bodies.append(bg.value)
+                      self.done.data_ptr(), self.B, self.loop_counter.data_ptr(), ctypes.byref(h), None)
+            n0 = launches()
             with torch.cuda.stream(body_stream):
                 body()
+            counts["body"] = launches() - n0 + 1  # + the loop's condition update
             _lib.call("std_capture_while_end", body_stream.cuda_stream, h.value, self.done.data_ptr(), self.B,
                       self.loop_counter.data_ptr(), limit)
 
@@ -628,29 +638,20 @@ class STDRunner:
                 continue
             self.reset()
             torch.cuda.synchronize()
-            bodies: List[int] = []
-            g = torch.cuda.CUDAGraph(keep_graph=True)  # kept for launch accounting (launch_counts)
+            counts = {"start": launches()}
+            g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
-            g.instantiate()
             self._graphs[name] = g
-            self._loop_bodies[name] = bodies[0]
+            self._loop_launches[name] = {"outer": counts["outer"], "body": counts["body"]}
 
     def launch_counts(self, name: str) -> Dict[str, int]:
-        """Kernel launches of one replay of loop graph `name` ("std_loop" /
-        "ar_loop"): once-per-decode kernels outside the loop body and
-        per-iteration kernels in the body, counted from the captured graph
-        nodes; "*_ours" are this library's kernels."""
-        import ctypes
-
-        from . import _lib
-
-        out = {}
-        for part, graph in (("outer", self._graphs[name].raw_cuda_graph()), ("body", self._loop_bodies[name])):
-            c = (ctypes.c_int * 2)()
-            _lib.call("std_graph_kernel_counts", ctypes.c_void_p(graph), c)
-            out[part], out[part + "_ours"] = int(c[0]), int(c[1])
-        return out
+        """This library's kernel launches in one replay of loop graph `name`
+        ("std_loop" / "ar_loop"): "outer" run once per decode (round 1 and the
+        loop's init kernel), "body" once per loop iteration (a round or an AR
+        step, and the condition update).  Counted from the library's launch
+        counter while the graph was captured."""
+        return dict(self._loop_launches[name])
 
     def _all_done(self) -> bool:
         self.all_done_host.copy_(self.all_done, non_blocking=True)

@@ -192,6 +192,57 @@ def test_select_scores_bit_exact_and_topk(ops, case):
     _no_device_error(ops)
 
 
+@pytest.mark.parametrize("seed", [1, 2])
+def test_select_config0_other_seeds_bit_exact(ops, seed):
+    """configs[0] selection with two more input seeds: scores bit-exact against
+    the oracle, top-K equal to the oracle's and to the reference's sets."""
+    case = CONFIG0
+    inp = make_layer_inputs(case, seed)
+    qb = bf16_bits(inp["q_text"][0].permute(1, 0, 2).contiguous())
+    kb = bf16_bits(inp["k"][0])
+    ref_scores = oracle.select_scores(qb, kb, case.q_start, case.P)
+    q = torch.from_numpy(qb.view(np.int16)).view(torch.bfloat16).cuda()
+    k = torch.from_numpy(kb.view(np.int16)).view(torch.bfloat16).cuda()
+    scores = ops.select_scores(q, k, case.P, case.q_start)
+    got = scores.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref_scores.view(np.uint32))
+    topk = ops.topk_select(scores, torch.arange(case.V, dtype=torch.int32, device="cuda"), case.k).cpu().numpy()
+    assert np.array_equal(topk, oracle.topk_lowest(ref_scores, np.arange(case.V, dtype=np.int32), case.k))
+    gl = np.load(os.path.join(GOLDEN, f"selection_config0_seed{seed}.npz"))
+    for h in range(4):
+        assert set(topk[h].tolist()) == set(gl["ref_topk"][h].tolist())
+    _no_device_error(ops)
+
+
+def test_select_config3_sizes_bit_exact(ops):
+    """configs[3] selection sizes (131072 visual + 128 text keys, 64 query rows,
+    K = 3968): scores bit-exact against the oracle and top-K equal to the
+    oracle's lowest-index selection, including the exact fp32 ties at the K-th
+    score that this length produces."""
+    from oracle.inputs import CONFIG3_LAYER as case
+
+    inp = make_layer_inputs(case, 0)
+    qb = bf16_bits(inp["q_text"][0].permute(1, 0, 2).contiguous())
+    kb = bf16_bits(inp["k"][0])
+    del inp
+    ref_scores = oracle.select_scores(qb, kb, case.q_start, case.P)
+    q = torch.from_numpy(qb.view(np.int16)).view(torch.bfloat16).cuda()
+    k = torch.from_numpy(kb.view(np.int16)).view(torch.bfloat16).cuda()
+    scores = ops.select_scores(q, k, case.P, case.q_start)
+    got = scores.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref_scores.view(np.uint32)), f"{(got != ref_scores).sum()} differ"
+    topk = ops.topk_select(scores, torch.arange(case.V, dtype=torch.int32, device="cuda"), case.k).cpu().numpy()
+    ref_topk = oracle.topk_lowest(ref_scores, np.arange(case.V, dtype=np.int32), case.k)
+    assert np.array_equal(topk, ref_topk)
+    for h in range(4):  # the boundary holds an exact tie on some head: the tie rule is exercised
+        kth = np.sort(ref_scores[h, : case.V])[::-1][case.k - 1]
+        if (ref_scores[h, : case.V] == kth).sum() > 1:
+            break
+    else:
+        pytest.fail("expected an exact tie at the K-th score on some head")
+    _no_device_error(ops)
+
+
 def test_select_probs_written(ops):
     case = SMALL
     inp = make_layer_inputs(case, 0)

@@ -143,3 +143,68 @@ def test_accept_round_edge_cases():
     a, bonus, app, fin = oracle.accept_round([4, 8], [3, 1], 5, False, 10, eos_token_id=2, ignore_eos=True)
     assert (a, bonus, app) == (0, 5, [5])
     assert oracle.rollback_lengths(100, 1, 50, 3) == (104, 53)
+
+
+@pytest.mark.parametrize("seed", [1, 2])
+def test_selection_matches_reference_other_seeds(seed):
+    """configs[0]-shaped selection with two more input seeds: the oracle's top-K
+    sets equal the reference's on every head."""
+    g = np.load(os.path.join(GOLDEN, f"selection_config0_seed{seed}.npz"))
+    inp = make_layer_inputs(CONFIG0, seed)
+    qb = bf16_bits(inp["q_text"][0].permute(1, 0, 2).contiguous())
+    kb = bf16_bits(inp["k"][0])
+    assert digest(qb) == str(g["q_digest"]) and digest(kb) == str(g["k_digest"]), "input RNG drifted"
+    scores = oracle.select_scores(qb, kb, CONFIG0.q_start, CONFIG0.P)
+    ref = g["ref_scores"]
+    assert np.abs(scores - ref).max() <= 1e-3 * np.abs(ref).max()
+    assert (scores == ref).mean() > 0.85
+    k = int(g["k"])
+    topk = oracle.topk_lowest(scores, np.arange(CONFIG0.V, dtype=np.int32), k)
+    for h in range(topk.shape[0]):
+        assert set(topk[h].tolist()) == set(g["ref_topk"][h].tolist())
+    # the reference's own boundary is not a tie: its K-th score is unique
+    assert np.all(g["tie_equal_to_kth"] == 1)
+
+
+def test_selection_matches_reference_config3_sizes():
+    """configs[3] sizes (131072 visual keys, K = 3968).  At this length the fp16
+    softmax probabilities are coarsely quantised, so the K-th score of every
+    head is an exact fp32 tie or a near tie.  The reference fills the last
+    slots from such a tie class in torch.topk's own order, and its library
+    rounding (CPU matmul order, vectorised exp) moves a few scores by one or
+    two ulp relative to the restated chain.  Pinned here: the oracle's scores
+    agree with the reference's at the K + 256 best positions, every position
+    whose reference score is clearly above the boundary is selected by both,
+    and the sets differ only inside a 5e-5 relative band around the K-th
+    score (measured: 5 of 15872 selected positions, all of them there)."""
+    from oracle.inputs import CONFIG3_LAYER as case
+
+    g = np.load(os.path.join(GOLDEN, "selection_config3.npz"))
+    inp = make_layer_inputs(case, 0)
+    qb = bf16_bits(inp["q_text"][0].permute(1, 0, 2).contiguous())
+    kb = bf16_bits(inp["k"][0])
+    del inp
+    assert digest(qb) == str(g["q_digest"]) and digest(kb) == str(g["k_digest"]), "input RNG drifted"
+    scores = oracle.select_scores(qb, kb, case.q_start, case.P)
+    k = int(g["k"])
+    assert k == case.k == 3968
+    pos, ref = g["boundary_pos"].astype(np.int64), g["boundary_scores"]
+    mine = np.take_along_axis(scores, pos, axis=1)
+    assert np.abs(mine - ref).max() <= 1e-3 * np.abs(ref).max()
+    assert (mine == ref).mean() > 0.80
+    vis = scores[:, : case.V].astype(np.float64).sum(axis=1)
+    assert np.allclose(vis, g["score_sums"], rtol=1e-5)
+    topk = oracle.topk_lowest(scores, np.arange(case.V, dtype=np.int32), k)
+    band = 5e-5
+    n_diff = 0
+    for h in range(topk.shape[0]):
+        mine_set, ref_set = set(topk[h].tolist()), set(g["ref_topk"][h].tolist())
+        kth = float(g["tie_kth"][h])
+        ref_score = dict(zip(pos[h].tolist(), ref[h].tolist()))
+        clearly_above = {p for p, v in ref_score.items() if v > kth * (1 + band)}
+        assert clearly_above <= mine_set and clearly_above <= ref_set
+        diff = mine_set ^ ref_set
+        n_diff += len(diff)
+        for p in diff:
+            assert p in ref_score and abs(ref_score[p] - kth) <= band * kth, (h, p)
+    assert n_diff <= 16  # a handful of boundary positions out of 4 x 3968
