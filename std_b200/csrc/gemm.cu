@@ -32,6 +32,17 @@ constexpr uint32_t GM_SMEM_BUDGET = 104 * 1024;  // per CTA: two CTAs per SM
 constexpr int GM_THREADS = 128;
 constexpr uint32_t GM_WTILE = GM_BM * GM_BK * 2;  // 16 KB
 
+// In-kernel epilogues that need the full K sum of a 128-feature tile.  With K
+// split over several CTAs, each CTA stores its fp32 partial and counts itself
+// in on the tile's arrival counter; the last CTA to arrive sums the partials
+// in split order (the order gemm_reduce_kernel uses) and applies the epilogue
+// for the whole tile.  No CTA waits for another.
+enum GemmFixup : int {
+  FIX_NONE = 0,
+  FIX_ROPE = 1,   // QKV projection: bias, RoPE of q/k heads, q -> q_out, k/v -> the cache slot (one head per tile)
+  FIX_RESID = 2,  // O / down projection: resid += y (bf16), and the tile's per-row sum of squares of the new resid
+};
+
 struct GemmParams {
   int M, N, K, nmma, splits, kblocks, stages;
   const __nv_bfloat16* bias;  // [N] or null
@@ -46,7 +57,144 @@ struct GemmParams {
   // rows 0..63 are gate, 64..127 up of features 64*tile ..; writes
   // act[t][64*tile + r] = bf16(bf16(silu(gate)) * up) instead of y
   __nv_bfloat16* act;
+  // RMSNorm prologue (norm_w != null): X is a residual stream and each staged
+  // X tile becomes bf16(norm_w[k] * bf16(x * inv[t])) before the MMA reads it,
+  // inv[t] = rsqrt(sum_i norm_sumsq[i * M + t] / K + eps), i < K / 128 (the
+  // per-tile sums of squares written by the producer of x)
+  const float* norm_sumsq;
+  const __nv_bfloat16* norm_w;
+  float norm_eps;
+  // split-K fixup (fixup != FIX_NONE)
+  int fixup;
+  int* tile_count;  // [tiles] arrival counters, zero between calls
+  RopeParams rope;  // FIX_ROPE: rows t < rope_rows are real tokens (t = b * rope.n + j)
+  int rope_rows;
+  __nv_bfloat16* resid;  // FIX_RESID: [M, N]
+  float* sumsq_out;      // FIX_RESID: [N / 128, M]
+  // dependents are released only after this grid's own wait (a following
+  // kernel that reads before its wait then sees every earlier kernel done)
+  int late_trigger;
 };
+
+// Sum of 128 per-thread values (one per thread of a 128-thread block, warp w
+// holding values 32w..32w+31): xor tree inside each warp, then the four warp
+// sums in order.  The fixed order makes a tile's sum of squares identical
+// wherever it is computed (GEMM fixup, embedding).
+STD_DEV float tile_sum128(float v, float* s_part4, int slot) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) s_part4[slot * 4 + (threadIdx.x >> 5)] = v;
+  return v;
+}
+STD_DEV float tile_sum128_finish(const float* s_part4, int slot) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(s_part4[slot * 4 + 0], s_part4[slot * 4 + 1]), s_part4[slot * 4 + 2]),
+                   s_part4[slot * 4 + 3]);
+}
+
+// RMSNorm of staged X rows in place: the 128B-swizzled [rows][64] bf16 tile at
+// `tile` holds columns k0..k0+63 of rows 0..nrows-1; rows >= M are left as
+// loaded (zero fill).  Threads [t0, t0 + nthr) share the work.
+STD_DEV void norm_x_tile(uint8_t* tile, int nrows, int M, int k0, const float* s_inv, const __nv_bfloat16* w,
+                         int t, int nthr) {
+  for (int i = t; i < nrows * 8; i += nthr) {
+    const int r = i >> 3, pc = i & 7;
+    if (r >= M) continue;
+    const int c = pc ^ (r & 7);  // logical 16-byte chunk: columns k0 + 8c .. +7
+    uint4* q = reinterpret_cast<uint4*>(tile + r * 128 + pc * 16);
+    float v[8], wv[8], y[8];
+    const uint4 u = *q;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+    load8(w + k0 + 8 * c, wv);
+    const float inv = s_inv[r];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(wv[j], bf16_round(__fmul_rn(v[j], inv)));
+    uint4 o;
+    o.x = pack_bf16x2(y[0], y[1]);
+    o.y = pack_bf16x2(y[2], y[3]);
+    o.z = pack_bf16x2(y[4], y[5]);
+    o.w = pack_bf16x2(y[6], y[7]);
+    *q = o;
+  }
+}
+
+// Apply a split-K fixup epilogue to the tile's bf16 results y[t] (t < M) of
+// feature f = n0 + thread.  `yv(t)` returns them; s_y (>= 32 x 128 bf16) and
+// s_part (>= 4 x 32 floats) are free shared memory.
+template <class YV>
+STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloat16* s_y, float* s_part) {
+  const int tid = threadIdx.x;
+  const int f = n0 + tid;
+  if (p.fixup == FIX_RESID) {
+    for (int t0 = 0; t0 < p.M; t0 += 32) {
+      const int nt = p.M - t0 < 32 ? p.M - t0 : 32;
+      for (int j = 0; j < nt; ++j) {
+        const int t = t0 + j;
+        float xn = 0.f;
+        if (f < p.N) {
+          __nv_bfloat16* xp = p.resid + static_cast<size_t>(t) * p.N + f;
+          xn = bf16_round(__fadd_rn(__bfloat162float(*xp), yv(t)));
+          *xp = __float2bfloat16_rn(xn);
+        }
+        tile_sum128(__fmul_rn(xn, xn), s_part, j);
+      }
+      __syncthreads();
+      if (tid < nt) p.sumsq_out[static_cast<size_t>(tile) * p.M + t0 + tid] = tile_sum128_finish(s_part, tid);
+      __syncthreads();
+    }
+    return;
+  }
+  // FIX_ROPE: one head per tile (D == 128); thread = dim d; rotate_half pairs d and d +- 64
+  const RopeParams& r = p.rope;
+  const int heads = r.Hq + 2 * r.Hkv;
+  if (tile >= heads) return;
+  const int d = tid, half = 64, c = d & 63;
+  for (int t0 = 0; t0 < p.rope_rows; t0 += 32) {
+    const int nt = p.rope_rows - t0 < 32 ? p.rope_rows - t0 : 32;
+    for (int j = 0; j < nt; ++j) s_y[j * 128 + d] = __float2bfloat16_rn(yv(t0 + j));
+    __syncthreads();
+    for (int j = 0; j < nt; ++j) {
+      const int row = t0 + j;
+      const int b = row / r.n, jj = row % r.n;
+      int pos = r.pos_base[b] + r.pos_off + jj;
+      const int slot = r.slot_base[b] + r.slot_off + jj;
+      const bool slot_ok = slot >= 0 && slot < r.cap;
+      if (pos < 0 || pos >= r.max_pos) {
+        if (d == 0) std_set_error(STD_DEVERR_BOUNDS);
+        pos = pos < 0 ? 0 : r.max_pos - 1;
+      }
+      if (!slot_ok && d == 0 && tile >= r.Hq) std_set_error(STD_DEVERR_LENGTH);
+      const float lo = __bfloat162float(s_y[j * 128 + c]);
+      const float hi = __bfloat162float(s_y[j * 128 + half + c]);
+      __nv_bfloat16* dst;
+      if (tile < r.Hq) {
+        dst = r.q_out + (static_cast<size_t>(row) * r.Hq + tile) * 128;
+      } else {
+        if (!slot_ok) continue;
+        const int hk = tile < r.Hq + r.Hkv ? tile - r.Hq : tile - r.Hq - r.Hkv;
+        dst = (tile < r.Hq + r.Hkv ? r.k_cache : r.v_cache) +
+              ((static_cast<size_t>(b) * r.Hkv + hk) * r.cap + slot) * 128;
+      }
+      float out;
+      if (tile >= r.Hq + r.Hkv) {
+        out = d < half ? lo : hi;  // v: no rotation
+      } else {
+        const float cs = __bfloat162float(r.cos_t[static_cast<size_t>(pos) * half + c]);
+        const float sn = __bfloat162float(r.sin_t[static_cast<size_t>(pos) * half + c]);
+        // q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16
+        out = d < half ? bf16_round(__fadd_rn(bf16_round(__fmul_rn(lo, cs)), bf16_round(__fmul_rn(-hi, sn))))
+                       : bf16_round(__fadd_rn(bf16_round(__fmul_rn(hi, cs)), bf16_round(__fmul_rn(lo, sn))));
+      }
+      dst[d] = __float2bfloat16_rn(out);
+    }
+    __syncthreads();
+  }
+}
 
 __global__ void __launch_bounds__(GM_THREADS)
     gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
@@ -58,14 +206,20 @@ __global__ void __launch_bounds__(GM_THREADS)
   const int nkb = kb1 - kb0;
   const int n0 = tile * GM_BM;
   const uint32_t xtile = static_cast<uint32_t>(p.nmma) * GM_BK * 2;
+  const bool norm = p.norm_w != nullptr;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.stages;
   uint8_t* sW = smem;                 // [S][16 KB]
   uint8_t* sX = smem + S * GM_WTILE;  // [S][xtile]
-  __shared__ __align__(8) uint64_t bar_full[GM_MAX_STAGES], bar_empty[GM_MAX_STAGES], bar_done;
+  __shared__ __align__(8) uint64_t bar_full[GM_MAX_STAGES], bar_empty[GM_MAX_STAGES], bar_xready[GM_MAX_STAGES],
+      bar_done;
   __shared__ uint32_t s_tmem;
+  __shared__ float s_inv[256];
+  __shared__ float s_part[4 * 32];
+  __shared__ int s_last;
+  __shared__ int s_norm_ok[2][2];
 
   uint32_t ncols = 32;
   while (ncols < static_cast<uint32_t>(p.nmma)) ncols <<= 1;
@@ -77,6 +231,7 @@ __global__ void __launch_bounds__(GM_THREADS)
     for (int i = 0; i < S; ++i) {
       mbar_init(&bar_full[i], 1);
       mbar_init(&bar_empty[i], 1);
+      mbar_init(&bar_xready[i], 1);
     }
     mbar_init(&bar_done, 1);
     fence_barrier_init();
@@ -90,8 +245,9 @@ __global__ void __launch_bounds__(GM_THREADS)
   // Every kernel that follows a GEMM reads its inputs after its own wait (or,
   // a GEMM, only weights before it): let it be scheduled now, so it is
   // resident when this one completes.  After the TMEM allocation, so a
-  // successor can never hold columns this CTA still needs.
-  pdl_launch_dependents();
+  // successor can never hold columns this CTA still needs.  With late_trigger
+  // the release waits for this grid's own predecessors (below).
+  if (!p.late_trigger) pdl_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
@@ -105,6 +261,7 @@ __global__ void __launch_bounds__(GM_THREADS)
       tma_load_2d_hint(sW + i * GM_WTILE, &tmW, &bar_full[i], (kb0 + i) * GM_BK, n0, stream_policy);
     }
     pdl_wait();
+    if (p.late_trigger) pdl_launch_dependents();
     for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * xtile, &tmX, &bar_full[i], (kb0 + i) * GM_BK, 0);
     int issued = pre;
     for (int i = pre; i < nkb; ++i) {
@@ -122,7 +279,7 @@ __global__ void __launch_bounds__(GM_THREADS)
     const uint32_t idesc = idesc_bf16_f32(GM_BM, p.nmma, 0, 0);
     for (int i = 0; i < nkb; ++i) {
       const int st = i % S;
-      if (!mbar_wait(&bar_full[st], (i / S) & 1)) break;
+      if (!mbar_wait(norm ? &bar_xready[st] : &bar_full[st], (i / S) & 1)) break;
       tc_fence_after();
       const uint32_t aW = smem_u32(sW + st * GM_WTILE), aX = smem_u32(sX + st * xtile);
 #pragma unroll
@@ -132,11 +289,42 @@ __global__ void __launch_bounds__(GM_THREADS)
       umma_commit(&bar_empty[st]);
     }
     umma_commit(&bar_done);
+  } else if (norm && warp >= 2) {
+    // ---- RMSNorm of the staged X tiles (warps 2-3) ----
+    const int t = tid - 64;
+    pdl_wait();
+    if (p.late_trigger) pdl_launch_dependents();
+    const int ntiles_in = p.K / GM_BM;
+    for (int r = t; r < p.nmma; r += 64) {
+      float inv = 0.f;
+      if (r < p.M) {
+        float ss = 0.f;
+        for (int i = 0; i < ntiles_in; ++i) ss = __fadd_rn(ss, __ldcg(&p.norm_sumsq[static_cast<size_t>(i) * p.M + r]));
+        inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.K)), p.norm_eps));
+      }
+      s_inv[r] = inv;
+    }
+    named_bar_sync(1, 64);
+    for (int i = 0; i < nkb; ++i) {
+      const int st = i % S;
+      // a timed-out wait must end the loop in both warps together (the named
+      // barrier counts 64 threads): vote per warp, then read both votes after
+      // the barrier (double-buffered, so a warp that runs ahead never
+      // overwrites a vote the other warp has yet to read)
+      const bool ok_w = __all_sync(0xffffffffu, mbar_wait(&bar_full[st], (i / S) & 1));
+      if (ok_w) norm_x_tile(sX + st * xtile, p.nmma, p.M, (kb0 + i) * GM_BK, s_inv, p.norm_w, t, 64);
+      fence_async_smem();
+      if (lane == 0) s_norm_ok[i & 1][warp - 2] = ok_w ? 1 : 0;
+      named_bar_sync(1, 64);
+      if (t == 0) mbar_arrive(&bar_xready[st]);
+      if (!(s_norm_ok[i & 1][0] && s_norm_ok[i & 1][1])) break;
+    }
   }
 
   // ---- epilogue: thread = output feature, columns = tokens ----
   mbar_wait(&bar_done, 0);
   pdl_wait();  // every thread: the previous kernel is complete before any store
+  if (p.late_trigger) pdl_launch_dependents();
   __syncwarp();
   tc_fence_after();
   const int f = n0 + warp * 32 + lane;
@@ -195,7 +383,24 @@ __global__ void __launch_bounds__(GM_THREADS)
       }
     }
   }
-  for (int t0 = 0; p.amax_keys == nullptr && p.act == nullptr && t0 < p.nmma; t0 += 32) {
+  const bool fused = p.fixup != FIX_NONE;
+  if (fused && p.splits == 1) {
+    // the whole K sum is in this CTA's TMEM: stage the tile's bf16 results in
+    // shared memory (token-major, [nmma][128]) and apply the fixup from there
+    __nv_bfloat16* s_res = reinterpret_cast<__nv_bfloat16*>(smem);
+    for (int t0 = 0; t0 < p.nmma; t0 += 32) {
+      uint32_t v[32];
+      tmem_ld32(trow + t0, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) s_res[(t0 + j) * 128 + tid] = __float2bfloat16_rn(__uint_as_float(v[j]) + bias);
+    }
+    __syncthreads();
+    gemm_fixup(p, tile, n0, [&](int t) { return __bfloat162float(s_res[t * 128 + tid]); },
+               reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(p.nmma) * 256), s_part);
+  }
+  for (int t0 = 0; p.amax_keys == nullptr && p.act == nullptr && !(fused && p.splits == 1) && t0 < p.nmma;
+       t0 += 32) {
     uint32_t v[32];
     tmem_ld32(trow + t0, v);
     tmem_wait_ld();
@@ -210,12 +415,67 @@ __global__ void __launch_bounds__(GM_THREADS)
         p.partial[(static_cast<size_t>(split) * p.M + t) * p.N + f] = acc;
     }
   }
+  if (fused && p.splits > 1) {
+    // count this CTA in; the last of the tile's splits applies the fixup
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int prev = atomicAdd(&p.tile_count[tile], 1);
+      s_last = prev == p.splits - 1;
+      if (s_last) p.tile_count[tile] = 0;  // every split has arrived: ready for the next call
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const float fb = (p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
+      const size_t MN = static_cast<size_t>(p.M) * p.N;
+      gemm_fixup(p, tile, n0,
+                 [&](int t) {
+                   if (f >= p.N) return 0.f;
+                   const float* pp = p.partial + static_cast<size_t>(t) * p.N + f;
+                   float a = __ldcg(pp);
+                   for (int s2 = 1; s2 < p.splits; ++s2) a += __ldcg(pp + s2 * MN);
+                   return bf16_round(a + fb);
+                 },
+                 reinterpret_cast<__nv_bfloat16*>(smem), s_part);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, ncols);
+  }
+}
+
+// Embedding rows for a decode forward, with each 128-column tile's sum of
+// squares per row (sumsq [H/128, ld]) for the RMSNorm prologue of the first
+// projection: out[b*n + j] = table[tok[b*tok_stride + tok_start + j]].
+__global__ void __launch_bounds__(128) embed_sumsq_kernel(const __nv_bfloat16* table, int vocab, int H,
+                                                          const int32_t* tok, int tok_stride, int tok_start, int n,
+                                                          __nv_bfloat16* out, float* sumsq, int ld) {
+  __shared__ float s_part[4];
+  pdl_launch_dependents();  // followed by a GEMM, which reads this only after its own wait
+  pdl_wait();
+  const int row = blockIdx.x;
+  const int b = row / n, j = row % n;
+  int id = tok[b * tok_stride + tok_start + j];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) std_set_error(STD_DEVERR_BOUNDS);
+    id = 0;
+  }
+  const __nv_bfloat16* src = table + static_cast<size_t>(id) * H;
+  __nv_bfloat16* dst = out + static_cast<size_t>(row) * H;
+  for (int t = 0; t < H / GM_BM; ++t) {
+    const int c = t * GM_BM + threadIdx.x;
+    const __nv_bfloat16 v = src[c];
+    dst[c] = v;
+    const float x = __bfloat162float(v);
+    tile_sum128(__fmul_rn(x, x), s_part, 0);
+    __syncthreads();
+    if (threadIdx.x == 0) sumsq[static_cast<size_t>(t) * ld + row] = tile_sum128_finish(s_part, 0);
+    __syncthreads();
   }
 }
 
@@ -339,13 +599,33 @@ extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
 
 // Launch gemm_kernel: with splits > 1 it writes fp32 partials to `partial`,
 // otherwise bf16 y (+ bias).  Shapes are checked by the callers.
+// Fields of an in-kernel epilogue / prologue (norm, fixup) for gemm_launch.
+struct GemmExtra {
+  const float* norm_sumsq = nullptr;
+  const void* norm_w = nullptr;
+  float norm_eps = 0.f;
+  int fixup = stdb::FIX_NONE;
+  int* tile_count = nullptr;
+  stdb::RopeParams rope = {};
+  int rope_rows = 0;
+  void* resid = nullptr;
+  float* sumsq_out = nullptr;
+  int late_trigger = 0;
+};
+
 static int gemm_launch(const void* x, const void* w, const void* bias, void* y, float* partial, int M, int N, int K,
                        int splits, cudaStream_t s, unsigned long long* amax_keys = nullptr, int amax_rows = 0,
-                       void* act = nullptr) {
+                       void* act = nullptr, const GemmExtra* ext = nullptr) {
   const int nmma = gemm_nmma(M);
   const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
   int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
   stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
+  // a fused fixup stages the tile's results ([nmma][128] bf16) and a 32-row
+  // RoPE exchange buffer in the (then idle) stage buffers
+  const uint32_t fix_bytes = static_cast<uint32_t>(nmma) * 256u + 32u * 256u;
+  while (ext != nullptr && ext->fixup != stdb::FIX_NONE && static_cast<uint32_t>(stages) * stage_bytes < fix_bytes)
+    ++stages;
+  if (stages > stdb::GM_MAX_STAGES) return 1;
   const size_t smem = static_cast<size_t>(stages) * stage_bytes + 1024;
   static SmemGrant grant;
   if (ensure_smem(stdb::gemm_kernel, grant, smem) != 0) return 3;
@@ -370,6 +650,18 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   p.amax_keys = amax_keys;
   p.amax_rows = amax_rows;
   p.act = static_cast<__nv_bfloat16*>(act);
+  const GemmExtra none;
+  const GemmExtra& e = ext != nullptr ? *ext : none;
+  p.norm_sumsq = e.norm_sumsq;
+  p.norm_w = static_cast<const __nv_bfloat16*>(e.norm_w);
+  p.norm_eps = e.norm_eps;
+  p.fixup = e.fixup;
+  p.tile_count = e.tile_count;
+  p.rope = e.rope;
+  p.rope_rows = e.rope_rows;
+  p.resid = static_cast<__nv_bfloat16*>(e.resid);
+  p.sumsq_out = e.sumsq_out;
+  p.late_trigger = e.late_trigger;
   // may begin while the previous kernel in the stream finishes: the weight
   // tiles of the first stages are requested before griddepcontrol.wait
   return launch_pdl(stdb::gemm_kernel, dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits), dim3(stdb::GM_THREADS),
@@ -520,6 +812,154 @@ extern "C" int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int
   return launch_pdl(stdb::silu_mul_kernel<stdb::GemmOut>, dim3(blocks), dim3(256), 0, s,
                     gemm_out_view(workspace, nullptr, splits, M, N), I, 1, total8,
                     static_cast<__nv_bfloat16*>(act)) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+// ---------------------------------------------------------------------------
+// Decode-layer GEMMs with their neighbours folded in (one launch each):
+// the RMSNorm in front of a projection runs on the staged X tiles, and the
+// split-K reduction with the op after a projection runs in the last CTA of
+// each 128-feature tile.  Workspace: [tile counters | split partials]; the
+// counters must be zero before the first call (zero the buffer once) and
+// every call leaves them zero.
+// ---------------------------------------------------------------------------
+static constexpr size_t kCountersBytes = 4096;  // up to 1024 tiles (N <= 131072)
+
+extern "C" size_t std_gemm_fused_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return kCountersBytes + std_gemm_workspace_bytes(M, N, K);
+}
+
+static bool fused_ws_ok(void* workspace, size_t workspace_bytes, int M, int N, int K) {
+  return workspace != nullptr && workspace_bytes >= std_gemm_fused_workspace_bytes(M, N, K) &&
+         (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 && (N + stdb::GM_BM - 1) / stdb::GM_BM <= 1024;
+}
+
+static bool norm_ok(const float* sumsq, const void* norm_w, int K) {
+  return sumsq != nullptr && norm_w != nullptr && K % stdb::GM_BM == 0;
+}
+
+extern "C" int std_embed_sumsq(const void* table, int vocab, int H, const int32_t* tok, int tok_stride, int tok_start,
+                               int n, int B, void* out, float* sumsq, int ld, void* stream) {
+  if (table == nullptr || tok == nullptr || out == nullptr || sumsq == nullptr || vocab <= 0 || H <= 0 ||
+      H % stdb::GM_BM != 0 || n <= 0 || B <= 0 || ld < B * n)
+    return 1;
+  return launch_pdl(stdb::embed_sumsq_kernel, dim3(B * n), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                    static_cast<const __nv_bfloat16*>(table), vocab, H, tok, tok_stride, tok_start, n,
+                    static_cast<__nv_bfloat16*>(out), sumsq, ld) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+extern "C" int std_gemm_norm_rope_append(const void* x, const float* sumsq, const void* norm_w, float eps,
+                                         const void* w, const void* bias, int M, int K, int B, int n, int Hq, int Hkv,
+                                         int D, const int32_t* pos_base, int pos_off, const int32_t* slot_base,
+                                         int slot_off, const void* cos_t, const void* sin_t, int max_pos, void* q_out,
+                                         void* k_cache, void* v_cache, int cap, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  const int N = (Hq + 2 * Hkv) * D;
+  if (D != stdb::GM_BM || B <= 0 || n <= 0 || B * n > M || cap <= 0 || max_pos <= 0) return 1;
+  if (!gemm_shape_ok(x, w, M, N, K, 8) || !norm_ok(sumsq, norm_w, K)) return 1;
+  if (q_out == nullptr || k_cache == nullptr || v_cache == nullptr || pos_base == nullptr || slot_base == nullptr ||
+      cos_t == nullptr || sin_t == nullptr)
+    return 1;
+  if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
+  GemmExtra e;
+  e.norm_sumsq = sumsq;
+  e.norm_w = norm_w;
+  e.norm_eps = eps;
+  e.fixup = stdb::FIX_ROPE;
+  e.tile_count = static_cast<int*>(workspace);
+  e.rope.n = n;
+  e.rope.Hq = Hq;
+  e.rope.Hkv = Hkv;
+  e.rope.D = D;
+  e.rope.cap = cap;
+  e.rope.max_pos = max_pos;
+  e.rope.pos_base = pos_base;
+  e.rope.pos_off = pos_off;
+  e.rope.slot_base = slot_base;
+  e.rope.slot_off = slot_off;
+  e.rope.cos_t = static_cast<const __nv_bfloat16*>(cos_t);
+  e.rope.sin_t = static_cast<const __nv_bfloat16*>(sin_t);
+  e.rope.q_out = static_cast<__nv_bfloat16*>(q_out);
+  e.rope.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  e.rope.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  e.rope_rows = B * n;
+  // the draft kernel that follows reads older K/V rows and the lengths before
+  // its own wait: release it only once this grid's predecessors are done
+  e.late_trigger = 1;
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
+  return gemm_launch(x, w, bias, nullptr, partial, M, N, K, gemm_splits(N, K), static_cast<cudaStream_t>(stream),
+                     nullptr, 0, nullptr, &e);
+}
+
+extern "C" int std_gemm_residual(const void* a, const void* w, const void* bias, void* resid, float* sumsq_out, int M,
+                                 int N, int K, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!gemm_shape_ok(a, w, M, N, K, stdb::GM_BM) || resid == nullptr || sumsq_out == nullptr) return 1;
+  if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
+  GemmExtra e;
+  e.fixup = stdb::FIX_RESID;
+  e.tile_count = static_cast<int*>(workspace);
+  e.resid = resid;
+  e.sumsq_out = sumsq_out;
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
+  return gemm_launch(a, w, bias, nullptr, partial, M, N, K, gemm_splits(N, K), static_cast<cudaStream_t>(stream),
+                     nullptr, 0, nullptr, &e);
+}
+
+extern "C" int std_gemm_norm_silu_mul(const void* x, const float* sumsq, const void* norm_w, float eps,
+                                      const void* w, int M, int I, int K, void* act, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  const int N = 2 * I;
+  if (!gemm_shape_ok(x, w, M, N, K, 8) || act == nullptr || I % 64 != 0 || !norm_ok(sumsq, norm_w, K)) return 1;
+  GemmExtra e;
+  e.norm_sumsq = sumsq;
+  e.norm_w = norm_w;
+  e.norm_eps = eps;
+  const int splits = gemm_splits(N, K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (splits == 1) return gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, nullptr, 0, act, &e);
+  if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
+  int rc = gemm_launch(x, w, nullptr, partial, partial, M, N, K, splits, s, nullptr, 0, nullptr, &e);
+  if (rc != 0) return rc;
+  const size_t total8 = static_cast<size_t>(M) * I / 8;
+  const int blocks = static_cast<int>((total8 + 255) / 256 < 148 * 8 ? (total8 + 255) / 256 : 148 * 8);
+  return launch_pdl(stdb::silu_mul_kernel<stdb::GemmOut>, dim3(blocks), dim3(256), 0, s,
+                    gemm_out_view(partial, nullptr, splits, M, N), I, 1, total8,
+                    static_cast<__nv_bfloat16*>(act)) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+extern "C" int std_gemm_norm_argmax(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w,
+                                    int M, int N, int K, int rows_out, int n, int out_stride, int out_start,
+                                    int32_t* out, unsigned long long* keys, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  if (!gemm_shape_ok(x, w, M, N, K, 8) || out == nullptr || keys == nullptr || !norm_ok(sumsq, norm_w, K)) return 1;
+  if (rows_out <= 0 || rows_out > M || n <= 0) return 1;
+  GemmExtra e;
+  e.norm_sumsq = sumsq;
+  e.norm_w = norm_w;
+  e.norm_eps = eps;
+  const int splits = gemm_splits(N, K);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (splits == 1) {
+    int rc = gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, keys, rows_out, nullptr, &e);
+    if (rc != 0) return rc;
+    return launch_pdl(stdb::argmax_keys_kernel, dim3((rows_out + 127) / 128), dim3(128), 0, s, keys, rows_out, n,
+                      out_stride, out_start, out) == cudaSuccess
+               ? 0
+               : 4;
+  }
+  if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
+  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
+  int rc = gemm_launch(x, w, nullptr, partial, partial, M, N, K, splits, s, nullptr, 0, nullptr, &e);
+  if (rc != 0) return rc;
+  return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,
+                    gemm_out_view(partial, nullptr, splits, M, N), N, n, out_stride, out_start, out) == cudaSuccess
              ? 0
              : 4;
 }

@@ -8,10 +8,11 @@ Positions are 1-D (the fork disables get_rope_index, :2074-2105), so M-RoPE
 reduces to ordinary RoPE with theta = 1e6.
 
 Compute split:
-  * decode forwards: every kernel is from libstd_b200.so -- the tcgen05
-    weight-streaming GEMM for projections, MLP and lm_head, RMSNorm (fused
-    with the residual add), RoPE + KV append, draft / verify attention,
-    SiLU*up, lm_head fused with the greedy argmax;
+  * decode forwards: every kernel is from libstd_b200.so -- five launches
+    per layer: the tcgen05 weight-streaming GEMMs with the RMSNorm in their
+    prologue and the split-K reduction plus RoPE + KV append, residual add or
+    SiLU*up in their epilogue, and draft / verify attention; the final norm,
+    lm_head and greedy argmax are one more GEMM launch;
   * prefill (thousands of rows): cuBLAS GEMMs through torch and torch SDPA
     attention (library flash/efficient kernels), as the reference does.
 Dense decode forwards (AR steps and verify) always run their GEMMs on the same
@@ -138,11 +139,14 @@ class Workspace:
         self.attn = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
         self.o = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
         self.act = torch.zeros(rows, c.intermediate_size, device=d, dtype=dt)
+        # per 128-column tile and row, the sum of squares of the residual
+        # stream x (RMSNorm statistics passed from one fused GEMM to the next)
+        self.tiles = c.hidden_size // 128
+        self.sumsq_buf = torch.zeros(self.tiles * rows, device=d, dtype=torch.float32)
 
-
-def _mm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: Optional[torch.Tensor] = None):
-    """Decode-forward linear layer: the tcgen05 weight-streaming GEMM (ops.gemm)."""
-    return ops.gemm(x, w, out, bias)
+    def sumsq(self, rows: int) -> torch.Tensor:
+        """[hidden/128, rows] view: the layout the fused GEMMs of a `rows`-row forward use."""
+        return self.sumsq_buf[: self.tiles * rows].view(self.tiles, rows)
 
 
 def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *, B: int, n: int, rows: int,
@@ -157,7 +161,7 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     tokens).  GEMMs run on `rows` >= B*n rows (the fixed padded count for dense
     forwards).  The argmax of each new token's logits goes to
     argmax_out[b*argmax_stride + argmax_start + j]; argmax_out=None skips the
-    lm_head (a draft step whose prediction is never used).  dense_attn (a
+    final norm and lm_head (a draft step whose prediction is never used).  dense_attn (a
     seq_shard.ShardExchange on the owner rank) replaces the local verify
     kernel by the sequence-sharded attention over every rank's key range.
     sparse_index = (dense cache, selection [layers, B, Hkv, n_idx] int32):
@@ -169,22 +173,22 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     c = model.config
     M = B * n
     Hq, Hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+    eps = c.rms_norm_eps
     cos_t, sin_t = model.cos_t, model.sin_t
-    x, h = ws.x[:rows], ws.h[:rows]
+    x = ws.x[:rows]
+    sumsq = ws.sumsq(rows)
     if dense_attn is not None and not sparse:
         dense_attn.begin(n)
-    ops.embed(model.embed, tok, tok_start, n, ws.x[:M])
-    ops.rmsnorm(x, model.layers[0].w_in, c.rms_norm_eps, h)
-    n_layers = len(model.layers)
+    # Five launches per layer: [RMSNorm + QKV + RoPE + KV append] -> attention
+    # -> [O proj + residual] -> [RMSNorm + gate/up + SiLU*up] -> [down proj +
+    # residual].  The norms run on the GEMMs' staged x tiles from the
+    # per-tile sums of squares the previous GEMM (or the embedding) left in
+    # `sumsq`; the residual adds run in the last CTA of each output tile.
+    ops.embed_sumsq(model.embed, tok, tok_start, n, ws.x[:M], sumsq)
     for li, lw in enumerate(model.layers):
         kc, vc = cache[li, 0], cache[li, 1]
-        if rows == M:
-            ops.gemm_rope_append(h, lw.w_qkv, lw.b_qkv, B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off,
-                                 cos_t, sin_t, ws.q[:M], kc, vc)
-        else:  # padded rows: the GEMM runs on `rows`, RoPE on the M real ones
-            _mm(h, lw.w_qkv, ws.qkv[:rows], lw.b_qkv)
-            ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
-                            ws.q[:M], kc, vc)
+        ops.gemm_norm_rope_append(x, sumsq, lw.w_in, eps, lw.w_qkv, lw.b_qkv, B, n, Hq, Hkv, D, pos_base, pos_off,
+                                  slot_base, slot_off, cos_t, sin_t, ws.q[:M], kc, vc)
         if sparse and sparse_index is not None:
             dense, sel = sparse_index
             ops.draft_attention_indexed(ws.q[:M], dense[li, 0], dense[li, 1], sel[li], kc, vc, lens, len_offset,
@@ -199,16 +203,13 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
                                  out=ws.attn[:M].view(B, n, Hq, D))
         if collector is not None and not sparse:
             collector(li, ws.q[:M].view(B, n, Hq, D))
-        ops.gemm_add_rmsnorm(ws.attn[:rows], lw.w_o, x, lw.w_post, c.rms_norm_eps, h)
-        ops.gemm_silu_mul(h, lw.w_gu, ws.act[:rows])
-        if li + 1 < n_layers:
-            next_norm = model.layers[li + 1].w_in
-        else:  # the final norm feeds lm_head; a draft step without lm_head only adds
-            next_norm = model.norm if argmax_out is not None else None
-        ops.gemm_add_rmsnorm(ws.act[:rows], lw.w_down, x, next_norm, c.rms_norm_eps, h)
+        ops.gemm_residual(ws.attn[:rows], lw.w_o, x, sumsq)
+        ops.gemm_norm_silu_mul(x, sumsq, lw.w_post, eps, lw.w_gu, ws.act[:rows])
+        ops.gemm_residual(ws.act[:rows], lw.w_down, x, sumsq)
     if argmax_out is None:
         return
-    ops.gemm_argmax(h, model.lm_head, argmax_out, rows_out=M, n=n, out_stride=argmax_stride, out_start=argmax_start)
+    ops.gemm_norm_argmax(x, sumsq, model.norm, eps, model.lm_head, argmax_out, rows_out=M, n=n,
+                         out_stride=argmax_stride, out_start=argmax_start)
 
 
 # ---------------------------------------------------------------------- prefill

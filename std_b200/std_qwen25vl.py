@@ -659,12 +659,15 @@ class STDRunner:
         return bool(self.all_done_host.item())
 
     # ------------------------------------------------------------------ loops
-    def run_std(self) -> float:
+    def run_std(self, device_loop: Optional[bool] = None) -> float:
         """STD decode of every request from the post-prefill state; returns seconds (device time).
 
         With the device loop the whole decode is one graph launch and one
-        synchronisation; otherwise the host launches a round graph and reads
-        the 4-byte all-done flag after each round."""
+        synchronisation; otherwise (device_loop=False, or a runner built
+        without it) the host launches a round graph and reads the 4-byte
+        all-done flag after each round."""
+        if device_loop is False and self.device_loop:
+            return self._without_device_loop(self.run_std)
         self.capture("std")
         self.reset()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -689,7 +692,19 @@ class STDRunner:
         end.synchronize()
         return start.elapsed_time(end) / 1000.0
 
-    def run_ar(self) -> float:
+    def _without_device_loop(self, fn):
+        """Run fn with the host-driven loop (per-round graphs) on this runner."""
+        saved = {k: self._graphs.pop(k) for k in ("std_loop", "ar_loop") if k in self._graphs}
+        self.device_loop = False
+        try:
+            return fn()
+        finally:
+            self.device_loop = True
+            self._graphs.update(saved)
+
+    def run_ar(self, device_loop: Optional[bool] = None) -> float:
+        if device_loop is False and self.device_loop:
+            return self._without_device_loop(self.run_ar)
         self.capture("ar")
         self.reset()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
