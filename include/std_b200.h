@@ -231,11 +231,13 @@ int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, 
  * of x (written by std_embed_sumsq and std_gemm_residual), from which the
  * RMSNorm in front of a projection (Qwen2RMSNorm, modeling_qwen2_5_vl.py:
  * 183-197: bf16(norm_w * bf16(x * rsqrt(mean(x^2) + eps)))) is applied to the
- * staged x tiles inside the GEMM.  Split-K partial sums are reduced inside the
- * GEMM by the last CTA of each 128-feature tile, which also applies the op
- * that follows the projection.  workspace: std_gemm_fused_workspace_bytes,
- * 256-byte aligned, zeroed once before its first use (each call leaves its
- * counters zero); it must not be shared by launches that run concurrently. */
+ * staged x tiles inside the GEMM.  When K is split, the CTAs of one
+ * 128-feature tile form a thread-block cluster and reduce their partial sums
+ * through distributed shared memory, in split order, before applying the op
+ * that follows the projection (no global scratch).  The norm + SiLU / argmax
+ * ops take a workspace of std_gemm_fused_workspace_bytes (split partials for
+ * their reduction kernel when K is split); it must not be shared by launches
+ * that run concurrently. */
 size_t std_gemm_fused_workspace_bytes(int M, int N, int K);
 /* Replaces: nn.Embedding (modeling_qwen2_5_vl.py:1336) of a decode step:
  * out[b*n + j] = table[tok[b*tok_stride + tok_start + j]] (rows [B*n, H]) and
@@ -247,17 +249,19 @@ int std_embed_sumsq(const void* table, int vocab, int H, const int32_t* tok, int
  * step (modeling_qwen2_5_vl.py:1179, :1050-1052, :690-732; kv_cache.py:54-69):
  * qkv = rmsnorm(x) . w^T + bias over M rows (M >= B*n: padded rows are
  * computed and dropped), then for the B*n real rows the std_rope_append step
- * (q -> q_out, k/v -> cache slot slot_base[b] + slot_off + j).  D == 128. */
+ * (q -> q_out, k/v -> cache slot slot_base[b] + slot_off + j).  D == 128,
+ * M <= 128. */
 int std_gemm_norm_rope_append(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w,
                               const void* bias, int M, int K, int B, int n, int Hq, int Hkv, int D,
                               const int32_t* pos_base, int pos_off, const int32_t* slot_base, int slot_off,
                               const void* cos_t, const void* sin_t, int max_pos, void* q_out, void* k_cache,
-                              void* v_cache, int cap, void* workspace, size_t workspace_bytes, void* stream);
+                              void* v_cache, int cap, void* stream);
 /* Replaces: o_proj / down_proj and the residual add after them
  * (modeling_qwen2_5_vl.py:1200-1221): resid <- bf16(resid + bf16(a . w^T +
- * bias)) over [M, N], and sumsq_out [N/128, M] of the new resid.  N % 128 == 0. */
+ * bias)) over [M, N], and sumsq_out [N/128, M] of the new resid.  N % 128 == 0,
+ * M <= 128. */
 int std_gemm_residual(const void* a, const void* w, const void* bias, void* resid, float* sumsq_out, int M, int N,
-                      int K, void* workspace, size_t workspace_bytes, void* stream);
+                      int K, void* stream);
 /* Replaces: post_attention_layernorm + Qwen2MLP's act_fn(gate_proj(h)) *
  * up_proj(h) (modeling_qwen2_5_vl.py:1214, :674-687): act [M, I] from the
  * residual stream x, with w [2I, K] in 64-row [gate | up] blocks. */

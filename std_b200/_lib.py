@@ -52,8 +52,8 @@ SIGNATURES: Dict[str, tuple] = {
     "std_gemm_fused_workspace_bytes": (SZ, [I, I, I]),
     "std_embed_sumsq": (I, [P, I, I, PI32, I, I, I, I, P, PF, I, P]),
     "std_gemm_norm_rope_append": (I, [P, PF, P, F, P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I,
-                                      P, SZ, P]),
-    "std_gemm_residual": (I, [P, P, P, P, PF, I, I, I, P, SZ, P]),
+                                      P]),
+    "std_gemm_residual": (I, [P, P, P, P, PF, I, I, I, P]),
     "std_gemm_norm_silu_mul": (I, [P, PF, P, F, P, I, I, I, P, P, SZ, P]),
     "std_gemm_norm_argmax": (I, [P, PF, P, F, P, I, I, I, I, I, I, I, PI32, P, P, SZ, P]),
     "std_rmsnorm": (I, [P, P, F, I, I, P, P]),

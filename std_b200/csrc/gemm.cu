@@ -64,9 +64,8 @@ struct GemmParams {
   const float* norm_sumsq;
   const __nv_bfloat16* norm_w;
   float norm_eps;
-  // split-K fixup (fixup != FIX_NONE)
+  // split-K fixup (fixup != FIX_NONE; the splits of a tile form one cluster)
   int fixup;
-  int* tile_count;  // [tiles] arrival counters, zero between calls
   RopeParams rope;  // FIX_ROPE: rows t < rope_rows are real tokens (t = b * rope.n + j)
   int rope_rows;
   __nv_bfloat16* resid;  // FIX_RESID: [M, N]
@@ -92,8 +91,8 @@ STD_DEV float tile_sum128_finish(const float* s_part4, int slot) {
 }
 
 // RMSNorm of staged X rows in place: the 128B-swizzled [rows][64] bf16 tile at
-// `tile` holds columns k0..k0+63 of rows 0..nrows-1; rows >= M are left as
-// loaded (zero fill).  Threads [t0, t0 + nthr) share the work.
+// `tile` holds columns k0..k0+63 (indices into w) of rows 0..nrows-1; rows >=
+// M are left as loaded (zero fill).  Threads t, t + nthr, ... share the work.
 STD_DEV void norm_x_tile(uint8_t* tile, int nrows, int M, int k0, const float* s_inv, const __nv_bfloat16* w,
                          int t, int nthr) {
   for (int i = t; i < nrows * 8; i += nthr) {
@@ -126,15 +125,18 @@ STD_DEV void norm_x_tile(uint8_t* tile, int nrows, int M, int k0, const float* s
 // Apply a split-K fixup epilogue to the tile's bf16 results y[t] (t < M) of
 // feature f = n0 + thread.  `yv(t)` returns them; s_y (>= 32 x 128 bf16) and
 // s_part (>= 4 x 32 floats) are free shared memory.
+// Tokens handled here: t = t_first + i * t_step (the cluster rank's share).
 template <class YV>
-STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloat16* s_y, float* s_part) {
+STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloat16* s_y, float* s_part,
+                        int t_first, int t_step) {
   const int tid = threadIdx.x;
   const int f = n0 + tid;
   if (p.fixup == FIX_RESID) {
-    for (int t0 = 0; t0 < p.M; t0 += 32) {
-      const int nt = p.M - t0 < 32 ? p.M - t0 : 32;
+    const int mine = t_first < p.M ? (p.M - t_first + t_step - 1) / t_step : 0;
+    for (int i0 = 0; i0 < mine; i0 += 32) {
+      const int nt = mine - i0 < 32 ? mine - i0 : 32;
       for (int j = 0; j < nt; ++j) {
-        const int t = t0 + j;
+        const int t = t_first + (i0 + j) * t_step;
         float xn = 0.f;
         if (f < p.N) {
           __nv_bfloat16* xp = p.resid + static_cast<size_t>(t) * p.N + f;
@@ -144,7 +146,8 @@ STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloa
         tile_sum128(__fmul_rn(xn, xn), s_part, j);
       }
       __syncthreads();
-      if (tid < nt) p.sumsq_out[static_cast<size_t>(tile) * p.M + t0 + tid] = tile_sum128_finish(s_part, tid);
+      if (tid < nt)
+        p.sumsq_out[static_cast<size_t>(tile) * p.M + t_first + (i0 + tid) * t_step] = tile_sum128_finish(s_part, tid);
       __syncthreads();
     }
     return;
@@ -154,12 +157,13 @@ STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloa
   const int heads = r.Hq + 2 * r.Hkv;
   if (tile >= heads) return;
   const int d = tid, half = 64, c = d & 63;
-  for (int t0 = 0; t0 < p.rope_rows; t0 += 32) {
-    const int nt = p.rope_rows - t0 < 32 ? p.rope_rows - t0 : 32;
-    for (int j = 0; j < nt; ++j) s_y[j * 128 + d] = __float2bfloat16_rn(yv(t0 + j));
+  const int mine = t_first < p.rope_rows ? (p.rope_rows - t_first + t_step - 1) / t_step : 0;
+  for (int i0 = 0; i0 < mine; i0 += 32) {
+    const int nt = mine - i0 < 32 ? mine - i0 : 32;
+    for (int j = 0; j < nt; ++j) s_y[j * 128 + d] = __float2bfloat16_rn(yv(t_first + (i0 + j) * t_step));
     __syncthreads();
     for (int j = 0; j < nt; ++j) {
-      const int row = t0 + j;
+      const int row = t_first + (i0 + j) * t_step;
       const int b = row / r.n, jj = row % r.n;
       int pos = r.pos_base[b] + r.pos_off + jj;
       const int slot = r.slot_base[b] + r.slot_off + jj;
@@ -213,12 +217,13 @@ __global__ void __launch_bounds__(GM_THREADS)
   const int S = p.stages;
   uint8_t* sW = smem;                 // [S][16 KB]
   uint8_t* sX = smem + S * GM_WTILE;  // [S][xtile]
+  // norm prologue: the CTA's K range of the norm weight, [nkb * 64] bf16
+  __nv_bfloat16* s_normw = reinterpret_cast<__nv_bfloat16*>(sX + S * xtile);
   __shared__ __align__(8) uint64_t bar_full[GM_MAX_STAGES], bar_empty[GM_MAX_STAGES], bar_xready[GM_MAX_STAGES],
       bar_done;
   __shared__ uint32_t s_tmem;
   __shared__ float s_inv[256];
   __shared__ float s_part[4 * 32];
-  __shared__ int s_last;
   __shared__ int s_norm_ok[2][2];
 
   uint32_t ncols = 32;
@@ -292,6 +297,9 @@ __global__ void __launch_bounds__(GM_THREADS)
   } else if (norm && warp >= 2) {
     // ---- RMSNorm of the staged X tiles (warps 2-3) ----
     const int t = tid - 64;
+    // this CTA's columns of the norm weight (constant: before the wait)
+    for (int i = t; i < nkb * 8; i += 64)
+      reinterpret_cast<uint4*>(s_normw)[i] = *reinterpret_cast<const uint4*>(p.norm_w + kb0 * GM_BK + i * 8);
     pdl_wait();
     if (p.late_trigger) pdl_launch_dependents();
     const int ntiles_in = p.K / GM_BM;
@@ -312,7 +320,7 @@ __global__ void __launch_bounds__(GM_THREADS)
       // the barrier (double-buffered, so a warp that runs ahead never
       // overwrites a vote the other warp has yet to read)
       const bool ok_w = __all_sync(0xffffffffu, mbar_wait(&bar_full[st], (i / S) & 1));
-      if (ok_w) norm_x_tile(sX + st * xtile, p.nmma, p.M, (kb0 + i) * GM_BK, s_inv, p.norm_w, t, 64);
+      if (ok_w) norm_x_tile(sX + st * xtile, p.nmma, p.M, i * GM_BK, s_inv, s_normw, t, 64);
       fence_async_smem();
       if (lane == 0) s_norm_ok[i & 1][warp - 2] = ok_w ? 1 : 0;
       named_bar_sync(1, 64);
@@ -384,23 +392,7 @@ __global__ void __launch_bounds__(GM_THREADS)
     }
   }
   const bool fused = p.fixup != FIX_NONE;
-  if (fused && p.splits == 1) {
-    // the whole K sum is in this CTA's TMEM: stage the tile's bf16 results in
-    // shared memory (token-major, [nmma][128]) and apply the fixup from there
-    __nv_bfloat16* s_res = reinterpret_cast<__nv_bfloat16*>(smem);
-    for (int t0 = 0; t0 < p.nmma; t0 += 32) {
-      uint32_t v[32];
-      tmem_ld32(trow + t0, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) s_res[(t0 + j) * 128 + tid] = __float2bfloat16_rn(__uint_as_float(v[j]) + bias);
-    }
-    __syncthreads();
-    gemm_fixup(p, tile, n0, [&](int t) { return __bfloat162float(s_res[t * 128 + tid]); },
-               reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(p.nmma) * 256), s_part);
-  }
-  for (int t0 = 0; p.amax_keys == nullptr && p.act == nullptr && !(fused && p.splits == 1) && t0 < p.nmma;
-       t0 += 32) {
+  for (int t0 = 0; p.amax_keys == nullptr && p.act == nullptr && !fused && t0 < p.nmma; t0 += 32) {
     uint32_t v[32];
     tmem_ld32(trow + t0, v);
     tmem_wait_ld();
@@ -415,29 +407,41 @@ __global__ void __launch_bounds__(GM_THREADS)
         p.partial[(static_cast<size_t>(split) * p.M + t) * p.N + f] = acc;
     }
   }
-  if (fused && p.splits > 1) {
-    // count this CTA in; the last of the tile's splits applies the fixup
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int prev = atomicAdd(&p.tile_count[tile], 1);
-      s_last = prev == p.splits - 1;
-      if (s_last) p.tile_count[tile] = 0;  // every split has arrived: ready for the next call
+  if (fused) {
+    // The K splits of this tile are one thread-block cluster (rank = split).
+    // Each CTA stages its fp32 accumulator [M][128] in its shared memory;
+    // rank r then reduces tokens r, r + splits, ... by reading every rank's
+    // stage in split order over distributed shared memory (the order
+    // gemm_reduce_kernel adds global partials in) and applies the fixup.
+    float* s_acc = reinterpret_cast<float*>(smem);
+    for (int t0 = 0; t0 < p.nmma; t0 += 32) {
+      uint32_t v[32];
+      tmem_ld32(trow + t0, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (t0 + j < p.M) s_acc[(t0 + j) * GM_BM + tid] = __uint_as_float(v[j]);
     }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      const float fb = (p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
-      const size_t MN = static_cast<size_t>(p.M) * p.N;
-      gemm_fixup(p, tile, n0,
-                 [&](int t) {
-                   if (f >= p.N) return 0.f;
-                   const float* pp = p.partial + static_cast<size_t>(t) * p.N + f;
-                   float a = __ldcg(pp);
-                   for (int s2 = 1; s2 < p.splits; ++s2) a += __ldcg(pp + s2 * MN);
-                   return bf16_round(a + fb);
-                 },
-                 reinterpret_cast<__nv_bfloat16*>(smem), s_part);
+    if (p.splits > 1) {
+      cluster_arrive_release();
+      cluster_wait_acquire();
+    } else {
+      __syncthreads();
+    }
+    const float fb = (p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
+    const uint32_t my_acc = smem_u32(s_acc) + static_cast<uint32_t>(tid) * 4u;
+    gemm_fixup(p, tile, n0,
+               [&](int t) {
+                 const uint32_t off = static_cast<uint32_t>(t) * GM_BM * 4u;
+                 float a = p.splits > 1 ? ld_dsmem_f32(mapa_rank(my_acc + off, 0)) : s_acc[t * GM_BM + tid];
+                 for (int s2 = 1; s2 < p.splits; ++s2) a += ld_dsmem_f32(mapa_rank(my_acc + off, s2));
+                 return bf16_round(a + fb);
+               },
+               reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(p.M) * GM_BM * 4), s_part, split,
+               p.splits);
+    if (p.splits > 1) {  // no CTA leaves while another may still read its stage
+      cluster_arrive_release();
+      cluster_wait_acquire();
     }
   }
   tc_fence_before();
@@ -591,6 +595,13 @@ static int gemm_splits(int N, int K) {
 
 static int gemm_nmma(int M) { return ((M + 15) / 16) * 16; }
 
+// Splits of a GEMM whose split-K sum is reduced inside one cluster: at most
+// 8 (the portable cluster size).
+static int gemm_splits_cluster(int N, int K) {
+  const int s = gemm_splits(N, K);
+  return s > 8 ? 8 : s;
+}
+
 extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int s = gemm_splits(N, K);
@@ -605,7 +616,6 @@ struct GemmExtra {
   const void* norm_w = nullptr;
   float norm_eps = 0.f;
   int fixup = stdb::FIX_NONE;
-  int* tile_count = nullptr;
   stdb::RopeParams rope = {};
   int rope_rows = 0;
   void* resid = nullptr;
@@ -620,13 +630,22 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
   int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
   stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
-  // a fused fixup stages the tile's results ([nmma][128] bf16) and a 32-row
+  const bool norm = ext != nullptr && ext->norm_w != nullptr;
+  const bool fused = ext != nullptr && ext->fixup != stdb::FIX_NONE;
+  // norm prologue: the CTA's K range of the norm weight after the stages
+  const uint32_t kmax = static_cast<uint32_t>((K / stdb::GM_BK + splits - 1) / splits) * stdb::GM_BK;
+  const uint32_t normw_bytes = norm ? kmax * 2u : 0u;
+  if (norm) {
+    stages = static_cast<int>((stdb::GM_SMEM_BUDGET - normw_bytes) / stage_bytes);
+    stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
+  }
+  // a fused fixup stages the tile's fp32 accumulator ([M][128]) and a 32-row
   // RoPE exchange buffer in the (then idle) stage buffers
-  const uint32_t fix_bytes = static_cast<uint32_t>(nmma) * 256u + 32u * 256u;
-  while (ext != nullptr && ext->fixup != stdb::FIX_NONE && static_cast<uint32_t>(stages) * stage_bytes < fix_bytes)
-    ++stages;
+  const uint32_t fix_bytes = static_cast<uint32_t>(M) * 512u + 32u * 256u;
+  while (fused && static_cast<uint32_t>(stages) * stage_bytes < fix_bytes) ++stages;
   if (stages > stdb::GM_MAX_STAGES) return 1;
-  const size_t smem = static_cast<size_t>(stages) * stage_bytes + 1024;
+  const size_t smem = static_cast<size_t>(stages) * stage_bytes + normw_bytes + 1024;
+  if (smem > 227 * 1024) return 1;
   static SmemGrant grant;
   if (ensure_smem(stdb::gemm_kernel, grant, smem) != 0) return 3;
   CUtensorMap tw, tx;
@@ -656,7 +675,6 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   p.norm_w = static_cast<const __nv_bfloat16*>(e.norm_w);
   p.norm_eps = e.norm_eps;
   p.fixup = e.fixup;
-  p.tile_count = e.tile_count;
   p.rope = e.rope;
   p.rope_rows = e.rope_rows;
   p.resid = static_cast<__nv_bfloat16*>(e.resid);
@@ -664,10 +682,13 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   p.late_trigger = e.late_trigger;
   // may begin while the previous kernel in the stream finishes: the weight
   // tiles of the first stages are requested before griddepcontrol.wait
-  return launch_pdl(stdb::gemm_kernel, dim3((N + stdb::GM_BM - 1) / stdb::GM_BM, splits), dim3(stdb::GM_THREADS),
-                    smem, s, tw, tx, p) == cudaSuccess
-             ? 0
-             : 4;
+  const dim3 grid((N + stdb::GM_BM - 1) / stdb::GM_BM, splits);
+  if (fused && splits > 1)  // the splits of a tile reduce in one cluster
+    return launch_pdl_cluster(stdb::gemm_kernel, grid, dim3(stdb::GM_THREADS), dim3(1, splits, 1), smem, s, tw, tx,
+                              p) == cudaSuccess
+               ? 0
+               : 4;
+  return launch_pdl(stdb::gemm_kernel, grid, dim3(stdb::GM_THREADS), smem, s, tw, tx, p) == cudaSuccess ? 0 : 4;
 }
 
 static bool gemm_shape_ok(const void* x, const void* w, int M, int N, int K, int n_align) {
@@ -819,21 +840,18 @@ extern "C" int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int
 // ---------------------------------------------------------------------------
 // Decode-layer GEMMs with their neighbours folded in (one launch each):
 // the RMSNorm in front of a projection runs on the staged X tiles, and the
-// split-K reduction with the op after a projection runs in the last CTA of
-// each 128-feature tile.  Workspace: [tile counters | split partials]; the
-// counters must be zero before the first call (zero the buffer once) and
-// every call leaves them zero.
+// split-K reduction with the op after a projection runs inside the cluster
+// formed by each 128-feature tile's K splits (distributed shared memory).
+// Only the norm + SiLU / argmax ops take a workspace (split partials for
+// their separate reduction kernel, used when K is split).
 // ---------------------------------------------------------------------------
-static constexpr size_t kCountersBytes = 4096;  // up to 1024 tiles (N <= 131072)
-
 extern "C" size_t std_gemm_fused_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  return kCountersBytes + std_gemm_workspace_bytes(M, N, K);
+  return std_gemm_workspace_bytes(M, N, K);  // split partials for the norm + SiLU / argmax ops
 }
 
 static bool fused_ws_ok(void* workspace, size_t workspace_bytes, int M, int N, int K) {
-  return workspace != nullptr && workspace_bytes >= std_gemm_fused_workspace_bytes(M, N, K) &&
-         (reinterpret_cast<uintptr_t>(workspace) & 255) == 0 && (N + stdb::GM_BM - 1) / stdb::GM_BM <= 1024;
+  return workspace != nullptr && workspace_bytes >= std_gemm_fused_workspace_bytes(M, N, K);
 }
 
 static bool norm_ok(const float* sumsq, const void* norm_w, int K) {
@@ -856,21 +874,18 @@ extern "C" int std_gemm_norm_rope_append(const void* x, const float* sumsq, cons
                                          const void* w, const void* bias, int M, int K, int B, int n, int Hq, int Hkv,
                                          int D, const int32_t* pos_base, int pos_off, const int32_t* slot_base,
                                          int slot_off, const void* cos_t, const void* sin_t, int max_pos, void* q_out,
-                                         void* k_cache, void* v_cache, int cap, void* workspace,
-                                         size_t workspace_bytes, void* stream) {
+                                         void* k_cache, void* v_cache, int cap, void* stream) {
   const int N = (Hq + 2 * Hkv) * D;
-  if (D != stdb::GM_BM || B <= 0 || n <= 0 || B * n > M || cap <= 0 || max_pos <= 0) return 1;
+  if (D != stdb::GM_BM || B <= 0 || n <= 0 || B * n > M || M > 128 || cap <= 0 || max_pos <= 0) return 1;
   if (!gemm_shape_ok(x, w, M, N, K, 8) || !norm_ok(sumsq, norm_w, K)) return 1;
   if (q_out == nullptr || k_cache == nullptr || v_cache == nullptr || pos_base == nullptr || slot_base == nullptr ||
       cos_t == nullptr || sin_t == nullptr)
     return 1;
-  if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
   GemmExtra e;
   e.norm_sumsq = sumsq;
   e.norm_w = norm_w;
   e.norm_eps = eps;
   e.fixup = stdb::FIX_ROPE;
-  e.tile_count = static_cast<int*>(workspace);
   e.rope.n = n;
   e.rope.Hq = Hq;
   e.rope.Hkv = Hkv;
@@ -890,23 +905,19 @@ extern "C" int std_gemm_norm_rope_append(const void* x, const float* sumsq, cons
   // the draft kernel that follows reads older K/V rows and the lengths before
   // its own wait: release it only once this grid's predecessors are done
   e.late_trigger = 1;
-  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
-  return gemm_launch(x, w, bias, nullptr, partial, M, N, K, gemm_splits(N, K), static_cast<cudaStream_t>(stream),
-                     nullptr, 0, nullptr, &e);
+  return gemm_launch(x, w, bias, nullptr, nullptr, M, N, K, gemm_splits_cluster(N, K),
+                     static_cast<cudaStream_t>(stream), nullptr, 0, nullptr, &e);
 }
 
 extern "C" int std_gemm_residual(const void* a, const void* w, const void* bias, void* resid, float* sumsq_out, int M,
-                                 int N, int K, void* workspace, size_t workspace_bytes, void* stream) {
-  if (!gemm_shape_ok(a, w, M, N, K, stdb::GM_BM) || resid == nullptr || sumsq_out == nullptr) return 1;
-  if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
+                                 int N, int K, void* stream) {
+  if (!gemm_shape_ok(a, w, M, N, K, stdb::GM_BM) || M > 128 || resid == nullptr || sumsq_out == nullptr) return 1;
   GemmExtra e;
   e.fixup = stdb::FIX_RESID;
-  e.tile_count = static_cast<int*>(workspace);
   e.resid = resid;
   e.sumsq_out = sumsq_out;
-  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
-  return gemm_launch(a, w, bias, nullptr, partial, M, N, K, gemm_splits(N, K), static_cast<cudaStream_t>(stream),
-                     nullptr, 0, nullptr, &e);
+  return gemm_launch(a, w, bias, nullptr, nullptr, M, N, K, gemm_splits_cluster(N, K),
+                     static_cast<cudaStream_t>(stream), nullptr, 0, nullptr, &e);
 }
 
 extern "C" int std_gemm_norm_silu_mul(const void* x, const float* sumsq, const void* norm_w, float eps,
@@ -922,7 +933,7 @@ extern "C" int std_gemm_norm_silu_mul(const void* x, const float* sumsq, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (splits == 1) return gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, nullptr, 0, act, &e);
   if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
-  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
+  float* partial = static_cast<float*>(workspace);
   int rc = gemm_launch(x, w, nullptr, partial, partial, M, N, K, splits, s, nullptr, 0, nullptr, &e);
   if (rc != 0) return rc;
   const size_t total8 = static_cast<size_t>(M) * I / 8;
@@ -955,7 +966,7 @@ extern "C" int std_gemm_norm_argmax(const void* x, const float* sumsq, const voi
                : 4;
   }
   if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
-  float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCountersBytes);
+  float* partial = static_cast<float*>(workspace);
   int rc = gemm_launch(x, w, nullptr, partial, partial, M, N, K, splits, s, nullptr, 0, nullptr, &e);
   if (rc != 0) return rc;
   return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,

@@ -319,10 +319,9 @@ def gemm_silu_mul(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor):
 # ----------------------------------------------------------------------------
 
 def _fused_ws(M: int, N: int, K: int, device: torch.device) -> torch.Tensor:
-    """Workspace of the fused GEMMs: tile counters (zero; every call leaves them
-    zero) followed by split-K partials.  Its own buffer, apart from the
-    workspace of the unfused GEMMs, which reuse theirs without a zero prefix."""
-    return workspace("gemm_fused", _lib.query("std_gemm_fused_workspace_bytes", M, N, K), device)
+    """Split-K partials of the norm + SiLU / argmax GEMMs (their separate
+    reduction kernel runs only when K is split)."""
+    return workspace("gemm", _lib.query("std_gemm_fused_workspace_bytes", M, N, K), device)
 
 
 def embed_sumsq(table: torch.Tensor, tok: torch.Tensor, tok_start: int, n: int, out: torch.Tensor,
@@ -345,11 +344,10 @@ def gemm_norm_rope_append(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Te
     N = w.shape[0]
     for t, nm in ((x, "x"), (w, "w"), (norm_w, "norm_w")):
         _check(t, torch.bfloat16, nm)
-    ws = _fused_ws(M, N, K, x.device)
     _lib.call("std_gemm_norm_rope_append", x.data_ptr(), sumsq.data_ptr(), norm_w.data_ptr(), float(eps), w.data_ptr(),
               _p(bias), M, K, B, n, Hq, Hkv, D, pos_base.data_ptr(), int(pos_off), slot_base.data_ptr(), int(slot_off),
               cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape[0], q_out.data_ptr(), k_cache.data_ptr(),
-              v_cache.data_ptr(), k_cache.shape[-2], ws.data_ptr(), ws.numel(), _stream())
+              v_cache.data_ptr(), k_cache.shape[-2], _stream())
     return q_out
 
 
@@ -361,9 +359,8 @@ def gemm_residual(a: torch.Tensor, w: torch.Tensor, resid: torch.Tensor, sumsq_o
     for t, nm in ((a, "a"), (w, "w"), (resid, "resid")):
         _check(t, torch.bfloat16, nm)
     _check(sumsq_out, torch.float32, "sumsq_out")
-    ws = _fused_ws(M, N, K, a.device)
     _lib.call("std_gemm_residual", a.data_ptr(), w.data_ptr(), _p(bias), resid.data_ptr(), sumsq_out.data_ptr(), M, N, K,
-              ws.data_ptr(), ws.numel(), _stream())
+              _stream())
     return resid
 
 

@@ -289,6 +289,8 @@ class STDRunner:
             self.sel_idx = None
         model.rope_tables(self.cap_d + 2)
         self.dense_rows = _round_up(batch_size * (gamma + 1), 16)
+        if self.dense_rows > 128:
+            raise ValueError("requests x (gamma + 1) must be <= 128 (the fused decode GEMMs' row limit)")
         self.ws = Workspace(model, max(self.dense_rows, batch_size))
         B = batch_size
         i32 = dict(dtype=torch.int32, device=dev)
@@ -745,18 +747,23 @@ class STDRunner:
         phases = {"drafts": self._drafts, "verify_first": lambda: self._verify_phase(0),
                   "verify": lambda: self._verify_phase(1), "accept_first": lambda: self._accept_and_flag(0),
                   "accept": lambda: self._accept_and_flag(1), "bonus": self._bonus_step}
-        if self.use_graphs:
+        if self.use_graphs and any("phase_" + name not in self._graphs for name in phases):
+            # Warm up with whole rounds (workspaces, kernel attributes), never
+            # with a phase out of its round: a bonus step run straight after
+            # reset() would write its K/V row over the last prompt row of the
+            # sparse cache.  Capturing a phase runs nothing.
+            self.reset()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.std_round(True)
+                self.std_round(False)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
             for name, fn in phases.items():
                 key = "phase_" + name
                 if key in self._graphs:
                     continue
-                self.reset()
-                side = torch.cuda.Stream()
-                side.wait_stream(torch.cuda.current_stream())
-                with torch.cuda.stream(side):
-                    fn()
-                torch.cuda.current_stream().wait_stream(side)
-                torch.cuda.synchronize()
                 self.reset()
                 torch.cuda.synchronize()
                 g = torch.cuda.CUDAGraph()

@@ -349,6 +349,11 @@ def test_device_loop_matches_host_loop_and_profiled_rounds():
         assert out["loop"][2] == out[key][2], key
     assert torch.equal(ar[0], ar_host[0]) and torch.equal(ar[1], ar_host[1])
     assert torch.equal(out["loop"][1], ar[1])
+    # a second runner prefilled from the same inputs decodes identically
+    other = STDRunner(model, B, layout, 30, gamma=5, k=k, eos_token_id=eos)
+    other.prefill(embeds)
+    other.run_std()
+    assert torch.equal(other.out_tokens.cpu(), out["loop"][0]) and other.std_stats() == out["loop"][2]
     for b in range(B):
         n = int(ar[1][b])
         assert out["loop"][0][b, :n].tolist() == ar[0][b, :n].tolist()

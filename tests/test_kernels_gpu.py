@@ -674,19 +674,12 @@ def _rms_ref(x, sumsq, w, eps):
     return (w.float() * (x.float() * inv[:, None]).to(torch.bfloat16).float()).to(torch.bfloat16)
 
 
-def _fused_counters_zero():
-    from std_b200 import ops as o
-
-    ws = [v for (kind, _), v in o._WS.items() if kind == "gemm_fused"]
-    return all(int(w[:4096].count_nonzero()) == 0 for w in ws)
-
-
 @pytest.mark.parametrize("M,N,K", [(8, 3584, 3584), (80, 3584, 18944), (5, 896, 1536), (16, 256, 384)])
 def test_gemm_residual_vs_fp32(ops, M, N, K):
-    """resid += a @ w^T in one launch (split-K reduced by the last CTA of each
-    tile): bf16(resid + bf16(sum)) within bf16 rounding of the fp32 result,
-    per-tile sums of squares of the new residual, counters left zero, and
-    repeated calls bit-identical."""
+    """resid += a @ w^T in one launch (split-K reduced inside each tile's
+    cluster): bf16(resid + bf16(sum)) within bf16 rounding of the fp32 result,
+    per-tile sums of squares of the new residual, and repeated calls
+    bit-identical."""
     g = torch.Generator(device="cuda").manual_seed(M + N)
     a = (torch.randn(M, K, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
     w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
@@ -706,7 +699,6 @@ def test_gemm_residual_vs_fp32(ops, M, N, K):
     err = (resid.float() - want).abs()
     assert err.max().item() <= 0.02 * want.abs().max().item()
     assert torch.allclose(ss, _tile_sumsq(resid), rtol=1e-5, atol=1e-6)
-    assert _fused_counters_zero()
     _no_device_error(ops)
 
 
@@ -750,7 +742,6 @@ def test_gemm_norm_rope_append_vs_fp32(ops, M, B, n):
         vb = vc[b][:, slots[b]].float().permute(1, 0, 2)
         assert (kb - rot[b, :, Hq:Hq + Hkv]).abs().max().item() < tol
         assert (vb - qkv[b, :, Hq + Hkv:]).abs().max().item() < tol
-    assert _fused_counters_zero()
     _no_device_error(ops)
 
 
