@@ -269,10 +269,13 @@ int std_gemm_norm_silu_mul(const void* x, const float* sumsq, const void* norm_w
                            int I, int K, void* act, void* workspace, size_t workspace_bytes, void* stream);
 /* Replaces: the final norm + lm_head + greedy argmax (modeling_qwen2_5_vl.py:
  * 1463, :1749; std_qwen25vl.py:98-99, :806): as std_gemm_argmax on
- * rmsnorm(x).  keys: M uint64 scratch, zero on entry and left zero. */
+ * rmsnorm(x).  keys: M uint64 scratch, zero on entry and left zero.
+ * margin_out (optional, indexed like out): the row's largest minus
+ * second-largest bf16 logit (verification_policy.py:29-46). */
 int std_gemm_norm_argmax(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w, int M,
                          int N, int K, int rows_out, int n, int out_stride, int out_start, int32_t* out,
-                         unsigned long long* keys, void* workspace, size_t workspace_bytes, void* stream);
+                         float* margin_out, unsigned long long* keys, void* workspace, size_t workspace_bytes,
+                         void* stream);
 
 /* ---- (d) fused greedy acceptance + rollback ---------------------------- */
 
@@ -289,6 +292,28 @@ int std_accept_commit(int B, int gamma, int pending, int32_t* tok, int tok_strid
                       const int32_t* dense_next, int max_new, int eos, int ignore_eos, int32_t* ctx_len,
                       int32_t* dense_len, int32_t* sparse_len, int32_t* n_gen, int32_t* done, int32_t* out_tokens,
                       int32_t* stats, int32_t* accept_hist, int hist_cap, void* stream);
+
+/* Replaces: the verification policies of a parallel verify
+ * (std_qwen25vl.py:816-884 margin check, math_on_full_accept and
+ * verify_fallback; verification_policy.py:29-67 min_prediction_margin and
+ * needs_sequential_fallback).  One thread per request (B <= 1024): computes
+ * the accepted prefix, the smallest top-1 minus top-2 margin of the committed
+ * predictions from margins [B, vstride] (threshold NaN: no margin check;
+ * margin_hist [B, hist_cap] gets the round's value at index stats[b][0], NaN
+ * when no prediction has a verify row), and whether the round is re-verified:
+ * mode 0 none, 1 sequential_on_reject, 2 sequential_on_low_accept (accept <=
+ * max_accept), 3 sequential_on_low_margin, 4 sequential_guard;
+ * math_on_full_accept re-verifies a full accept.  rerun[b] (int32), counters
+ * [B, 3] (+= margin reruns, fallbacks, accepted extra), first_accept [B],
+ * any_rerun [1]; with cond != 0 (a conditional handle of the graph being
+ * captured) the kernel also sets that IF condition to any_rerun.  after = 1:
+ * the bookkeeping after a replay (accepted extra from the replayed vpred). */
+int std_verify_policy(int B, int gamma, int pending, const int32_t* tok, int tok_stride, const int32_t* vpred,
+                      int vstride, const int32_t* dense_next, int max_new, const int32_t* n_gen, const int32_t* done,
+                      const int32_t* stats, const float* margins, float threshold, int mode, int max_accept,
+                      int math_on_full_accept, int32_t* rerun, int32_t* first_accept, int32_t* counters,
+                      float* margin_hist, int hist_cap, int32_t* any_rerun, unsigned long long cond, int after,
+                      void* stream);
 
 /* AR bookkeeping (std_qwen25vl.py:584-590).  std_ar_commit records
  * tok[b][0] as the next generated token of each running request and sets
@@ -318,6 +343,15 @@ int std_capture_while_begin(void* stream, void* body_stream, const int32_t* done
                             unsigned long long* handle_out, void** body_graph_out);
 int std_capture_while_end(void* body_stream, unsigned long long handle, const int32_t* done, int B, int32_t* counter,
                           int max_iters);
+/* IF conditional node (no reference counterpart; it runs the re-verification
+ * of std_verify_policy without a host round trip): std_graph_cond_handle
+ * creates a handle in the graph `stream` is capturing, for the kernel that
+ * sets it; std_capture_if_begin appends an IF node on that handle after the
+ * stream's captured work and starts capturing body_stream into its body;
+ * std_capture_if_end ends the body capture. */
+int std_graph_cond_handle(void* stream, unsigned long long* handle_out);
+int std_capture_if_begin(void* stream, void* body_stream, unsigned long long handle);
+int std_capture_if_end(void* body_stream);
 /* Launch accounting (no reference counterpart): how many kernel launches
  * this library has enqueued in this process so far, counting launches
  * recorded into CUDA graphs under stream capture.  Host-side counter. */

@@ -55,7 +55,12 @@ SIGNATURES: Dict[str, tuple] = {
                                       P]),
     "std_gemm_residual": (I, [P, P, P, P, PF, I, I, I, P]),
     "std_gemm_norm_silu_mul": (I, [P, PF, P, F, P, I, I, I, P, P, SZ, P]),
-    "std_gemm_norm_argmax": (I, [P, PF, P, F, P, I, I, I, I, I, I, I, PI32, P, P, SZ, P]),
+    "std_gemm_norm_argmax": (I, [P, PF, P, F, P, I, I, I, I, I, I, I, PI32, PF, P, P, SZ, P]),
+    "std_verify_policy": (I, [I, I, I, PI32, I, PI32, I, PI32, I, PI32, PI32, PI32, PF, F, I, I, I, PI32, PI32, PI32, PF,
+                              I, PI32, ctypes.c_ulonglong, I, P]),
+    "std_graph_cond_handle": (I, [P, P]),
+    "std_capture_if_begin": (I, [P, P, ctypes.c_ulonglong]),
+    "std_capture_if_end": (I, [P]),
     "std_rmsnorm": (I, [P, P, F, I, I, P, P]),
     "std_add_rmsnorm": (I, [P, P, P, F, I, I, P, P]),
     "std_rope_append": (I, [P, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I, P]),

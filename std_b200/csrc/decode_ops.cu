@@ -243,19 +243,22 @@ __global__ void add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, size_
 // 0), read 8 columns at a time from a row source (a logits matrix, or a
 // GEMM's split-K partials).  Written to out[(row / n) * out_stride +
 // out_start + row % n].
+// With margin_out, also the row's largest minus second-largest logit (equal
+// maxima give 0), written at the same index.
 template <class Src>
 __global__ void __launch_bounds__(1024) argmax_kernel(const Src logits, int V, int n, int out_stride, int out_start,
-                                                      int32_t* out) {
+                                                      int32_t* out, float* margin_out) {
   pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x;
-  float best = -INFINITY;
+  float best = -INFINITY, second = -INFINITY;
   int bi = 0x7fffffff;
   for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
     float v8[8];
     logits.load8(row, c, v8);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
+      second = fmaxf(second, fminf(best, v8[k]));
       if (v8[k] > best || (v8[k] == best && c + k < bi)) {
         best = v8[k];
         bi = c + k;
@@ -265,28 +268,34 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const Src logits, int V, i
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const float os = __shfl_xor_sync(0xffffffffu, second, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    second = fmaxf(fmaxf(second, os), fminf(best, ov));
     if (ov > best || (ov == best && oi < bi)) {
       best = ov;
       bi = oi;
     }
   }
-  __shared__ float s_v[32];
+  __shared__ float s_v[32], s_s[32];
   __shared__ int s_i[32];
   if ((threadIdx.x & 31) == 0) {
     s_v[threadIdx.x >> 5] = best;
+    s_s[threadIdx.x >> 5] = second;
     s_i[threadIdx.x >> 5] = bi;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      second = fmaxf(fmaxf(second, s_s[w]), fminf(best, s_v[w]));
       if (s_v[w] > best || (s_v[w] == best && s_i[w] < bi)) {
         best = s_v[w];
         bi = s_i[w];
       }
     }
     if (bi == 0x7fffffff) bi = 0;
-    out[(row / n) * out_stride + out_start + row % n] = bi;
+    const size_t o = static_cast<size_t>(row / n) * out_stride + out_start + row % n;
+    out[o] = bi;
+    if (margin_out != nullptr) margin_out[o] = best - second;
   }
 }
 
@@ -363,6 +372,117 @@ __global__ void accept_commit_kernel(const AcceptParams p) {
   p.dense_len[b] += p.pending + accept;
   p.sparse_len[b] += accept + 1;
   p.tok[static_cast<size_t>(b) * p.tok_stride] = bonus;
+}
+
+// ------------------------------- verification policy ---------------------
+// The reference's checks on a parallel verify (std_qwen25vl.py:816-884,
+// verification_policy.py:29-67), per request, before the round is committed:
+//   * margin check (verify_margin_threshold): the smallest top-1 minus top-2
+//     logit over the committed predictions i = 0..accept (verify row i with a
+//     pending bonus, i - 1 without; rows outside the block are skipped); a
+//     margin below the threshold is a "margin rerun" unless the fallback mode
+//     is sequential_on_low_margin;
+//   * math_on_full_accept: a full accept is re-verified (a fallback);
+//   * verify_fallback: sequential_guard always, sequential_on_reject when a
+//     draft was rejected, sequential_on_low_accept when additionally accept <=
+//     max_accept, sequential_on_low_margin on a low margin (a fallback, and a
+//     margin rerun too).
+// Every re-verification here is the exact replay of the round's dense
+// predictions (one token at a time); rerun[b] marks the requests that asked
+// for it, and the round's graph runs the replay when any request did.
+struct PolicyParams {
+  int B, gamma, pending, tok_stride, vstride, max_new, mode, max_accept, math_on_full_accept, hist_cap;
+  float threshold;  // NaN: no margin check
+  const int32_t* tok;
+  const int32_t* vpred;
+  const int32_t* dense_next;
+  const int32_t* n_gen;
+  const int32_t* done;
+  const int32_t* stats;   // [B, 4]; stats[b][0] = rounds committed so far (this round's index)
+  const float* margins;   // [B, vstride]
+  int32_t* rerun;         // [B]
+  int32_t* first_accept;  // [B]
+  int32_t* counters;      // [B, 3]: margin reruns, fallbacks, accepted extra
+  float* margin_hist;     // [B, hist_cap]: the round's smallest margin (NaN: none)
+  int32_t* any_rerun;     // [1]
+  unsigned long long cond;
+};
+
+STD_DEV int accepted_prefix(const int32_t* draft, const int32_t* vp, int pending, int dnext, int propose) {
+  int accept = 0;
+  while (accept < propose) {
+    const int pred = pending ? vp[accept] : (accept == 0 ? dnext : vp[accept - 1]);
+    if (draft[accept] != pred) break;
+    ++accept;
+  }
+  return accept;
+}
+
+enum PolicyMode : int { POL_NONE = 0, POL_ON_REJECT = 1, POL_ON_LOW_ACCEPT = 2, POL_ON_LOW_MARGIN = 3, POL_GUARD = 4 };
+
+__global__ void verify_policy_kernel(const PolicyParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = threadIdx.x;
+  int rr = 0;
+  if (b < p.B && !p.done[b]) {
+    const int32_t* draft = p.tok + static_cast<size_t>(b) * p.tok_stride + 1;
+    const int32_t* vp = p.vpred + static_cast<size_t>(b) * p.vstride;
+    const int propose = min(p.gamma, p.max_new - p.n_gen[b]);
+    const int accept = accepted_prefix(draft, vp, p.pending, p.dense_next[b], propose);
+    p.first_accept[b] = accept;
+    int32_t* cnt = p.counters + static_cast<size_t>(b) * 3;
+    bool low_margin = false;
+    if (!isnan(p.threshold)) {
+      float mmin = INFINITY;
+      bool any = false;
+      const int nq = p.gamma + p.pending;
+      for (int i = 0; i <= accept; ++i) {
+        const int row = p.pending ? i : i - 1;
+        if (row < 0 || row >= nq) continue;
+        mmin = fminf(mmin, p.margins[static_cast<size_t>(b) * p.vstride + row]);
+        any = true;
+      }
+      const int r = p.stats[b * 4];
+      if (r < p.hist_cap) p.margin_hist[static_cast<size_t>(b) * p.hist_cap + r] = any ? mmin : NAN;
+      low_margin = any && mmin < p.threshold;
+      if (low_margin && p.mode != POL_ON_LOW_MARGIN) {
+        cnt[0] += 1;
+        rr = 1;
+      }
+    }
+    if (p.math_on_full_accept && accept == propose) {
+      cnt[1] += 1;
+      rr = 1;
+    }
+    const bool seq = p.mode == POL_GUARD || (p.mode == POL_ON_LOW_MARGIN && low_margin) ||
+                     (p.mode == POL_ON_REJECT && accept < propose) ||
+                     (p.mode == POL_ON_LOW_ACCEPT && accept < propose && accept <= p.max_accept);
+    if (seq) {
+      cnt[1] += 1;
+      if (low_margin && p.mode == POL_ON_LOW_MARGIN) cnt[0] += 1;
+      rr = 1;
+    }
+  }
+  if (b < p.B) p.rerun[b] = rr;
+  const int any = __syncthreads_or(rr);
+  if (threadIdx.x == 0) {
+    *p.any_rerun = any;
+    if (p.cond != 0ull) cudaGraphSetConditional(static_cast<cudaGraphConditionalHandle>(p.cond), any ? 1u : 0u);
+  }
+}
+
+// After a replay: accepted-extra bookkeeping from the replayed predictions.
+__global__ void verify_policy_after_kernel(const PolicyParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = threadIdx.x;
+  if (b >= p.B || p.done[b] || !p.rerun[b]) return;
+  const int32_t* draft = p.tok + static_cast<size_t>(b) * p.tok_stride + 1;
+  const int32_t* vp = p.vpred + static_cast<size_t>(b) * p.vstride;
+  const int propose = min(p.gamma, p.max_new - p.n_gen[b]);
+  const int accept = accepted_prefix(draft, vp, p.pending, p.dense_next[b], propose);
+  if (accept > p.first_accept[b]) p.counters[static_cast<size_t>(b) * 3 + 2] += accept - p.first_accept[b];
 }
 
 // AR step bookkeeping (std_qwen25vl.py:584-590).  ar_commit records cur =
@@ -493,8 +613,8 @@ extern "C" int std_argmax_rows(const void* logits, int rows, int V, int n, int o
   if (rows <= 0 || V <= 0 || n <= 0) return 1;
   if (V % 8 != 0) return 1;
   return launch_pdl(stdb::argmax_kernel<stdb::Bf16Rows>, dim3(rows), dim3(1024), 0, static_cast<cudaStream_t>(stream),
-                    stdb::Bf16Rows{static_cast<const __nv_bfloat16*>(logits), V}, V, n, out_stride, out_start,
-                    out) == cudaSuccess
+                    stdb::Bf16Rows{static_cast<const __nv_bfloat16*>(logits), V}, V, n, out_stride, out_start, out,
+                    static_cast<float*>(nullptr)) == cudaSuccess
              ? 0
              : 4;
 }
@@ -527,6 +647,64 @@ extern "C" int std_accept_commit(int B, int gamma, int pending, int32_t* tok, in
   p.stats = stats;
   p.accept_hist = accept_hist;
   return launch_pdl(stdb::accept_commit_kernel, dim3((B + 127) / 128), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), p) == cudaSuccess
+             ? 0
+             : 4;
+}
+
+static stdb::PolicyParams policy_params(int B, int gamma, int pending, const int32_t* tok, int tok_stride,
+                                        const int32_t* vpred, int vstride, const int32_t* dense_next, int max_new,
+                                        const int32_t* n_gen, const int32_t* done, const int32_t* stats,
+                                        const float* margins, float threshold, int mode, int max_accept,
+                                        int math_on_full_accept, int32_t* rerun, int32_t* first_accept,
+                                        int32_t* counters, float* margin_hist, int hist_cap, int32_t* any_rerun,
+                                        unsigned long long cond) {
+  stdb::PolicyParams p;
+  p.B = B;
+  p.gamma = gamma;
+  p.pending = pending;
+  p.tok_stride = tok_stride;
+  p.vstride = vstride;
+  p.max_new = max_new;
+  p.mode = mode;
+  p.max_accept = max_accept;
+  p.math_on_full_accept = math_on_full_accept;
+  p.hist_cap = hist_cap;
+  p.threshold = threshold;
+  p.tok = tok;
+  p.vpred = vpred;
+  p.dense_next = dense_next;
+  p.n_gen = n_gen;
+  p.done = done;
+  p.stats = stats;
+  p.margins = margins;
+  p.rerun = rerun;
+  p.first_accept = first_accept;
+  p.counters = counters;
+  p.margin_hist = margin_hist;
+  p.any_rerun = any_rerun;
+  p.cond = cond;
+  return p;
+}
+
+extern "C" int std_verify_policy(int B, int gamma, int pending, const int32_t* tok, int tok_stride, const int32_t* vpred,
+                                 int vstride, const int32_t* dense_next, int max_new, const int32_t* n_gen,
+                                 const int32_t* done, const int32_t* stats, const float* margins, float threshold,
+                                 int mode, int max_accept, int math_on_full_accept, int32_t* rerun,
+                                 int32_t* first_accept, int32_t* counters, float* margin_hist, int hist_cap,
+                                 int32_t* any_rerun, unsigned long long cond, int after, void* stream) {
+  if (B <= 0 || B > 1024 || gamma < 1 || (pending != 0 && pending != 1) || vstride < gamma + pending) return 1;
+  if (mode < stdb::POL_NONE || mode > stdb::POL_GUARD || max_new <= 0 || hist_cap <= 0) return 1;
+  if (tok == nullptr || vpred == nullptr || dense_next == nullptr || n_gen == nullptr || done == nullptr ||
+      stats == nullptr || rerun == nullptr || first_accept == nullptr || counters == nullptr || any_rerun == nullptr)
+    return 1;
+  if (!isnan(threshold) && (margins == nullptr || margin_hist == nullptr)) return 1;
+  const stdb::PolicyParams p =
+      policy_params(B, gamma, pending, tok, tok_stride, vpred, vstride, dense_next, max_new, n_gen, done, stats,
+                    margins, threshold, mode, max_accept, math_on_full_accept, rerun, first_accept, counters,
+                    margin_hist, hist_cap, any_rerun, cond);
+  const int threads = ((B + 31) / 32) * 32;
+  return launch_pdl(after ? stdb::verify_policy_after_kernel : stdb::verify_policy_kernel, dim3(1), dim3(threads), 0,
                     static_cast<cudaStream_t>(stream), p) == cudaSuccess
              ? 0
              : 4;

@@ -53,6 +53,9 @@ struct GemmParams {
   // (order_key(value) << 32 | ~column): the maximum, first column on ties
   unsigned long long* amax_keys;
   int amax_rows;
+  // with amax_keys: also the two largest values of each row within each warp's
+  // 32 columns, amax_top2[(tile * 4 + warp) * M + t] (verify margins)
+  float2* amax_top2;
   // fused SiLU * up (splits == 1; weights in 64-row [gate | up] blocks): tile
   // rows 0..63 are gate, 64..127 up of features 64*tile ..; writes
   // act[t][64*tile + r] = bf16(bf16(silu(gate)) * up) instead of y
@@ -125,6 +128,21 @@ STD_DEV void norm_x_tile(uint8_t* tile, int nrows, int M, int k0, const float* s
 // Apply a split-K fixup epilogue to the tile's bf16 results y[t] (t < M) of
 // feature f = n0 + thread.  `yv(t)` returns them; s_y (>= 32 x 128 bf16) and
 // s_part (>= 4 x 32 floats) are free shared memory.
+// (a1, a2) <- the two largest of the (a1, a2) pairs of the warp's lanes
+// (a2 <= a1 in every pair; equal maxima give a2 == a1).
+STD_DEV void top2_merge(float& a1, float& a2, float b1, float b2) {
+  const float hi = fmaxf(a1, b1), lo = fminf(a1, b1);
+  a2 = fmaxf(lo, fmaxf(a2, b2));
+  a1 = hi;
+}
+STD_DEV void top2_warp(float& a1, float& a2) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float b1 = __shfl_xor_sync(0xffffffffu, a1, o), b2 = __shfl_xor_sync(0xffffffffu, a2, o);
+    top2_merge(a1, a2, b1, b2);
+  }
+}
+
 // Tokens handled here: t = t_first + i * t_step (the cluster rank's share).
 template <class YV>
 STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloat16* s_y, float* s_part,
@@ -217,8 +235,11 @@ __global__ void __launch_bounds__(GM_THREADS)
   const int S = p.stages;
   uint8_t* sW = smem;                 // [S][16 KB]
   uint8_t* sX = smem + S * GM_WTILE;  // [S][xtile]
-  // norm prologue: the CTA's K range of the norm weight, [nkb * 64] bf16
+  // norm prologue: the CTA's K range of the norm weight ([kmax] bf16, kmax =
+  // the largest split's K range), then the sums of squares [K/128][M] fp32
   __nv_bfloat16* s_normw = reinterpret_cast<__nv_bfloat16*>(sX + S * xtile);
+  float* s_ssq = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s_normw) +
+                                          ((p.kblocks + p.splits - 1) / p.splits) * GM_BK * 2);
   __shared__ __align__(8) uint64_t bar_full[GM_MAX_STAGES], bar_empty[GM_MAX_STAGES], bar_xready[GM_MAX_STAGES],
       bar_done;
   __shared__ uint32_t s_tmem;
@@ -297,17 +318,50 @@ __global__ void __launch_bounds__(GM_THREADS)
   } else if (norm && warp >= 2) {
     // ---- RMSNorm of the staged X tiles (warps 2-3) ----
     const int t = tid - 64;
+    // Global reads here are batched (eight or sixteen independent loads per
+    // thread before their stores): one memory latency per batch instead of
+    // one per element.
     // this CTA's columns of the norm weight (constant: before the wait)
-    for (int i = t; i < nkb * 8; i += 64)
-      reinterpret_cast<uint4*>(s_normw)[i] = *reinterpret_cast<const uint4*>(p.norm_w + kb0 * GM_BK + i * 8);
+    const int nw16 = nkb * 8;
+    const uint4* wsrc = reinterpret_cast<const uint4*>(p.norm_w + kb0 * GM_BK);
+    for (int base = 0; base < nw16; base += 64 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * 64 + t;
+        if (i < nw16) v[j] = wsrc[i];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = base + j * 64 + t;
+        if (i < nw16) reinterpret_cast<uint4*>(s_normw)[i] = v[j];
+      }
+    }
     pdl_wait();
     if (p.late_trigger) pdl_launch_dependents();
+    // per-tile sums of squares [K/128, M] -> shared; then each row adds its
+    // tiles in order
     const int ntiles_in = p.K / GM_BM;
+    const int nss = ntiles_in * p.M;
+    for (int base = 0; base < nss; base += 64 * 16) {
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int i = base + j * 64 + t;
+        v[j] = i < nss ? __ldcg(&p.norm_sumsq[i]) : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int i = base + j * 64 + t;
+        if (i < nss) s_ssq[i] = v[j];
+      }
+    }
+    named_bar_sync(1, 64);
     for (int r = t; r < p.nmma; r += 64) {
       float inv = 0.f;
       if (r < p.M) {
         float ss = 0.f;
-        for (int i = 0; i < ntiles_in; ++i) ss = __fadd_rn(ss, __ldcg(&p.norm_sumsq[static_cast<size_t>(i) * p.M + r]));
+        for (int i = 0; i < ntiles_in; ++i) ss = __fadd_rn(ss, s_ssq[i * p.M + r]);
         inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.K)), p.norm_eps));
       }
       s_inv[r] = inv;
@@ -356,6 +410,11 @@ __global__ void __launch_bounds__(GM_THREADS)
         key = other > key ? other : key;
       }
       if (lane == 0 && key != 0ull) atomicMax(&p.amax_keys[t], key);
+      if (p.amax_top2 != nullptr && t < p.amax_rows) {
+        float a1 = f < p.N ? bf16_round(__uint_as_float(v[j]) + bias) : -INFINITY, a2 = -INFINITY;
+        top2_warp(a1, a2);
+        if (lane == 0) p.amax_top2[static_cast<size_t>(tile * 4 + warp) * p.M + t] = make_float2(a1, a2);
+      }
     }
   }
   if (p.act != nullptr) {
@@ -569,6 +628,34 @@ __global__ void argmax_keys_kernel(unsigned long long* keys, int rows, int n, in
   keys[t] = 0ull;
 }
 
+// As argmax_keys_kernel, plus each row's top-1 minus top-2 logit from the
+// per-warp pairs in top2 [nsub, M] (one block per row):
+// margin_out[(t / n) * out_stride + out_start + t % n].
+__global__ void __launch_bounds__(256) argmax_margin_kernel(unsigned long long* keys, const float2* top2, int nsub,
+                                                            int M, int n, int out_stride, int out_start, int32_t* out,
+                                                            float* margin_out) {
+  __shared__ float2 s_w[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  float a1 = -INFINITY, a2 = -INFINITY;
+  for (int i = threadIdx.x; i < nsub; i += blockDim.x) {
+    const float2 v = top2[static_cast<size_t>(i) * M + t];
+    top2_merge(a1, a2, v.x, v.y);
+  }
+  top2_warp(a1, a2);
+  if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = make_float2(a1, a2);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) top2_merge(a1, a2, s_w[w].x, s_w[w].y);
+    const unsigned long long k = keys[t];
+    const size_t o = static_cast<size_t>(t / n) * out_stride + out_start + t % n;
+    out[o] = k == 0ull ? 0 : static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+    margin_out[o] = a1 - a2;
+    keys[t] = 0ull;
+  }
+}
+
 }  // namespace stdb
 
 // ---------------------------------------------------------------------------
@@ -621,6 +708,7 @@ struct GemmExtra {
   void* resid = nullptr;
   float* sumsq_out = nullptr;
   int late_trigger = 0;
+  void* amax_top2 = nullptr;
 };
 
 static int gemm_launch(const void* x, const void* w, const void* bias, void* y, float* partial, int M, int N, int K,
@@ -634,7 +722,8 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   const bool fused = ext != nullptr && ext->fixup != stdb::FIX_NONE;
   // norm prologue: the CTA's K range of the norm weight after the stages
   const uint32_t kmax = static_cast<uint32_t>((K / stdb::GM_BK + splits - 1) / splits) * stdb::GM_BK;
-  const uint32_t normw_bytes = norm ? kmax * 2u : 0u;
+  const uint32_t normw_bytes =
+      norm ? kmax * 2u + ((static_cast<uint32_t>(K / stdb::GM_BM) * static_cast<uint32_t>(M) * 4u + 15u) & ~15u) : 0u;
   if (norm) {
     stages = static_cast<int>((stdb::GM_SMEM_BUDGET - normw_bytes) / stage_bytes);
     stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
@@ -680,6 +769,7 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   p.resid = static_cast<__nv_bfloat16*>(e.resid);
   p.sumsq_out = e.sumsq_out;
   p.late_trigger = e.late_trigger;
+  p.amax_top2 = static_cast<float2*>(e.amax_top2);
   // may begin while the previous kernel in the stream finishes: the weight
   // tiles of the first stages are requested before griddepcontrol.wait
   const dim3 grid((N + stdb::GM_BM - 1) / stdb::GM_BM, splits);
@@ -811,7 +901,8 @@ extern "C" int std_gemm_argmax(const void* x, const void* w, int M, int N, int K
   int rc = gemm_launch(x, w, nullptr, workspace, static_cast<float*>(workspace), M, N, K, splits, s);
   if (rc != 0) return rc;
   return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,
-                    gemm_out_view(workspace, nullptr, splits, M, N), N, n, out_stride, out_start, out) == cudaSuccess
+                    gemm_out_view(workspace, nullptr, splits, M, N), N, n, out_stride, out_start, out,
+                    static_cast<float*>(nullptr)) == cudaSuccess
              ? 0
              : 4;
 }
@@ -847,7 +938,10 @@ extern "C" int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int
 // ---------------------------------------------------------------------------
 extern "C" size_t std_gemm_fused_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  return std_gemm_workspace_bytes(M, N, K);  // split partials for the norm + SiLU / argmax ops
+  // split partials for the norm + SiLU / argmax ops, or the argmax margins' per-warp top-2 pairs
+  const size_t part = std_gemm_workspace_bytes(M, N, K);
+  const size_t top2 = static_cast<size_t>((N + stdb::GM_BM - 1) / stdb::GM_BM) * 4 * M * sizeof(float2);
+  return part > top2 ? part : top2;
 }
 
 static bool fused_ws_ok(void* workspace, size_t workspace_bytes, int M, int N, int K) {
@@ -947,8 +1041,8 @@ extern "C" int std_gemm_norm_silu_mul(const void* x, const float* sumsq, const v
 
 extern "C" int std_gemm_norm_argmax(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w,
                                     int M, int N, int K, int rows_out, int n, int out_stride, int out_start,
-                                    int32_t* out, unsigned long long* keys, void* workspace, size_t workspace_bytes,
-                                    void* stream) {
+                                    int32_t* out, float* margin_out, unsigned long long* keys, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
   if (!gemm_shape_ok(x, w, M, N, K, 8) || out == nullptr || keys == nullptr || !norm_ok(sumsq, norm_w, K)) return 1;
   if (rows_out <= 0 || rows_out > M || n <= 0) return 1;
   GemmExtra e;
@@ -958,8 +1052,18 @@ extern "C" int std_gemm_norm_argmax(const void* x, const float* sumsq, const voi
   const int splits = gemm_splits(N, K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (splits == 1) {
+    if (margin_out != nullptr) {
+      if (!fused_ws_ok(workspace, workspace_bytes, M, N, K)) return 5;
+      e.amax_top2 = workspace;
+    }
     int rc = gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, keys, rows_out, nullptr, &e);
     if (rc != 0) return rc;
+    if (margin_out != nullptr)
+      return launch_pdl(stdb::argmax_margin_kernel, dim3(rows_out), dim3(256), 0, s, keys,
+                        static_cast<const float2*>(workspace), ((N + stdb::GM_BM - 1) / stdb::GM_BM) * 4, M, n,
+                        out_stride, out_start, out, margin_out) == cudaSuccess
+                 ? 0
+                 : 4;
     return launch_pdl(stdb::argmax_keys_kernel, dim3((rows_out + 127) / 128), dim3(128), 0, s, keys, rows_out, n,
                       out_stride, out_start, out) == cudaSuccess
                ? 0
@@ -970,7 +1074,8 @@ extern "C" int std_gemm_norm_argmax(const void* x, const float* sumsq, const voi
   int rc = gemm_launch(x, w, nullptr, partial, partial, M, N, K, splits, s, nullptr, 0, nullptr, &e);
   if (rc != 0) return rc;
   return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,
-                    gemm_out_view(partial, nullptr, splits, M, N), N, n, out_stride, out_start, out) == cudaSuccess
+                    gemm_out_view(partial, nullptr, splits, M, N), N, n, out_stride, out_start, out,
+                    margin_out) == cudaSuccess
              ? 0
              : 4;
 }

@@ -101,4 +101,50 @@ extern "C" int std_capture_while_end(void* body_stream, unsigned long long handl
   return (launch == cudaSuccess && end == cudaSuccess) ? 0 : 4;
 }
 
+// IF node: a conditional handle in the graph `stream` is capturing (for a
+// kernel that sets it), then the node after the stream's current work, with
+// `body_stream` capturing its body until std_capture_if_end.
+extern "C" int std_graph_cond_handle(void* stream, unsigned long long* handle_out) {
+  if (stream == nullptr || handle_out == nullptr) return 1;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  cudaGraph_t graph = nullptr;
+  if (cudaStreamGetCaptureInfo(static_cast<cudaStream_t>(stream), &st, nullptr, &graph, nullptr, nullptr) !=
+      cudaSuccess)
+    return 4;
+  if (st != cudaStreamCaptureStatusActive || graph == nullptr) return 1;
+  cudaGraphConditionalHandle h;
+  if (cudaGraphConditionalHandleCreate(&h, graph, 0, cudaGraphCondAssignDefault) != cudaSuccess) return 4;
+  *handle_out = static_cast<unsigned long long>(h);
+  return 0;
+}
+
+extern "C" int std_capture_if_begin(void* stream, void* body_stream, unsigned long long handle) {
+  if (stream == nullptr || body_stream == nullptr || stream == body_stream) return 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  cudaGraph_t graph = nullptr;
+  const cudaGraphNode_t* deps = nullptr;
+  size_t ndeps = 0;
+  if (cudaStreamGetCaptureInfo(s, &st, nullptr, &graph, &deps, &ndeps) != cudaSuccess) return 4;
+  if (st != cudaStreamCaptureStatusActive || graph == nullptr) return 1;
+  cudaGraphNodeParams np = {};
+  np.type = cudaGraphNodeTypeConditional;
+  np.conditional.handle = static_cast<cudaGraphConditionalHandle>(handle);
+  np.conditional.type = cudaGraphCondTypeIf;
+  np.conditional.size = 1;
+  cudaGraphNode_t node;
+  if (cudaGraphAddNode(&node, graph, deps, ndeps, &np) != cudaSuccess) return 4;
+  if (cudaStreamUpdateCaptureDependencies(s, &node, 1, cudaStreamSetCaptureDependencies) != cudaSuccess) return 4;
+  if (cudaStreamBeginCaptureToGraph(static_cast<cudaStream_t>(body_stream), np.conditional.phGraph_out[0], nullptr,
+                                    nullptr, 0, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+    return 4;
+  return 0;
+}
+
+extern "C" int std_capture_if_end(void* body_stream) {
+  if (body_stream == nullptr) return 1;
+  cudaGraph_t g = nullptr;
+  return cudaStreamEndCapture(static_cast<cudaStream_t>(body_stream), &g) == cudaSuccess ? 0 : 4;
+}
+
 extern "C" long long std_launch_count(void) { return g_std_launches.load(std::memory_order_relaxed); }

@@ -153,7 +153,8 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
                    tok: torch.Tensor, tok_start: int, pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor,
                    slot_off: int, lens: torch.Tensor, len_offset: int, sparse: bool,
                    argmax_out: Optional[torch.Tensor], argmax_stride: int = 1, argmax_start: int = 0,
-                   dense_attn=None, sparse_index=None, collector=None) -> None:
+                   dense_attn=None, sparse_index=None, collector=None,
+                   margin_out: Optional[torch.Tensor] = None) -> None:
     """One forward of n new tokens per request through all layers (graph-capturable).
 
     cache: [layers, 2, B, Hkv, cap, D].  sparse=True uses the draft kernel
@@ -168,7 +169,8 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     the draft reads its prompt rows from the dense cache by position and
     `cache` holds only the generated tokens' draft-path K/V (the tail).
     collector(li, q [B, n, Hq, D]) observes each layer's queries of a dense
-    forward (verification-guided re-selection).
+    forward (verification-guided re-selection).  margin_out (fp32, indexed
+    like argmax_out) receives each row's top-1 minus top-2 logit.
     """
     c = model.config
     M = B * n
@@ -209,7 +211,7 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     if argmax_out is None:
         return
     ops.gemm_norm_argmax(x, sumsq, model.norm, eps, model.lm_head, argmax_out, rows_out=M, n=n,
-                         out_stride=argmax_stride, out_start=argmax_start)
+                         out_stride=argmax_stride, out_start=argmax_start, margin_out=margin_out)
 
 
 # ---------------------------------------------------------------------- prefill

@@ -379,8 +379,9 @@ def gemm_norm_silu_mul(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Tenso
 
 def gemm_norm_argmax(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Tensor, eps: float, w: torch.Tensor,
                      out: torch.Tensor, rows_out: Optional[int] = None, n: int = 1, out_stride: int = 1,
-                     out_start: int = 0):
-    """Greedy argmax of rmsnorm(x) @ w^T's bf16 rows without storing the logits."""
+                     out_start: int = 0, margin_out: Optional[torch.Tensor] = None):
+    """Greedy argmax of rmsnorm(x) @ w^T's bf16 rows without storing the logits
+    (with margin_out, fp32 indexed like out: top-1 minus top-2 logit)."""
     M, K = x.shape
     N = w.shape[0]
     for t, nm in ((x, "x"), (w, "w"), (norm_w, "norm_w")):
@@ -389,9 +390,11 @@ def gemm_norm_argmax(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Tensor,
     rows_out = M if rows_out is None else rows_out
     keys = workspace("argmax_keys", M * 8, x.device)  # zero-initialised, left zero by every call
     ws = _fused_ws(M, N, K, x.device)
+    if margin_out is not None:
+        _check(margin_out, torch.float32, "margin_out")
     _lib.call("std_gemm_norm_argmax", x.data_ptr(), sumsq.data_ptr(), norm_w.data_ptr(), float(eps), w.data_ptr(), M, N,
-              K, rows_out, n, out_stride, out_start, out.data_ptr(), keys.data_ptr(), ws.data_ptr(), ws.numel(),
-              _stream())
+              K, rows_out, n, out_stride, out_start, out.data_ptr(), _p(margin_out), keys.data_ptr(), ws.data_ptr(),
+              ws.numel(), _stream())
     return out
 
 

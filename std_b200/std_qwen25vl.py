@@ -49,6 +49,10 @@ def topk_intersection_counts(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     pos = torch.searchsorted(b.contiguous(), a.contiguous()).clamp(max=k - 1)
     return ((b.gather(-1, pos) == a)).sum(dim=-1)
 VERIFY_MODES = ("parallel", "sequential")
+# verify_fallback values (std_qwen25vl.py:637-647) -> the policy kernel's mode
+VERIFY_FALLBACKS = {"none": 0, "sequential_on_reject": 1, "sequential_on_low_accept": 2,
+                    "sequential_on_low_margin": 3, "sequential_guard": 4}
+VERIFY_ATTN_BACKENDS = ("default", "math", "math_on_full_accept")
 
 
 @dataclass
@@ -235,7 +239,9 @@ class STDRunner:
                  use_graphs: bool = True, verify_mode: str = "parallel", shard=None,
                  sparse_cache: str = "compact", selection_policy: str = "static",
                  selection_update_interval: int = 1, min_selection_change_ratio: float = 0.0,
-                 device_loop: bool = True):
+                 device_loop: bool = True, verify_fallback: str = "none",
+                 verify_margin_threshold: Optional[float] = None, sequential_fallback_max_accept: int = 1,
+                 verify_attn_backend: str = "default"):
         c = model.config
         if gamma < 1 or 7 * (gamma + 1) > 126:
             raise ValueError("gamma must be in [1, 17]")
@@ -251,7 +257,25 @@ class STDRunner:
             raise ValueError("dynamic re-selection needs sparse_cache='indexed' (a selection change is an index update)")
         if selection_update_interval < 1 or not 0.0 <= min_selection_change_ratio <= 1.0:
             raise ValueError("selection_update_interval must be >= 1 and min_selection_change_ratio in [0, 1]")
+        if verify_fallback not in VERIFY_FALLBACKS:
+            raise ValueError(f"verify_fallback must be one of {tuple(VERIFY_FALLBACKS)}")
+        if sequential_fallback_max_accept < 0:
+            raise ValueError("sequential_fallback_max_accept must be non-negative.")
+        if verify_fallback == "sequential_on_low_margin" and verify_margin_threshold is None:
+            raise ValueError("sequential_on_low_margin requires verify_margin_threshold.")
+        if verify_margin_threshold is not None and verify_margin_threshold < 0:
+            raise ValueError("verify_margin_threshold must be non-negative.")
+        if verify_attn_backend not in VERIFY_ATTN_BACKENDS:
+            raise ValueError(f"verify_attn_backend must be one of {VERIFY_ATTN_BACKENDS}")
         self.verify_mode = verify_mode
+        # verification policies of a parallel verify (std_qwen25vl.py:816-884);
+        # every re-verification is the exact one-token-at-a-time replay
+        self.policy_mode = VERIFY_FALLBACKS[verify_fallback]
+        self.margin_threshold = verify_margin_threshold
+        self.max_accept = int(sequential_fallback_max_accept)
+        self.math_on_full_accept = verify_attn_backend == "math_on_full_accept"
+        self.policy_active = verify_mode == "parallel" and (
+            self.policy_mode != 0 or verify_margin_threshold is not None or self.math_on_full_accept)
         self.sparse_cache = sparse_cache
         self.dynamic = selection_policy == "previous_verify_topk"
         self.update_interval = selection_update_interval
@@ -310,6 +334,14 @@ class STDRunner:
         self.hist_cap = max_new_tokens + 1
         self.accept_hist = torch.zeros(B, self.hist_cap, **i32)
         self.all_done = torch.zeros(1, **i32)
+        # verification policy state
+        self.vmargin = torch.zeros(B, gamma + 1, dtype=torch.float32, device=dev)
+        self.rerun = torch.zeros(B, **i32)
+        self.first_accept = torch.zeros(B, **i32)
+        self.pol_counters = torch.zeros(B, 3, **i32)  # margin reruns, fallbacks, accepted extra
+        self.margin_hist = torch.full((B, self.hist_cap), float("nan"), dtype=torch.float32, device=dev)
+        self.any_rerun = torch.zeros(1, **i32)
+        self._if_stream: Optional[torch.cuda.Stream] = None
         self.all_done_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.topk = torch.zeros(c.num_hidden_layers, c.num_key_value_heads, k, **i32)
         self.topk_per_request: List[torch.Tensor] = []
@@ -402,6 +434,8 @@ class STDRunner:
         self.tok[:, 0] = self.dense_next   # AR: current token
         self.tok[:, 1] = self.dense_next   # STD: sparse_next = dense_next (copy_sparse_prefill)
         self.all_done.zero_()
+        self.pol_counters.zero_()
+        self.margin_hist.fill_(float("nan"))
         if self.dynamic:  # every decode starts from the static selection S_0
             self.topk_cur.copy_(self.topk_init)
             self._rebuild_selection()
@@ -469,7 +503,8 @@ class STDRunner:
                        tok_start=1 - pending, pos_base=self.dense_len, pos_off=0, slot_base=self.dense_len,
                        slot_off=-sh, lens=self.dense_len, len_offset=nq - sh, sparse=False,
                        argmax_out=self.vpred.view(-1), argmax_stride=self.gamma + 1, argmax_start=0,
-                       dense_attn=self.shard, collector=self._collect if self.dynamic else None)
+                       dense_attn=self.shard, collector=self._collect if self.dynamic else None,
+                       margin_out=self.vmargin.view(-1) if self.margin_threshold is not None else None)
 
     def _verify_sequential(self, pending: int) -> None:
         """verify_mode="sequential" (std_qwen25vl.py:504-528, :775-781, :885-893):
@@ -515,6 +550,48 @@ class STDRunner:
             self._verify_sequential(pending)
         else:
             self._verify(pending)
+            if self.policy_active:
+                self._policy(pending)
+
+    def _policy_call(self, pending: int, cond: int, after: int) -> None:
+        from . import _lib
+
+        thr = float("nan") if self.margin_threshold is None else float(self.margin_threshold)
+        _lib.call("std_verify_policy", self.B, self.gamma, pending, self.tok.data_ptr(), self.tok_stride,
+                  self.vpred.data_ptr(), self.gamma + 1, self.dense_next.data_ptr(), self.max_new,
+                  self.n_gen.data_ptr(), self.done.data_ptr(), self.stats.data_ptr(), self.vmargin.data_ptr(), thr,
+                  self.policy_mode, self.max_accept, 1 if self.math_on_full_accept else 0, self.rerun.data_ptr(),
+                  self.first_accept.data_ptr(), self.pol_counters.data_ptr(), self.margin_hist.data_ptr(),
+                  self.hist_cap, self.any_rerun.data_ptr(), cond, after, torch.cuda.current_stream().cuda_stream)
+
+    def _policy(self, pending: int) -> None:
+        """Decide, per request, whether this round's parallel verify is
+        re-verified (margin check, math_on_full_accept, verify_fallback), and
+        if any request asks, replay the round's dense predictions one token at
+        a time (the sequential verify) before the accept kernel commits.
+        Under graph capture the decision is an IF node whose condition the
+        policy kernel sets on the device; eagerly the host reads it."""
+        import ctypes
+
+        from . import _lib
+
+        if torch.cuda.is_current_stream_capturing():
+            s = torch.cuda.current_stream()
+            h = ctypes.c_ulonglong(0)
+            _lib.call("std_graph_cond_handle", s.cuda_stream, ctypes.byref(h))
+            self._policy_call(pending, h.value, 0)
+            if self._if_stream is None:
+                raise RuntimeError("capture() creates the replay stream before capturing")
+            _lib.call("std_capture_if_begin", s.cuda_stream, self._if_stream.cuda_stream, h.value)
+            with torch.cuda.stream(self._if_stream):
+                self._verify_sequential(pending)
+                self._policy_call(pending, 0, 1)
+            _lib.call("std_capture_if_end", self._if_stream.cuda_stream)
+            return
+        self._policy_call(pending, 0, 0)
+        if int(self.any_rerun.item()):
+            self._verify_sequential(pending)
+            self._policy_call(pending, 0, 1)
 
     def _post(self, pending: int, update: bool = False) -> None:
         self._accept(pending)
@@ -557,6 +634,8 @@ class STDRunner:
         reset afterwards."""
         if not self.use_graphs:
             return
+        if self.policy_active and self._if_stream is None:
+            self._if_stream = torch.cuda.Stream()
         want_std, want_ar = mode in ("std", "all"), mode in ("ar", "all")
         if self.shard is not None:
             # collectives stay outside the graphs: the dense forwards (verify,
@@ -747,6 +826,8 @@ class STDRunner:
         phases = {"drafts": self._drafts, "verify_first": lambda: self._verify_phase(0),
                   "verify": lambda: self._verify_phase(1), "accept_first": lambda: self._accept_and_flag(0),
                   "accept": lambda: self._accept_and_flag(1), "bonus": self._bonus_step}
+        if self.policy_active and self._if_stream is None:
+            self._if_stream = torch.cuda.Stream()
         if self.use_graphs and any("phase_" + name not in self._graphs for name in phases):
             # Warm up with whole rounds (workspaces, kernel attributes), never
             # with a phase out of its round: a bonus step run straight after
@@ -863,6 +944,9 @@ class STDRunner:
                 props.append(min(self.gamma, remaining))
                 n_gen += min(a + 1, remaining)
             proposed.append(props)
+        pc = self.pol_counters.cpu()
+        mh = self.margin_hist.cpu()
+        margins = [[float(m) for m in mh[b, : rounds[b]].tolist() if m == m] for b in range(self.B)]
         return {
             "rounds": rounds,
             "accepted": st[:, 1].tolist(),
@@ -870,6 +954,10 @@ class STDRunner:
             "accept_lengths": accept,
             "proposed_lengths": proposed,
             "pending_lengths": [[0] + [1] * (r - 1) if r > 0 else [] for r in rounds],
+            "verify_margin_reruns": pc[:, 0].tolist(),
+            "fallback_count": pc[:, 1].tolist(),
+            "fallback_accepted_extra": pc[:, 2].tolist(),
+            "verify_margins": margins,
         }
 
 
@@ -896,6 +984,9 @@ def _std_result(runner: STDRunner, ids: torch.Tensor, decoding_time: float, t0: 
         decode_rounds=int(max(st["rounds"])), final_gamma=gamma, gamma_history=[gamma] * int(max(st["rounds"])),
         accept_lengths=acc, proposed_lengths=[p for r in st["proposed_lengths"] for p in r],
         pending_lengths=[p for r in st["pending_lengths"] for p in r],
+        fallback_count=int(sum(st["fallback_count"])), fallback_accepted_extra=int(sum(st["fallback_accepted_extra"])),
+        verify_margin_reruns=int(sum(st["verify_margin_reruns"])),
+        min_verify_margin=min((m for r in st["verify_margins"] for m in r), default=0.0),
         draft_time=prof.get("draft_time", 0.0), verify_time=prof.get("verify_time", 0.0),
         bonus_time=prof.get("bonus_time", 0.0), cache_adjust_time=prof.get("cache_adjust_time", 0.0),
         prefill_time=tp["prefill_time"], selection_time=tp["selection_time"],
@@ -965,22 +1056,26 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                           sparse_cache: str = "compact") -> Tuple[GenerateResult, SparseSelection]:
     """Sparse-to-Dense greedy decoding (std_qwen25vl.py:609-978).
 
-    Implemented: verify_mode="parallel" | "sequential", verify_fallback="none",
-    sparse_attn_mode="b200", copy_sparse_prefill=True, fixed gamma.  Other
-    values of the reference's research flags raise ValueError (there is no
-    alternative backend to dispatch to).  B200 extension: sparse_cache=
+    Implemented: verify_mode "parallel" | "sequential"; every verify_fallback
+    mode, verify_margin_threshold (with min_verify_margin and
+    verify_margin_reruns) and verify_attn_backend "default" | "math" |
+    "math_on_full_accept", decided per request on the device; a
+    re-verification (the reference's math-backend rerun or sequential
+    fallback) is the exact one-token-at-a-time replay of the round's dense
+    predictions.  The verify kernel is the only attention backend, so "math"
+    runs it too (it is already exact: a verify row equals the AR step's row bit
+    for bit).  sparse_attn_mode="b200", copy_sparse_prefill=True, fixed gamma;
+    adaptive gamma and torch.compile raise ValueError.  profile_decode=True
+    fills draft_time / verify_time / cache_adjust_time / bonus_time from CUDA
+    events between the round's phases.  B200 extension: sparse_cache=
     "indexed" reads the selected prompt rows in place from the dense cache
     instead of compacting a copy (same tokens)."""
     if verify_mode not in VERIFY_MODES:
         raise ValueError(f"Unsupported verify_mode={verify_mode!r}; expected one of {VERIFY_MODES}.")
-    if verify_fallback != "none":
-        raise ValueError("verify_fallback other than 'none' is not part of the B200 path.")
     if sparse_attn_mode not in SPARSE_ATTN_MODES:
         raise ValueError(f"Unsupported sparse_attn_mode={sparse_attn_mode!r}; expected 'b200'.")
     if adaptive_gamma_min is not None or use_compile or not copy_sparse_prefill:
         raise ValueError("adaptive gamma, torch.compile and a separate sparse prefill are not part of the B200 path.")
-    if verify_attn_backend != "default":
-        raise ValueError("verify_attn_backend must be 'default' (the verify kernel is the only backend).")
     torch.cuda.synchronize()
     t0 = time.time()
     ids, layout, embeds = _prepare(model, inputs, video_token_id)
@@ -988,9 +1083,13 @@ def std_generate_qwen25vl(model: Qwen25VLDecoder, inputs: Dict[str, torch.Tensor
                          explicit_k)
     if runner is None:
         runner = STDRunner(model, ids.shape[0], layout, max_new_tokens, gamma=gamma, k=k, eos_token_id=eos_token_id,
-                           ignore_eos=ignore_eos, verify_mode=verify_mode, sparse_cache=sparse_cache)
-    elif runner.verify_mode != verify_mode:
-        raise ValueError("the runner was built for a different verify_mode")
+                           ignore_eos=ignore_eos, verify_mode=verify_mode, sparse_cache=sparse_cache,
+                           verify_fallback=verify_fallback, verify_margin_threshold=verify_margin_threshold,
+                           sequential_fallback_max_accept=sequential_fallback_max_accept,
+                           verify_attn_backend=verify_attn_backend)
+    elif (runner.verify_mode != verify_mode or runner.policy_mode != VERIFY_FALLBACKS.get(verify_fallback)
+          or runner.margin_threshold != verify_margin_threshold):
+        raise ValueError("the runner was built for a different verify_mode / verification policy")
     tp = runner.prefill(embeds, with_selection=True)
     prof = None
     if profile_decode and runner.shard is None:

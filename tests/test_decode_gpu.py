@@ -450,3 +450,61 @@ def test_qwen25vl_7b_std_equals_ar_and_selection_bit_exact():
     assert ops.device_error() == 0
     assert int(runner.n_gen.min()) == max_new
     assert torch.equal(std_tokens, ar_tokens)
+
+
+@pytest.mark.parametrize("full", [False, True])
+def test_verification_policies_count_and_keep_tokens(full):
+    """verify_margin_threshold, verify_fallback and math_on_full_accept
+    (std_qwen25vl.py:816-884): the device policy re-verifies exactly the rounds
+    the reference's rules select -- counted against each request's round
+    records -- the replay never changes a decision (accepted extra 0, same
+    accept lengths), and tokens stay equal to AR."""
+    from std_b200 import ops
+    from std_b200.model import TINY, Qwen25VLDecoder
+    from std_b200.std_qwen25vl import STDRunner, _prepare, selection_budget
+
+    model = Qwen25VLDecoder(TINY, seed=8)
+    B, V, T, gamma, max_new = 2, 400, 20, 4, 24
+    inp = _inputs(B, V, T, TINY.vocab_size, TINY.hidden_size, seed=51)
+    ids, layout, embeds = _prepare(model, inp, VIDEO)
+    k = V if full else selection_budget(layout.prompt_len, layout.text_start, V, 100, None)
+    base = STDRunner(model, B, layout, max_new, gamma=gamma, k=k, ignore_eos=True)
+    base.prefill(embeds)
+    base.run_std()
+    ref_tokens, ref_st = base.out_tokens.cpu().clone(), base.std_stats()
+    base.run_ar()
+    ar_tokens = base.out_tokens.cpu().clone()
+    assert torch.equal(ref_tokens, ar_tokens)
+    acc, props = ref_st["accept_lengths"], ref_st["proposed_lengths"]
+
+    def margin_rounds(b):  # rounds whose committed predictions include a verify row
+        return sum(1 for r, a in enumerate(acc[b]) if r > 0 or a > 0)
+
+    cases = [
+        (dict(verify_margin_threshold=1e9), lambda b: margin_rounds(b), lambda b: 0),
+        (dict(verify_margin_threshold=0.0), lambda b: 0, lambda b: 0),
+        (dict(verify_fallback="sequential_guard"), lambda b: 0, lambda b: len(acc[b])),
+        (dict(verify_fallback="sequential_on_reject"), lambda b: 0,
+         lambda b: sum(a < p for a, p in zip(acc[b], props[b]))),
+        (dict(verify_fallback="sequential_on_low_accept", sequential_fallback_max_accept=0), lambda b: 0,
+         lambda b: sum(a < p and a == 0 for a, p in zip(acc[b], props[b]))),
+        (dict(verify_fallback="sequential_on_low_margin", verify_margin_threshold=1e9), lambda b: margin_rounds(b),
+         lambda b: margin_rounds(b)),
+        (dict(verify_attn_backend="math_on_full_accept"), lambda b: 0,
+         lambda b: sum(a == p for a, p in zip(acc[b], props[b]))),
+    ]
+    for kw, want_reruns, want_fallbacks in cases:
+        r = STDRunner(model, B, layout, max_new, gamma=gamma, k=k, ignore_eos=True, **kw)
+        r.prefill(embeds)
+        r.run_std()
+        st = r.std_stats()
+        assert torch.equal(r.out_tokens.cpu(), ref_tokens), kw
+        assert st["accept_lengths"] == acc, kw
+        for b in range(B):
+            assert st["verify_margin_reruns"][b] == want_reruns(b), (kw, b)
+            assert st["fallback_count"][b] == want_fallbacks(b), (kw, b)
+            assert st["fallback_accepted_extra"][b] == 0
+            if "verify_margin_threshold" in kw:
+                assert len(st["verify_margins"][b]) == margin_rounds(b)
+                assert all(m >= 0 for m in st["verify_margins"][b])
+    assert ops.device_error() == 0
