@@ -239,6 +239,11 @@ int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, 
  * their reduction kernel when K is split); it must not be shared by launches
  * that run concurrently. */
 size_t std_gemm_fused_workspace_bytes(int M, int N, int K);
+/* Tuning (no reference counterpart): the per-CTA shared-memory budget of the
+ * GEMMs' stage ring, 40..200 KiB (default 104 KiB, two CTAs per SM).  A
+ * smaller ring leaves room for the next kernel's CTAs on the same SM.
+ * Applies to launches issued after the call, process-wide. */
+int std_gemm_set_smem_budget(int bytes);
 /* Replaces: nn.Embedding (modeling_qwen2_5_vl.py:1336) of a decode step:
  * out[b*n + j] = table[tok[b*tok_stride + tok_start + j]] (rows [B*n, H]) and
  * sumsq [H/128, ld] of those rows (ld >= B*n, the row count of the GEMMs
@@ -352,6 +357,9 @@ int std_capture_while_end(void* body_stream, unsigned long long handle, const in
 int std_graph_cond_handle(void* stream, unsigned long long* handle_out);
 int std_capture_if_begin(void* stream, void* body_stream, unsigned long long handle);
 int std_capture_if_end(void* body_stream);
+/* A new non-blocking CUDA stream on the current device, for capturing
+ * conditional bodies (a stream distinct from every pooled stream). */
+int std_stream_create(void** stream_out);
 /* Launch accounting (no reference counterpart): how many kernel launches
  * this library has enqueued in this process so far, counting launches
  * recorded into CUDA graphs under stream capture.  Host-side counter. */

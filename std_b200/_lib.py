@@ -50,6 +50,7 @@ SIGNATURES: Dict[str, tuple] = {
     "std_gemm_rope_append": (I, [P, P, P, I, I, I, I, I, I, P, I, P, I, P, P, I, P, P, P, I, P, SZ, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
     "std_gemm_fused_workspace_bytes": (SZ, [I, I, I]),
+    "std_gemm_set_smem_budget": (I, [I]),
     "std_embed_sumsq": (I, [P, I, I, PI32, I, I, I, I, P, PF, I, P]),
     "std_gemm_norm_rope_append": (I, [P, PF, P, F, P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I,
                                       P]),
@@ -61,6 +62,7 @@ SIGNATURES: Dict[str, tuple] = {
     "std_graph_cond_handle": (I, [P, P]),
     "std_capture_if_begin": (I, [P, P, ctypes.c_ulonglong]),
     "std_capture_if_end": (I, [P]),
+    "std_stream_create": (I, [P]),
     "std_rmsnorm": (I, [P, P, F, I, I, P, P]),
     "std_add_rmsnorm": (I, [P, P, P, F, I, I, P, P]),
     "std_rope_append": (I, [P, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I, P]),
@@ -80,6 +82,24 @@ _STATUS = {1: "bad shape or argument", 2: "capacity exceeded", 3: "unsupported d
            4: "CUDA launch error", 5: "workspace missing or too small"}
 
 _lib = None
+
+
+_CAPTURE_STREAMS: Dict[tuple, object] = {}
+
+
+def capture_stream(role: str):
+    """A dedicated CUDA stream (torch.cuda.ExternalStream) per (role, device)
+    for capturing conditional-node bodies; created once by the library."""
+    import torch
+
+    key = (role, torch.cuda.current_device())
+    st = _CAPTURE_STREAMS.get(key)
+    if st is None:
+        ptr = ctypes.c_void_p(0)
+        call("std_stream_create", ctypes.byref(ptr))
+        st = torch.cuda.ExternalStream(ptr.value)
+        _CAPTURE_STREAMS[key] = st
+    return st
 
 
 def load() -> ctypes.CDLL:

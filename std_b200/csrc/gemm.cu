@@ -21,6 +21,9 @@
 // the (N, K)-fixed split and the MMA N (the padded token count) -- not on the
 // other rows -- so callers that keep the padded count fixed (the dense decode
 // forwards) get bit-identical rows for AR steps and verify blocks.
+#include <map>
+#include <tuple>
+
 #include "common.cuh"
 
 namespace stdb {
@@ -28,7 +31,7 @@ namespace stdb {
 constexpr int GM_BM = 128;         // output features per CTA (MMA M)
 constexpr int GM_BK = 64;          // K per stage (one 128-B swizzle row)
 constexpr int GM_MAX_STAGES = 8;
-constexpr uint32_t GM_SMEM_BUDGET = 104 * 1024;  // per CTA: two CTAs per SM
+constexpr uint32_t GM_SMEM_BUDGET = 104 * 1024;  // default per-CTA stage budget: two CTAs per SM
 constexpr int GM_THREADS = 128;
 constexpr uint32_t GM_WTILE = GM_BM * GM_BK * 2;  // 16 KB
 
@@ -682,11 +685,67 @@ static int gemm_splits(int N, int K) {
 
 static int gemm_nmma(int M) { return ((M + 15) / 16) * 16; }
 
-// Splits of a GEMM whose split-K sum is reduced inside one cluster: at most
-// 8 (the portable cluster size).
+// How many clusters of `cluster` gemm_kernel CTAs (with `smem` bytes of
+// dynamic shared memory) the current device runs at once; 0 when unknown.
+// Clusters are placed within one GPC, so this can be well below
+// (SMs x CTAs per SM) / cluster.  Cached per (device, cluster, smem).
+static int gemm_active_clusters(int cluster, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, cluster, smem);
+  std::lock_guard<std::mutex> lock(mu);
+  const auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  static SmemGrant grant;
+  int n = 0;
+  if (ensure_smem(stdb::gemm_kernel, grant, smem) == 0) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = cluster;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, cluster);
+    cfg.blockDim = dim3(stdb::GM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, stdb::gemm_kernel, &cfg) != cudaSuccess) n = 0;
+    cudaGetLastError();
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Splits of a GEMM whose split-K sum is reduced inside one cluster (at most
+// 8, the portable cluster size): the largest count whose clusters -- one per
+// 128-feature tile -- all run in one wave; with none, the count of fewest
+// waves.  Depends on (N, K) and the device only, so every call on a weight
+// matrix (an AR step, a verify block) splits K the same way.
 static int gemm_splits_cluster(int N, int K) {
-  const int s = gemm_splits(N, K);
-  return s > 8 ? 8 : s;
+  const int tiles = (N + stdb::GM_BM - 1) / stdb::GM_BM;
+  const int kblocks = K / stdb::GM_BK;
+  int s_max = gemm_splits(N, K);
+  if (s_max > 8) s_max = 8;
+  if (s_max <= 1) return 1;
+  // shared memory of a two-CTA-per-SM launch (the ring budget; the norm
+  // prologue's extra rows are a few KB within the same 2-per-SM bound)
+  const size_t smem = static_cast<size_t>(stdb::GM_SMEM_BUDGET) + 1024;
+  int best = s_max, best_waves = 1 << 30;
+  for (int s = s_max; s >= 2; --s) {
+    if (kblocks / s < 2) continue;
+    const int active = gemm_active_clusters(s, smem);
+    if (active <= 0) return s_max;  // occupancy unknown: keep the wave heuristic
+    const int waves = (tiles + active - 1) / active;
+    if (waves == 1) return s;
+    if (waves < best_waves) {
+      best_waves = waves;
+      best = s;
+    }
+  }
+  return best;
 }
 
 extern "C" size_t std_gemm_workspace_bytes(int M, int N, int K) {
@@ -711,12 +770,24 @@ struct GemmExtra {
   void* amax_top2 = nullptr;
 };
 
+// Per-CTA shared-memory budget for the stage ring (the ring depth follows
+// from it).  A smaller budget leaves room on each SM for the next kernel's
+// CTAs, which then start streaming their weights before this one ends.
+static std::atomic<uint32_t> g_gemm_smem_budget{stdb::GM_SMEM_BUDGET};
+
+extern "C" int std_gemm_set_smem_budget(int bytes) {
+  if (bytes < 40 * 1024 || bytes > 200 * 1024) return 1;
+  g_gemm_smem_budget.store(static_cast<uint32_t>(bytes));
+  return 0;
+}
+
 static int gemm_launch(const void* x, const void* w, const void* bias, void* y, float* partial, int M, int N, int K,
                        int splits, cudaStream_t s, unsigned long long* amax_keys = nullptr, int amax_rows = 0,
                        void* act = nullptr, const GemmExtra* ext = nullptr) {
   const int nmma = gemm_nmma(M);
   const uint32_t stage_bytes = stdb::GM_WTILE + static_cast<uint32_t>(nmma) * stdb::GM_BK * 2;
-  int stages = static_cast<int>(stdb::GM_SMEM_BUDGET / stage_bytes);
+  const uint32_t budget = g_gemm_smem_budget.load();
+  int stages = static_cast<int>(budget / stage_bytes);
   stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
   const bool norm = ext != nullptr && ext->norm_w != nullptr;
   const bool fused = ext != nullptr && ext->fixup != stdb::FIX_NONE;
@@ -725,7 +796,7 @@ static int gemm_launch(const void* x, const void* w, const void* bias, void* y, 
   const uint32_t normw_bytes =
       norm ? kmax * 2u + ((static_cast<uint32_t>(K / stdb::GM_BM) * static_cast<uint32_t>(M) * 4u + 15u) & ~15u) : 0u;
   if (norm) {
-    stages = static_cast<int>((stdb::GM_SMEM_BUDGET - normw_bytes) / stage_bytes);
+    stages = static_cast<int>((budget - normw_bytes) / stage_bytes);
     stages = stages < 2 ? 2 : (stages > stdb::GM_MAX_STAGES ? stdb::GM_MAX_STAGES : stages);
   }
   // a fused fixup stages the tile's fp32 accumulator ([M][128]) and a 32-row

@@ -147,4 +147,16 @@ extern "C" int std_capture_if_end(void* body_stream) {
   return cudaStreamEndCapture(static_cast<cudaStream_t>(body_stream), &g) == cudaSuccess ? 0 : 4;
 }
 
+// A stream of its own for capturing a conditional body (non-blocking, never
+// destroyed): torch hands out pooled streams, so two of its streams can be
+// the same CUDA stream, and a body must be captured on a stream that is not
+// the one capturing its parent graph.
+extern "C" int std_stream_create(void** stream_out) {
+  if (stream_out == nullptr) return 1;
+  cudaStream_t s = nullptr;
+  if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return 4;
+  *stream_out = s;
+  return 0;
+}
+
 extern "C" long long std_launch_count(void) { return g_std_launches.load(std::memory_order_relaxed); }

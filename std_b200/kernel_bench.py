@@ -3,6 +3,7 @@
     python -m std_b200.kernel_bench --kernel verify --B 8 --L 32906 --nq 10
     python -m std_b200.kernel_bench --kernel draft  --B 8 --L 1025
     python -m std_b200.kernel_bench --kernel gemm   --M 8 --N 4608 --K 3584 [--cublas]
+    python -m std_b200.kernel_bench --kernel forward --B 8 --L 32906 [--gamma 9]
 
 Each repetition cycles through `--caches` distinct K/V caches (default: as
 many as keep the total above 256 MB, i.e. larger than the 126 MB L2), so the
@@ -14,6 +15,11 @@ adds the host cost of each call).  Prints achieved algorithmic GB/s:
           step, STD_DRAFT_AFTER_APPEND: the preceding draft launch writes none
           of its inputs)
   gemm:   2*N*K (weights) + 2*M*K + 2*M*N bytes per launch
+  forward: one sparse (draft) forward and one dense verify forward of the
+          7B-shaped decoder (random init) at B requests, as the decode loop
+          runs them (CUDA graph, one launch sequence each), with sparse
+          caches of L_s = K+text+1 keys and dense caches of L keys; the weight
+          bytes (14.1 GB) dominate.
 This is also the target command of the ncu captures summarised in profiles/.
 """
 
@@ -30,7 +36,9 @@ from .timing import graph_time_us
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["verify", "draft", "gemm"], default="verify")
+    ap.add_argument("--kernel", choices=["verify", "draft", "gemm", "forward"], default="verify")
+    ap.add_argument("--gamma", type=int, default=9)
+    ap.add_argument("--sparse-len", type=int, default=1025)
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=4608)
     ap.add_argument("--K", type=int, default=3584)
@@ -48,6 +56,8 @@ def main() -> None:
     torch.cuda.set_device(dev)
     if a.kernel == "gemm":
         return gemm_bench(a, dev)
+    if a.kernel == "forward":
+        return forward_bench(a, dev)
     B, L = a.B, a.L
     cap = (L + 255) // 256 * 256
     per_cache = 2 * B * 4 * cap * 128 * 2
@@ -115,6 +125,50 @@ def gemm_bench(a, dev) -> None:
     nbytes = 2 * N * K + 2 * M * K + 2 * M * N
     print(json.dumps({"kernel": "cublas" if a.cublas else "gemm", "M": M, "N": N, "K": K, "weights": n_w,
                       "launch_us": us, "algorithmic_bytes": nbytes, "achieved_gbs": nbytes / us / 1e3}))
+
+
+def forward_bench(a, dev) -> None:
+    """Graph-timed sparse (draft) and dense (verify) decode forwards."""
+    from .model import QWEN25_VL_7B, Qwen25VLDecoder, Workspace, decode_forward
+
+    c = QWEN25_VL_7B
+    B, L, gamma = a.B, a.L, a.gamma
+    model = Qwen25VLDecoder(c, seed=2, device=str(dev))
+    Hkv, D = c.num_key_value_heads, c.head_dim
+    cap_s = (a.sparse_len + gamma + 64 + 63) // 64 * 64
+    cap_d = (L + gamma + 2 + 127) // 128 * 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    sparse = torch.randn(c.num_hidden_layers, 2, B, Hkv, cap_s, D, generator=g, device=dev).to(torch.bfloat16)
+    dense = torch.empty(c.num_hidden_layers, 2, B, Hkv, cap_d, D, device=dev, dtype=torch.bfloat16)
+    dense.normal_(generator=g)
+    model.rope_tables(cap_d + 2)
+    rows = (B * (gamma + 1) + 15) // 16 * 16
+    ws = Workspace(model, rows)
+    i32 = dict(dtype=torch.int32, device=dev)
+    tok = torch.randint(0, 1000, (B, gamma + 2), generator=g, device=dev, dtype=torch.int32)
+    s_len = torch.full((B,), a.sparse_len - 1, **i32)
+    d_len = torch.full((B,), L - gamma - 1, **i32)
+    ctx = torch.full((B,), L - gamma - 1, **i32)
+    out = torch.zeros(B * (gamma + 2), **i32)
+
+    def sparse_fwd():
+        decode_forward(model, ws, sparse, B=B, n=1, rows=B, tok=tok, tok_start=1, pos_base=ctx, pos_off=0,
+                       slot_base=s_len, slot_off=0, lens=s_len, len_offset=1, sparse=True, argmax_out=out,
+                       argmax_stride=gamma + 2, argmax_start=2)
+
+    def dense_fwd():
+        decode_forward(model, ws, dense, B=B, n=gamma + 1, rows=rows, tok=tok, tok_start=0, pos_base=d_len, pos_off=0,
+                       slot_base=d_len, slot_off=0, lens=d_len, len_offset=gamma + 1, sparse=False, argmax_out=out,
+                       argmax_stride=gamma + 2, argmax_start=0)
+
+    res = {}
+    for name, fn in (("sparse_forward", sparse_fwd), ("dense_forward", dense_fwd)):
+        res[name + "_us"] = graph_time_us([fn], rounds=4)
+    wbytes = 2 * model.num_params() - 2 * c.vocab_size * c.hidden_size  # the embedding table is not streamed
+    res.update(B=B, L=L, sparse_len=a.sparse_len, gamma=gamma, weight_bytes=wbytes,
+               weight_stream_us=wbytes / 6548.5e3)
+    assert ops.device_error() == 0
+    print(json.dumps(res))
 
 
 if __name__ == "__main__":

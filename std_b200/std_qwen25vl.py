@@ -42,6 +42,12 @@ SPARSE_CACHE_MODES = ("compact", "indexed")
 SELECTION_POLICIES = ("static", "previous_verify_topk")
 
 
+def _lib_capture_stream(role: str):
+    from . import _lib
+
+    return _lib.capture_stream(role)
+
+
 def topk_intersection_counts(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """|a ∩ b| over the last dim of two selections of unique, ascending
     positions (dynamic_selection.py:85-101), on the selections' device."""
@@ -635,7 +641,7 @@ class STDRunner:
         if not self.use_graphs:
             return
         if self.policy_active and self._if_stream is None:
-            self._if_stream = torch.cuda.Stream()
+            self._if_stream = _lib_capture_stream("if_body")
         want_std, want_ar = mode in ("std", "all"), mode in ("ar", "all")
         if self.shard is not None:
             # collectives stay outside the graphs: the dense forwards (verify,
@@ -690,7 +696,7 @@ class STDRunner:
         from . import _lib
 
         if self._body_stream is None:
-            self._body_stream = torch.cuda.Stream()
+            self._body_stream = _lib_capture_stream("while_body")
         body_stream = self._body_stream
         limit = self.max_new + 1
 
@@ -827,7 +833,7 @@ class STDRunner:
                   "verify": lambda: self._verify_phase(1), "accept_first": lambda: self._accept_and_flag(0),
                   "accept": lambda: self._accept_and_flag(1), "bonus": self._bonus_step}
         if self.policy_active and self._if_stream is None:
-            self._if_stream = torch.cuda.Stream()
+            self._if_stream = _lib_capture_stream("if_body")
         if self.use_graphs and any("phase_" + name not in self._graphs for name in phases):
             # Warm up with whole rounds (workspaces, kernel attributes), never
             # with a phase out of its round: a bonus step run straight after
