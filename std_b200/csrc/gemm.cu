@@ -146,29 +146,76 @@ STD_DEV void top2_warp(float& a1, float& a2) {
   }
 }
 
-// Tokens handled here: t = t_first + i * t_step (the cluster rank's share).
-template <class YV>
-STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloat16* s_y, float* s_part,
-                        int t_first, int t_step) {
+// ---- split-K fixup (FIX_ROPE / FIX_RESID) ----------------------------------
+// The fixup of a tile runs on the tokens t = t_first + i * t_step (this
+// cluster rank's share), FX_TB tokens at a time.  Every global and
+// distributed-shared-memory read of a batch is issued before any of its
+// results is used, so a batch costs about one memory latency, not one per
+// token and split.
+constexpr int FX_TB = 8;
+constexpr int FX_MAX_SPLITS = 8;
+
+// y[j] = bf16(sum over splits, in split order, of the tile's fp32 partial for
+// token tt[j] and this thread's feature, + fb), j < n.  s_acc: this CTA's
+// stage [M][128]; with splits > 1 the partials are read from every cluster
+// rank's stage at the same offset (my_acc = this thread's column of s_acc).
+STD_DEV void fixup_sums(const GemmParams& p, const float* s_acc, uint32_t my_acc, float fb, const int (&tt)[FX_TB],
+                        int n, float (&y)[FX_TB]) {
+  float v[FX_MAX_SPLITS][FX_TB];
+  if (p.splits == 1) {
+#pragma unroll
+    for (int j = 0; j < FX_TB; ++j) v[0][j] = j < n ? s_acc[tt[j] * GM_BM + threadIdx.x] : 0.f;
+  } else {
+#pragma unroll
+    for (int s2 = 0; s2 < FX_MAX_SPLITS; ++s2)
+#pragma unroll
+      for (int j = 0; j < FX_TB; ++j)
+        v[s2][j] = (s2 < p.splits && j < n)
+                       ? ld_dsmem_f32(mapa_rank(my_acc + static_cast<uint32_t>(tt[j]) * GM_BM * 4u, s2))
+                       : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < FX_TB; ++j) {
+    float a = v[0][j];
+#pragma unroll
+    for (int s2 = 1; s2 < FX_MAX_SPLITS; ++s2)
+      if (s2 < p.splits) a += v[s2][j];
+    y[j] = bf16_round(a + fb);
+  }
+}
+
+// s_y: >= FX_TB x 128 bf16 of free shared memory; s_part: >= 4 x FX_TB floats;
+// s_tok: >= 4 x FX_TB ints.
+STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, const float* s_acc, uint32_t my_acc, float fb,
+                        __nv_bfloat16* s_y, float* s_part, int* s_tok, int t_first, int t_step) {
   const int tid = threadIdx.x;
   const int f = n0 + tid;
+  const int rows = p.fixup == FIX_RESID ? p.M : p.rope_rows;
+  const int mine = t_first < rows ? (rows - t_first + t_step - 1) / t_step : 0;
   if (p.fixup == FIX_RESID) {
-    const int mine = t_first < p.M ? (p.M - t_first + t_step - 1) / t_step : 0;
-    for (int i0 = 0; i0 < mine; i0 += 32) {
-      const int nt = mine - i0 < 32 ? mine - i0 : 32;
-      for (int j = 0; j < nt; ++j) {
-        const int t = t_first + (i0 + j) * t_step;
+    for (int i0 = 0; i0 < mine; i0 += FX_TB) {
+      const int nt = mine - i0 < FX_TB ? mine - i0 : FX_TB;
+      int tt[FX_TB];
+      float xo[FX_TB], y[FX_TB];
+#pragma unroll
+      for (int j = 0; j < FX_TB; ++j) {
+        tt[j] = t_first + (i0 + (j < nt ? j : 0)) * t_step;
+        xo[j] = (j < nt && f < p.N) ? __bfloat162float(p.resid[static_cast<size_t>(tt[j]) * p.N + f]) : 0.f;
+      }
+      fixup_sums(p, s_acc, my_acc, fb, tt, nt, y);
+#pragma unroll
+      for (int j = 0; j < FX_TB; ++j) {
+        if (j >= nt) break;
         float xn = 0.f;
         if (f < p.N) {
-          __nv_bfloat16* xp = p.resid + static_cast<size_t>(t) * p.N + f;
-          xn = bf16_round(__fadd_rn(__bfloat162float(*xp), yv(t)));
-          *xp = __float2bfloat16_rn(xn);
+          xn = bf16_round(__fadd_rn(xo[j], y[j]));
+          p.resid[static_cast<size_t>(tt[j]) * p.N + f] = __float2bfloat16_rn(xn);
         }
         tile_sum128(__fmul_rn(xn, xn), s_part, j);
       }
       __syncthreads();
-      if (tid < nt)
-        p.sumsq_out[static_cast<size_t>(tile) * p.M + t_first + (i0 + tid) * t_step] = tile_sum128_finish(s_part, tid);
+      if (tid < nt) p.sumsq_out[static_cast<size_t>(tile) * p.M + t_first + (i0 + tid) * t_step] =
+          tile_sum128_finish(s_part, tid);
       __syncthreads();
     }
     return;
@@ -178,42 +225,63 @@ STD_DEV void gemm_fixup(const GemmParams& p, int tile, int n0, YV yv, __nv_bfloa
   const int heads = r.Hq + 2 * r.Hkv;
   if (tile >= heads) return;
   const int d = tid, half = 64, c = d & 63;
-  const int mine = t_first < p.rope_rows ? (p.rope_rows - t_first + t_step - 1) / t_step : 0;
-  for (int i0 = 0; i0 < mine; i0 += 32) {
-    const int nt = mine - i0 < 32 ? mine - i0 : 32;
-    for (int j = 0; j < nt; ++j) s_y[j * 128 + d] = __float2bfloat16_rn(yv(t_first + (i0 + j) * t_step));
-    __syncthreads();
-    for (int j = 0; j < nt; ++j) {
-      const int row = t_first + (i0 + j) * t_step;
+  const bool is_q = tile < r.Hq, is_v = tile >= r.Hq + r.Hkv;
+  int* s_pos = s_tok;
+  int* s_slot = s_tok + FX_TB;
+  int* s_b = s_tok + 2 * FX_TB;
+  for (int i0 = 0; i0 < mine; i0 += FX_TB) {
+    const int nt = mine - i0 < FX_TB ? mine - i0 : FX_TB;
+    int tt[FX_TB];
+    float y[FX_TB];
+#pragma unroll
+    for (int j = 0; j < FX_TB; ++j) tt[j] = t_first + (i0 + (j < nt ? j : 0)) * t_step;
+    fixup_sums(p, s_acc, my_acc, fb, tt, nt, y);
+#pragma unroll
+    for (int j = 0; j < FX_TB; ++j)
+      if (j < nt) s_y[j * 128 + d] = __float2bfloat16_rn(y[j]);
+    if (d < nt) {  // the batch's positions and cache slots
+      const int row = t_first + (i0 + d) * t_step;
       const int b = row / r.n, jj = row % r.n;
       int pos = r.pos_base[b] + r.pos_off + jj;
       const int slot = r.slot_base[b] + r.slot_off + jj;
-      const bool slot_ok = slot >= 0 && slot < r.cap;
       if (pos < 0 || pos >= r.max_pos) {
-        if (d == 0) std_set_error(STD_DEVERR_BOUNDS);
+        std_set_error(STD_DEVERR_BOUNDS);
         pos = pos < 0 ? 0 : r.max_pos - 1;
       }
-      if (!slot_ok && d == 0 && tile >= r.Hq) std_set_error(STD_DEVERR_LENGTH);
+      const bool slot_ok = slot >= 0 && slot < r.cap;
+      if (!slot_ok && !is_q) std_set_error(STD_DEVERR_LENGTH);
+      s_pos[d] = pos;
+      s_slot[d] = slot_ok ? slot : -1;
+      s_b[d] = b;
+    }
+    __syncthreads();
+    float cs[FX_TB], sn[FX_TB];
+#pragma unroll
+    for (int j = 0; j < FX_TB; ++j) {
+      cs[j] = (j < nt && !is_v) ? __bfloat162float(r.cos_t[static_cast<size_t>(s_pos[j]) * half + c]) : 0.f;
+      sn[j] = (j < nt && !is_v) ? __bfloat162float(r.sin_t[static_cast<size_t>(s_pos[j]) * half + c]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < FX_TB; ++j) {
+      if (j >= nt) break;
       const float lo = __bfloat162float(s_y[j * 128 + c]);
       const float hi = __bfloat162float(s_y[j * 128 + half + c]);
       __nv_bfloat16* dst;
-      if (tile < r.Hq) {
-        dst = r.q_out + (static_cast<size_t>(row) * r.Hq + tile) * 128;
+      if (is_q) {
+        dst = r.q_out + (static_cast<size_t>(tt[j]) * r.Hq + tile) * 128;
       } else {
-        if (!slot_ok) continue;
-        const int hk = tile < r.Hq + r.Hkv ? tile - r.Hq : tile - r.Hq - r.Hkv;
-        dst = (tile < r.Hq + r.Hkv ? r.k_cache : r.v_cache) +
-              ((static_cast<size_t>(b) * r.Hkv + hk) * r.cap + slot) * 128;
+        if (s_slot[j] < 0) continue;
+        const int hk = is_v ? tile - r.Hq - r.Hkv : tile - r.Hq;
+        dst = (is_v ? r.v_cache : r.k_cache) +
+              ((static_cast<size_t>(s_b[j]) * r.Hkv + hk) * r.cap + s_slot[j]) * 128;
       }
       float out;
-      if (tile >= r.Hq + r.Hkv) {
+      if (is_v) {
         out = d < half ? lo : hi;  // v: no rotation
       } else {
-        const float cs = __bfloat162float(r.cos_t[static_cast<size_t>(pos) * half + c]);
-        const float sn = __bfloat162float(r.sin_t[static_cast<size_t>(pos) * half + c]);
         // q*cos + rotate_half(q)*sin, each product and the sum rounded to bf16
-        out = d < half ? bf16_round(__fadd_rn(bf16_round(__fmul_rn(lo, cs)), bf16_round(__fmul_rn(-hi, sn))))
-                       : bf16_round(__fadd_rn(bf16_round(__fmul_rn(hi, cs)), bf16_round(__fmul_rn(lo, sn))));
+        out = d < half ? bf16_round(__fadd_rn(bf16_round(__fmul_rn(lo, cs[j])), bf16_round(__fmul_rn(-hi, sn[j]))))
+                       : bf16_round(__fadd_rn(bf16_round(__fmul_rn(hi, cs[j])), bf16_round(__fmul_rn(lo, sn[j]))));
       }
       dst[d] = __float2bfloat16_rn(out);
     }
@@ -248,6 +316,7 @@ __global__ void __launch_bounds__(GM_THREADS)
   __shared__ uint32_t s_tmem;
   __shared__ float s_inv[256];
   __shared__ float s_part[4 * 32];
+  __shared__ int s_tok[4 * FX_TB];
   __shared__ int s_norm_ok[2][2];
 
   uint32_t ncols = 32;
@@ -492,14 +561,8 @@ __global__ void __launch_bounds__(GM_THREADS)
     }
     const float fb = (p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
     const uint32_t my_acc = smem_u32(s_acc) + static_cast<uint32_t>(tid) * 4u;
-    gemm_fixup(p, tile, n0,
-               [&](int t) {
-                 const uint32_t off = static_cast<uint32_t>(t) * GM_BM * 4u;
-                 float a = p.splits > 1 ? ld_dsmem_f32(mapa_rank(my_acc + off, 0)) : s_acc[t * GM_BM + tid];
-                 for (int s2 = 1; s2 < p.splits; ++s2) a += ld_dsmem_f32(mapa_rank(my_acc + off, s2));
-                 return bf16_round(a + fb);
-               },
-               reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(p.M) * GM_BM * 4), s_part, split,
+    gemm_fixup(p, tile, n0, s_acc, my_acc, fb,
+               reinterpret_cast<__nv_bfloat16*>(smem + static_cast<size_t>(p.M) * GM_BM * 4), s_part, s_tok, split,
                p.splits);
     if (p.splits > 1) {  // no CTA leaves while another may still read its stage
       cluster_arrive_release();

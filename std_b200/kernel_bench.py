@@ -39,6 +39,7 @@ def main() -> None:
     ap.add_argument("--kernel", choices=["verify", "draft", "gemm", "forward"], default="verify")
     ap.add_argument("--gamma", type=int, default=9)
     ap.add_argument("--sparse-len", type=int, default=1025)
+    ap.add_argument("--only", choices=["sparse", "dense"], default=None, help="forward: time one of the two")
     ap.add_argument("--M", type=int, default=8)
     ap.add_argument("--N", type=int, default=4608)
     ap.add_argument("--K", type=int, default=3584)
@@ -163,7 +164,8 @@ def forward_bench(a, dev) -> None:
 
     res = {}
     for name, fn in (("sparse_forward", sparse_fwd), ("dense_forward", dense_fwd)):
-        res[name + "_us"] = graph_time_us([fn], rounds=4)
+        if a.only is None or name.startswith(a.only):
+            res[name + "_us"] = graph_time_us([fn], rounds=4)
     wbytes = 2 * model.num_params() - 2 * c.vocab_size * c.hidden_size  # the embedding table is not streamed
     res.update(B=B, L=L, sparse_len=a.sparse_len, gamma=gamma, weight_bytes=wbytes,
                weight_stream_us=wbytes / 6548.5e3)
