@@ -214,9 +214,8 @@ def gemm_roofline(runner, model, M: int, hbm_peak: float):
     dev = model.device
     Hq, Hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
     bf = torch.bfloat16
-    x = torch.randn(M, c.hidden_size, device=dev).to(bf)
-    xf = x.float()
-    sumsq = (xf * xf).view(M, -1, 128).sum(-1).t().contiguous()  # [hidden/128, M]
+    h = (torch.randn(M, c.hidden_size, device=dev) * 0.5).to(bf)
+    x = torch.zeros(M, c.hidden_size, device=dev, dtype=bf)
     attn = (torch.randn(M, c.hidden_size, device=dev) * 0.5).to(bf)
     act = (torch.randn(M, c.intermediate_size, device=dev) * 0.5).to(bf)
     q = torch.empty(M, Hq, D, device=dev, dtype=bf)
@@ -226,15 +225,15 @@ def gemm_roofline(runner, model, M: int, hbm_peak: float):
     tok = torch.zeros(M, dtype=torch.int32, device=dev)
     cos_t, sin_t = model.cos_t, model.sin_t
     eps = c.rms_norm_eps
-    # the decode forward's own launches (decode_forward): norm prologues and
-    # split-K fixup epilogues inside the GEMMs
+    # the decode forward's own launches (decode_forward): each GEMM with the
+    # fused epilogue kernel that follows it
     calls = {
-        "qkv": lambda lw: ops.gemm_norm_rope_append(x, sumsq, lw.w_in, eps, lw.w_qkv, lw.b_qkv, M, 1, Hq, Hkv, D, zero,
-                                                    0, zero, 0, cos_t, sin_t, q, kc, vc),
-        "o": lambda lw: ops.gemm_residual(attn, lw.w_o, x, sumsq),
-        "gate_up": lambda lw: ops.gemm_norm_silu_mul(x, sumsq, lw.w_post, eps, lw.w_gu, act),
-        "down": lambda lw: ops.gemm_residual(act, lw.w_down, x, sumsq),
-        "lm_head": lambda lw: ops.gemm_norm_argmax(x, sumsq, model.norm, eps, model.lm_head, tok),
+        "qkv": lambda lw: ops.gemm_rope_append(h, lw.w_qkv, lw.b_qkv, M, 1, Hq, Hkv, D, zero, 0, zero, 0, cos_t, sin_t,
+                                               q, kc, vc),
+        "o": lambda lw: ops.gemm_add_rmsnorm(attn, lw.w_o, x, lw.w_post, eps, h),
+        "gate_up": lambda lw: ops.gemm_silu_mul(h, lw.w_gu, act),
+        "down": lambda lw: ops.gemm_add_rmsnorm(act, lw.w_down, x, lw.w_in, eps, h),
+        "lm_head": lambda lw: ops.gemm_argmax(h, model.lm_head, tok),
     }
     shapes, tot_b, tot_s, tot_n = {}, 0.0, 0.0, 0
     for name, N, K, per_fwd in gemm_shapes(c):
@@ -242,8 +241,15 @@ def gemm_roofline(runner, model, M: int, hbm_peak: float):
         us = graph_time_us([lambda lw=lw: fn(lw) for lw in model.layers], rounds=2)
         nbytes = 2 * N * K + 2 * M * K + 2 * M * (N if name != "gate_up" else N // 2)
         gbs = nbytes / (us * 1e-6) / 1e9
+        import ctypes
+
+        from std_b200 import _lib
+
+        sp, ac = ctypes.c_int(0), ctypes.c_int(0)
+        _lib.call("std_gemm_plan", N, K, 0, ctypes.byref(sp), ctypes.byref(ac))
         shapes[name] = {"N": N, "K": K, "launch_us": us, "algorithmic_bytes": nbytes, "achieved": gbs,
-                        "frac": gbs / hbm_peak, "per_forward": per_fwd}
+                        "frac": gbs / hbm_peak, "per_forward": per_fwd, "splits": sp.value,
+                        "active_clusters": ac.value}
         tot_b += nbytes * per_fwd
         tot_s += us * 1e-6 * per_fwd
         tot_n += per_fwd

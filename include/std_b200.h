@@ -212,10 +212,12 @@ int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int K, void* a
  * x [M, K] . w [N, K]^T, out[(t/n)*out_stride + out_start + t%n] = first
  * column of the maximum bf16 logit, without storing the logits.  keys: M
  * uint64 scratch, all zero on entry (zero it once before the first call); the
- * call leaves it zero.  Same result as std_gemm_bf16 + std_argmax_rows. */
+ * call leaves it zero.  Same result as std_gemm_bf16 + std_argmax_rows.
+ * margin_out (optional, fp32, indexed like out): the row's largest minus
+ * second-largest logit (verification_policy.py:29-46; equal maxima give 0). */
 int std_gemm_argmax(const void* x, const void* w, int M, int N, int K, int rows_out, int n, int out_stride,
-                    int out_start, int32_t* out, unsigned long long* keys, void* workspace, size_t workspace_bytes,
-                    void* stream);
+                    int out_start, int32_t* out, float* margin_out, unsigned long long* keys, void* workspace,
+                    size_t workspace_bytes, void* stream);
 /* Replaces: q/k/v_proj of a decode step (modeling_qwen2_5_vl.py:1050-1052),
  * RoPE (:690-732) and KVCache.cat (kv_cache.py:54-69): qkv = x . w^T + bias
  * (w [(Hq+2Hkv)*D, K]) then, per token row, the std_rope_append step on it.
@@ -244,6 +246,11 @@ size_t std_gemm_fused_workspace_bytes(int M, int N, int K);
  * smaller ring leaves room for the next kernel's CTAs on the same SM.
  * Applies to launches issued after the call, process-wide. */
 int std_gemm_set_smem_budget(int bytes);
+/* Launch plan (no reference counterpart): the K split count of a GEMM on an
+ * [N, K] weight (fused = 1: the decode-layer ops, whose splits form one
+ * cluster per 128-feature tile) and how many such clusters the device runs at
+ * once (0 when K is not split). */
+int std_gemm_plan(int N, int K, int fused, int* splits_out, int* active_clusters_out);
 /* Replaces: nn.Embedding (modeling_qwen2_5_vl.py:1336) of a decode step:
  * out[b*n + j] = table[tok[b*tok_stride + tok_start + j]] (rows [B*n, H]) and
  * sumsq [H/128, ld] of those rows (ld >= B*n, the row count of the GEMMs

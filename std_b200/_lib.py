@@ -46,11 +46,12 @@ SIGNATURES: Dict[str, tuple] = {
     "std_gemm_epilogue_workspace_bytes": (SZ, [I, I, I]),
     "std_gemm_add_rmsnorm": (I, [P, P, P, P, P, F, P, I, I, I, P, SZ, P]),
     "std_gemm_silu_mul": (I, [P, P, I, I, I, P, P, SZ, P]),
-    "std_gemm_argmax": (I, [P, P, I, I, I, I, I, I, I, PI32, P, P, SZ, P]),
+    "std_gemm_argmax": (I, [P, P, I, I, I, I, I, I, I, PI32, PF, P, P, SZ, P]),
     "std_gemm_rope_append": (I, [P, P, P, I, I, I, I, I, I, P, I, P, I, P, P, I, P, P, P, I, P, SZ, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
     "std_gemm_fused_workspace_bytes": (SZ, [I, I, I]),
     "std_gemm_set_smem_budget": (I, [I]),
+    "std_gemm_plan": (I, [I, I, I, P, P]),
     "std_embed_sumsq": (I, [P, I, I, PI32, I, I, I, I, P, PF, I, P]),
     "std_gemm_norm_rope_append": (I, [P, PF, P, F, P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I,
                                       P]),

@@ -945,7 +945,10 @@ extern "C" size_t std_gemm_epilogue_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const size_t part = std_gemm_workspace_bytes(M, N, K);
   const size_t ybytes = static_cast<size_t>(M) * N * 2;
-  const size_t b = part > ybytes ? part : ybytes;
+  // the argmax's margins: per-warp top-2 pairs [N/128 * 4, M] of float2
+  const size_t top2 = static_cast<size_t>((N + stdb::GM_BM - 1) / stdb::GM_BM) * 4 * M * 8;
+  size_t b = part > ybytes ? part : ybytes;
+  b = b > top2 ? b : top2;
   return ((b + 255) / 256) * 256;
 }
 
@@ -1017,15 +1020,26 @@ extern "C" int std_gemm_rope_append(const void* x, const void* w, const void* bi
 // lm_head + greedy argmax: the argmax of each of the first `rows_out` rows of
 // x . w^T (bf16 logits, first index on ties) without storing the logits.
 extern "C" int std_gemm_argmax(const void* x, const void* w, int M, int N, int K, int rows_out, int n, int out_stride,
-                               int out_start, int32_t* out, unsigned long long* keys, void* workspace,
-                               size_t workspace_bytes, void* stream) {
+                               int out_start, int32_t* out, float* margin_out, unsigned long long* keys,
+                               void* workspace, size_t workspace_bytes, void* stream) {
   if (!gemm_shape_ok(x, w, M, N, K, 8) || out == nullptr || keys == nullptr) return 1;
   if (rows_out <= 0 || rows_out > M || n <= 0) return 1;
   const int splits = gemm_splits(N, K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (splits == 1) {
-    int rc = gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, keys, rows_out);
+    GemmExtra e;
+    if (margin_out != nullptr) {  // per-warp top-2 pairs in the workspace
+      if (workspace == nullptr || workspace_bytes < std_gemm_epilogue_workspace_bytes(M, N, K)) return 5;
+      e.amax_top2 = workspace;
+    }
+    int rc = gemm_launch(x, w, nullptr, nullptr, nullptr, M, N, K, 1, s, keys, rows_out, nullptr, &e);
     if (rc != 0) return rc;
+    if (margin_out != nullptr)
+      return launch_pdl(stdb::argmax_margin_kernel, dim3(rows_out), dim3(256), 0, s, keys,
+                        static_cast<const float2*>(workspace), ((N + stdb::GM_BM - 1) / stdb::GM_BM) * 4, M, n,
+                        out_stride, out_start, out, margin_out) == cudaSuccess
+                 ? 0
+                 : 4;
     return launch_pdl(stdb::argmax_keys_kernel, dim3((rows_out + 127) / 128), dim3(128), 0, s, keys, rows_out, n,
                       out_stride, out_start, out) == cudaSuccess
                ? 0
@@ -1036,7 +1050,7 @@ extern "C" int std_gemm_argmax(const void* x, const void* w, int M, int N, int K
   if (rc != 0) return rc;
   return launch_pdl(stdb::argmax_kernel<stdb::GemmOut>, dim3(rows_out), dim3(1024), 0, s,
                     gemm_out_view(workspace, nullptr, splits, M, N), N, n, out_stride, out_start, out,
-                    static_cast<float*>(nullptr)) == cudaSuccess
+                    margin_out) == cudaSuccess
              ? 0
              : 4;
 }
@@ -1070,6 +1084,17 @@ extern "C" int std_gemm_silu_mul(const void* x, const void* w, int M, int I, int
 // Only the norm + SiLU / argmax ops take a workspace (split partials for
 // their separate reduction kernel, used when K is split).
 // ---------------------------------------------------------------------------
+// The launch plan of a GEMM: split count (cluster size for the fused
+// epilogues) and, for the plain one, of the unfused ops.
+extern "C" int std_gemm_plan(int N, int K, int fused, int* splits_out, int* active_clusters_out) {
+  if (N <= 0 || K <= 0 || K % stdb::GM_BK != 0 || splits_out == nullptr) return 1;
+  const int s = fused ? gemm_splits_cluster(N, K) : gemm_splits(N, K);
+  *splits_out = s;
+  if (active_clusters_out != nullptr)
+    *active_clusters_out = s > 1 ? gemm_active_clusters(s, static_cast<size_t>(stdb::GM_SMEM_BUDGET) + 1024) : 0;
+  return 0;
+}
+
 extern "C" size_t std_gemm_fused_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   // split partials for the norm + SiLU / argmax ops, or the argmax margins' per-warp top-2 pairs

@@ -8,11 +8,11 @@ Positions are 1-D (the fork disables get_rope_index, :2074-2105), so M-RoPE
 reduces to ordinary RoPE with theta = 1e6.
 
 Compute split:
-  * decode forwards: every kernel is from libstd_b200.so -- five launches
-    per layer: the tcgen05 weight-streaming GEMMs with the RMSNorm in their
-    prologue and the split-K reduction plus RoPE + KV append, residual add or
-    SiLU*up in their epilogue, and draft / verify attention; the final norm,
-    lm_head and greedy argmax are one more GEMM launch;
+  * decode forwards: every kernel is from libstd_b200.so -- the tcgen05
+    weight-streaming GEMM for projections, MLP and lm_head, RMSNorm (fused
+    with the residual add and the split-K sum), RoPE + KV append (fused with
+    the split-K sum), draft / verify attention, SiLU*up, lm_head fused with
+    the greedy argmax;
   * prefill (thousands of rows): cuBLAS GEMMs through torch and torch SDPA
     attention (library flash/efficient kernels), as the reference does.
 Dense decode forwards (AR steps and verify) always run their GEMMs on the same
@@ -104,6 +104,52 @@ class Qwen25VLDecoder:
         self._rope_len = 0
         self.cos_t = self.sin_t = None
 
+    # ------------------------------------------------------------------ checkpoints
+    @classmethod
+    def from_state_dict(cls, config: DecoderConfig, state: dict, device: str = "cuda",
+                        dtype: torch.dtype = torch.bfloat16) -> "Qwen25VLDecoder":
+        """Build the decoder from a Qwen2.5-VL language-model state dict with
+        the reference's parameter names (modeling_qwen2_5_vl.py: embed_tokens,
+        layers.{i}.self_attn.{q,k,v,o}_proj, layers.{i}.mlp.{gate,up,down}_proj,
+        layers.{i}.{input,post_attention}_layernorm, norm; lm_head), an
+        optional "model." prefix allowed.  q/k/v are fused into one matrix
+        (+ bias) and gate/up interleaved in 64-row [gate | up] blocks."""
+        self = cls.__new__(cls)
+        if config.num_attention_heads != 7 * config.num_key_value_heads or config.head_dim != 128:
+            raise ValueError("the STD kernels are built for 7 query heads per KV head and head_dim 128")
+        self.config, self.device, self.dtype = config, torch.device(device), dtype
+
+        def get(name):
+            for key in (name, "model." + name, "model.language_model." + name):
+                if key in state:
+                    return state[key].to(device=self.device, dtype=dtype).contiguous()
+            raise KeyError(name)
+
+        c = config
+        I = c.intermediate_size
+        self.embed = get("embed_tokens.weight")
+        self.layers = []
+        for i in range(c.num_hidden_layers):
+            pre = f"layers.{i}."
+            lw = LayerWeights()
+            lw.w_in = get(pre + "input_layernorm.weight")
+            lw.w_post = get(pre + "post_attention_layernorm.weight")
+            att = pre + "self_attn."
+            lw.w_qkv = torch.cat([get(att + "q_proj.weight"), get(att + "k_proj.weight"),
+                                  get(att + "v_proj.weight")]).contiguous()
+            lw.b_qkv = torch.cat([get(att + "q_proj.bias"), get(att + "k_proj.bias"), get(att + "v_proj.bias")])
+            lw.w_o = get(att + "o_proj.weight")
+            gate, up = get(pre + "mlp.gate_proj.weight"), get(pre + "mlp.up_proj.weight")
+            lw.w_gu = torch.stack([gate.view(I // 64, 64, -1), up.view(I // 64, 64, -1)], 1).reshape(2 * I, -1)
+            lw.w_gu = lw.w_gu.contiguous()
+            lw.w_down = get(pre + "mlp.down_proj.weight")
+            self.layers.append(lw)
+        self.norm = get("norm.weight")
+        self.lm_head = get("lm_head.weight") if any(k.endswith("lm_head.weight") for k in state) else self.embed
+        self._rope_len = 0
+        self.cos_t = self.sin_t = None
+        return self
+
     # ------------------------------------------------------------------ rope
     def rope_tables(self, max_pos: int):
         """cos/sin [max_pos, D/2] bf16: inv_freq = theta^(-2i/D) (fp32), angle =
@@ -177,20 +223,26 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
     Hq, Hkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
     eps = c.rms_norm_eps
     cos_t, sin_t = model.cos_t, model.sin_t
-    x = ws.x[:rows]
-    sumsq = ws.sumsq(rows)
+    x, h = ws.x[:rows], ws.h[:rows]
     if dense_attn is not None and not sparse:
         dense_attn.begin(n)
-    # Five launches per layer: [RMSNorm + QKV + RoPE + KV append] -> attention
-    # -> [O proj + residual] -> [RMSNorm + gate/up + SiLU*up] -> [down proj +
-    # residual].  The norms run on the GEMMs' staged x tiles from the
-    # per-tile sums of squares the previous GEMM (or the embedding) left in
-    # `sumsq`; the residual adds run in the last CTA of each output tile.
-    ops.embed_sumsq(model.embed, tok, tok_start, n, ws.x[:M], sumsq)
+    # Eight launches per layer: QKV GEMM -> [split-K sum + bias + RoPE + KV
+    # append] -> attention -> O GEMM -> [split-K sum + residual + RMSNorm] ->
+    # gate/up GEMM with SiLU*up in its epilogue -> down GEMM -> [split-K sum +
+    # residual + the next RMSNorm]; the bracketed steps are one small kernel
+    # each, reading the GEMM's split partials from L2.
+    ops.embed(model.embed, tok, tok_start, n, ws.x[:M])
+    ops.rmsnorm(x, model.layers[0].w_in, eps, h)
+    n_layers = len(model.layers)
     for li, lw in enumerate(model.layers):
         kc, vc = cache[li, 0], cache[li, 1]
-        ops.gemm_norm_rope_append(x, sumsq, lw.w_in, eps, lw.w_qkv, lw.b_qkv, B, n, Hq, Hkv, D, pos_base, pos_off,
-                                  slot_base, slot_off, cos_t, sin_t, ws.q[:M], kc, vc)
+        if rows == M:
+            ops.gemm_rope_append(h, lw.w_qkv, lw.b_qkv, B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off,
+                                 cos_t, sin_t, ws.q[:M], kc, vc)
+        else:  # padded rows: the GEMM runs on `rows`, RoPE on the M real ones
+            ops.gemm(h, lw.w_qkv, ws.qkv[:rows], lw.b_qkv)
+            ops.rope_append(ws.qkv[:M], B, n, Hq, Hkv, D, pos_base, pos_off, slot_base, slot_off, cos_t, sin_t,
+                            ws.q[:M], kc, vc)
         if sparse and sparse_index is not None:
             dense, sel = sparse_index
             ops.draft_attention_indexed(ws.q[:M], dense[li, 0], dense[li, 1], sel[li], kc, vc, lens, len_offset,
@@ -205,13 +257,17 @@ def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *
                                  out=ws.attn[:M].view(B, n, Hq, D))
         if collector is not None and not sparse:
             collector(li, ws.q[:M].view(B, n, Hq, D))
-        ops.gemm_residual(ws.attn[:rows], lw.w_o, x, sumsq)
-        ops.gemm_norm_silu_mul(x, sumsq, lw.w_post, eps, lw.w_gu, ws.act[:rows])
-        ops.gemm_residual(ws.act[:rows], lw.w_down, x, sumsq)
+        ops.gemm_add_rmsnorm(ws.attn[:rows], lw.w_o, x, lw.w_post, eps, h)
+        ops.gemm_silu_mul(h, lw.w_gu, ws.act[:rows])
+        if li + 1 < n_layers:
+            next_norm = model.layers[li + 1].w_in
+        else:  # the final norm feeds lm_head; a draft step without lm_head only adds
+            next_norm = model.norm if argmax_out is not None else None
+        ops.gemm_add_rmsnorm(ws.act[:rows], lw.w_down, x, next_norm, eps, h)
     if argmax_out is None:
         return
-    ops.gemm_norm_argmax(x, sumsq, model.norm, eps, model.lm_head, argmax_out, rows_out=M, n=n,
-                         out_stride=argmax_stride, out_start=argmax_start, margin_out=margin_out)
+    ops.gemm_argmax(h, model.lm_head, argmax_out, rows_out=M, n=n, out_stride=argmax_stride, out_start=argmax_start,
+                    margin_out=margin_out)
 
 
 # ---------------------------------------------------------------------- prefill

@@ -235,10 +235,11 @@ def gemm_add_rmsnorm(x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor, norm
 
 
 def gemm_argmax(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, rows_out: Optional[int] = None, n: int = 1,
-                out_stride: int = 1, out_start: int = 0):
+                out_stride: int = 1, out_start: int = 0, margin_out: Optional[torch.Tensor] = None):
     """Greedy argmax of x @ w^T's bf16 rows (lm_head + argmax) without storing the logits.
 
-    Result t (< rows_out, default all rows) goes to out[(t//n)*out_stride + out_start + t%n]."""
+    Result t (< rows_out, default all rows) goes to out[(t//n)*out_stride + out_start + t%n];
+    with margin_out (fp32, same indexing) also the row's top-1 minus top-2 logit."""
     M, K = x.shape
     N = w.shape[0]
     _check(x, torch.bfloat16, "x")
@@ -248,8 +249,10 @@ def gemm_argmax(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, rows_out: O
     keys = workspace("argmax_keys", M * 8, x.device)  # zero-initialised, left zero by every call
     nb = _lib.query("std_gemm_epilogue_workspace_bytes", M, N, K)
     ws = workspace("gemm", nb, x.device)
+    if margin_out is not None:
+        _check(margin_out, torch.float32, "margin_out")
     _lib.call("std_gemm_argmax", x.data_ptr(), w.data_ptr(), M, N, K, rows_out, n, out_stride, out_start,
-              out.data_ptr(), keys.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+              out.data_ptr(), _p(margin_out), keys.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
     return out
 
 

@@ -508,3 +508,41 @@ def test_verification_policies_count_and_keep_tokens(full):
                 assert len(st["verify_margins"][b]) == margin_rounds(b)
                 assert all(m >= 0 for m in st["verify_margins"][b])
     assert ops.device_error() == 0
+
+
+def test_acceptance_matches_reference_on_reduced_random_decoder():
+    """On a reduced random-init Qwen2.5-VL decoder (4 layers, the 7B's head
+    geometry and vocabulary) with configs[4]'s selected-to-visual ratio, the
+    reference's own STD decode (recorded on CPU in fp16 by
+    tests/golden/make_acceptance.py) accepts almost nothing: one draft in the
+    first round, none after.  The B200 path on the same weights and inputs
+    (bf16) shows the same acceptance, so the near-zero acceptance of the
+    random-weight benchmarks is a property of random weights, not of this
+    build; STD == AR holds."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__), "golden"))
+    import acceptance_case as case
+
+    from std_b200 import ops
+    from std_b200.model import Qwen25VLDecoder
+    from std_b200.std_qwen25vl import std_generate_qwen25vl, ar_generate_qwen25vl, tokens_equal
+
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "acceptance_reduced.npz"))
+    model = Qwen25VLDecoder.from_state_dict(case.decoder_config(), case.state_dict())
+    for i in range(len(case.REQUEST_SEEDS)):
+        ids, vis = case.request(i)
+        inp = {"input_ids": ids, "visual_embeds": vis.to(torch.bfloat16)}
+        std, sel = std_generate_qwen25vl(model, inp, video_token_id=case.VIDEO_TOKEN_ID, eos_token_id=-1,
+                                         max_new_tokens=case.MAX_NEW, gamma=case.GAMMA,
+                                         target_k_plus_text=case.K_PLUS_TEXT, ignore_eos=True)
+        ar = ar_generate_qwen25vl(model, inp, video_token_id=case.VIDEO_TOKEN_ID, eos_token_id=-1,
+                                  max_new_tokens=case.MAX_NEW, ignore_eos=True)
+        assert sel.k == int(g["k"]) == 112
+        assert tokens_equal(std.output_ids, ar.output_ids)
+        ref_acc = [a for a in g["accept_lengths"][i].tolist() if a >= 0]
+        ref_rate = sum(ref_acc) / (case.GAMMA * len(ref_acc))
+        assert ref_rate < 0.05  # the reference's own acceptance on random weights
+        assert abs(std.acceptance_rate - ref_rate) < 0.05, (std.accept_lengths, ref_acc)
+    assert ops.device_error() == 0
