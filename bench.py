@@ -245,11 +245,10 @@ def gemm_roofline(runner, model, M: int, hbm_peak: float):
 
         from std_b200 import _lib
 
-        sp, ac = ctypes.c_int(0), ctypes.c_int(0)
-        _lib.call("std_gemm_plan", N, K, 0, ctypes.byref(sp), ctypes.byref(ac))
+        sp = ctypes.c_int(0)
+        _lib.call("std_gemm_plan", N, K, ctypes.byref(sp))
         shapes[name] = {"N": N, "K": K, "launch_us": us, "algorithmic_bytes": nbytes, "achieved": gbs,
-                        "frac": gbs / hbm_peak, "per_forward": per_fwd, "splits": sp.value,
-                        "active_clusters": ac.value}
+                        "frac": gbs / hbm_peak, "per_forward": per_fwd, "splits": sp.value}
         tot_b += nbytes * per_fwd
         tot_s += us * 1e-6 * per_fwd
         tot_n += per_fwd

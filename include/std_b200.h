@@ -227,67 +227,16 @@ int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, 
                          const void* cos_t, const void* sin_t, int max_pos, void* q_out, void* k_cache,
                          void* v_cache, int cap, void* workspace, size_t workspace_bytes, void* stream);
 
-/* ---- decode-layer GEMMs with their neighbours folded in ----------------
- * One launch per projection.  x is the decoder's residual stream [M, K] bf16;
- * sumsq [K/128, M] fp32 holds, per 128-column tile and row, the sum of squares
- * of x (written by std_embed_sumsq and std_gemm_residual), from which the
- * RMSNorm in front of a projection (Qwen2RMSNorm, modeling_qwen2_5_vl.py:
- * 183-197: bf16(norm_w * bf16(x * rsqrt(mean(x^2) + eps)))) is applied to the
- * staged x tiles inside the GEMM.  When K is split, the CTAs of one
- * 128-feature tile form a thread-block cluster and reduce their partial sums
- * through distributed shared memory, in split order, before applying the op
- * that follows the projection (no global scratch).  The norm + SiLU / argmax
- * ops take a workspace of std_gemm_fused_workspace_bytes (split partials for
- * their reduction kernel when K is split); it must not be shared by launches
- * that run concurrently. */
-size_t std_gemm_fused_workspace_bytes(int M, int N, int K);
+/* ---- GEMM tuning and plan --------------------------------------------- */
+
 /* Tuning (no reference counterpart): the per-CTA shared-memory budget of the
- * GEMMs' stage ring, 40..200 KiB (default 104 KiB, two CTAs per SM).  A
- * smaller ring leaves room for the next kernel's CTAs on the same SM.
+ * GEMMs' stage ring, 40..200 KiB (default 104 KiB, two CTAs per SM).
  * Applies to launches issued after the call, process-wide. */
 int std_gemm_set_smem_budget(int bytes);
-/* Launch plan (no reference counterpart): the K split count of a GEMM on an
- * [N, K] weight (fused = 1: the decode-layer ops, whose splits form one
- * cluster per 128-feature tile) and how many such clusters the device runs at
- * once (0 when K is not split). */
-int std_gemm_plan(int N, int K, int fused, int* splits_out, int* active_clusters_out);
-/* Replaces: nn.Embedding (modeling_qwen2_5_vl.py:1336) of a decode step:
- * out[b*n + j] = table[tok[b*tok_stride + tok_start + j]] (rows [B*n, H]) and
- * sumsq [H/128, ld] of those rows (ld >= B*n, the row count of the GEMMs
- * that read them). */
-int std_embed_sumsq(const void* table, int vocab, int H, const int32_t* tok, int tok_stride, int tok_start, int n,
-                    int B, void* out, float* sumsq, int ld, void* stream);
-/* Replaces: input_layernorm + q/k/v_proj + RoPE + KVCache.cat of a decode
- * step (modeling_qwen2_5_vl.py:1179, :1050-1052, :690-732; kv_cache.py:54-69):
- * qkv = rmsnorm(x) . w^T + bias over M rows (M >= B*n: padded rows are
- * computed and dropped), then for the B*n real rows the std_rope_append step
- * (q -> q_out, k/v -> cache slot slot_base[b] + slot_off + j).  D == 128,
- * M <= 128. */
-int std_gemm_norm_rope_append(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w,
-                              const void* bias, int M, int K, int B, int n, int Hq, int Hkv, int D,
-                              const int32_t* pos_base, int pos_off, const int32_t* slot_base, int slot_off,
-                              const void* cos_t, const void* sin_t, int max_pos, void* q_out, void* k_cache,
-                              void* v_cache, int cap, void* stream);
-/* Replaces: o_proj / down_proj and the residual add after them
- * (modeling_qwen2_5_vl.py:1200-1221): resid <- bf16(resid + bf16(a . w^T +
- * bias)) over [M, N], and sumsq_out [N/128, M] of the new resid.  N % 128 == 0,
- * M <= 128. */
-int std_gemm_residual(const void* a, const void* w, const void* bias, void* resid, float* sumsq_out, int M, int N,
-                      int K, void* stream);
-/* Replaces: post_attention_layernorm + Qwen2MLP's act_fn(gate_proj(h)) *
- * up_proj(h) (modeling_qwen2_5_vl.py:1214, :674-687): act [M, I] from the
- * residual stream x, with w [2I, K] in 64-row [gate | up] blocks. */
-int std_gemm_norm_silu_mul(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w, int M,
-                           int I, int K, void* act, void* workspace, size_t workspace_bytes, void* stream);
-/* Replaces: the final norm + lm_head + greedy argmax (modeling_qwen2_5_vl.py:
- * 1463, :1749; std_qwen25vl.py:98-99, :806): as std_gemm_argmax on
- * rmsnorm(x).  keys: M uint64 scratch, zero on entry and left zero.
- * margin_out (optional, indexed like out): the row's largest minus
- * second-largest bf16 logit (verification_policy.py:29-46). */
-int std_gemm_norm_argmax(const void* x, const float* sumsq, const void* norm_w, float eps, const void* w, int M,
-                         int N, int K, int rows_out, int n, int out_stride, int out_start, int32_t* out,
-                         float* margin_out, unsigned long long* keys, void* workspace, size_t workspace_bytes,
-                         void* stream);
+/* Launch plan (no reference counterpart): how many ranges K is split into
+ * for a GEMM on an [N, K] weight matrix (split partials are summed in split
+ * order by the epilogue kernel). */
+int std_gemm_plan(int N, int K, int* splits_out);
 
 /* ---- (d) fused greedy acceptance + rollback ---------------------------- */
 

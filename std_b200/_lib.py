@@ -49,15 +49,8 @@ SIGNATURES: Dict[str, tuple] = {
     "std_gemm_argmax": (I, [P, P, I, I, I, I, I, I, I, PI32, PF, P, P, SZ, P]),
     "std_gemm_rope_append": (I, [P, P, P, I, I, I, I, I, I, P, I, P, I, P, P, I, P, P, P, I, P, SZ, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
-    "std_gemm_fused_workspace_bytes": (SZ, [I, I, I]),
     "std_gemm_set_smem_budget": (I, [I]),
-    "std_gemm_plan": (I, [I, I, I, P, P]),
-    "std_embed_sumsq": (I, [P, I, I, PI32, I, I, I, I, P, PF, I, P]),
-    "std_gemm_norm_rope_append": (I, [P, PF, P, F, P, P, I, I, I, I, I, I, I, PI32, I, PI32, I, P, P, I, P, P, P, I,
-                                      P]),
-    "std_gemm_residual": (I, [P, P, P, P, PF, I, I, I, P]),
-    "std_gemm_norm_silu_mul": (I, [P, PF, P, F, P, I, I, I, P, P, SZ, P]),
-    "std_gemm_norm_argmax": (I, [P, PF, P, F, P, I, I, I, I, I, I, I, PI32, PF, P, P, SZ, P]),
+    "std_gemm_plan": (I, [I, I, P]),
     "std_verify_policy": (I, [I, I, I, PI32, I, PI32, I, PI32, I, PI32, PI32, PI32, PF, F, I, I, I, PI32, PI32, PI32, PF,
                               I, PI32, ctypes.c_ulonglong, I, P]),
     "std_graph_cond_handle": (I, [P, P]),

@@ -83,12 +83,6 @@ STD_DEV void st_async_v4f32(uint32_t remote, float4 v, uint32_t remote_bar) {
                "r"(__float_as_uint(v.w)), "r"(remote_bar)
                : "memory");
 }
-// 32-bit load from distributed shared memory (an address from mapa_rank).
-STD_DEV float ld_dsmem_f32(uint32_t cluster_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-  return v;
-}
 STD_DEV void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 STD_DEV void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 STD_DEV void cluster_wait_acquire() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
@@ -397,29 +391,6 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
-// The same launch as a grid of thread-block clusters of `cluster` CTAs
-// (cluster.x * cluster.y * cluster.z <= 8).
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, dim3 cluster, size_t smem,
-                                      cudaStream_t stream, Args&&... args) {
-  count_launch();
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = cluster.x;
-  attr[1].val.clusterDim.y = cluster.y;
-  attr[1].val.clusterDim.z = cluster.z;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

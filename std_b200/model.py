@@ -185,14 +185,6 @@ class Workspace:
         self.attn = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
         self.o = torch.zeros(rows, c.hidden_size, device=d, dtype=dt)
         self.act = torch.zeros(rows, c.intermediate_size, device=d, dtype=dt)
-        # per 128-column tile and row, the sum of squares of the residual
-        # stream x (RMSNorm statistics passed from one fused GEMM to the next)
-        self.tiles = c.hidden_size // 128
-        self.sumsq_buf = torch.zeros(self.tiles * rows, device=d, dtype=torch.float32)
-
-    def sumsq(self, rows: int) -> torch.Tensor:
-        """[hidden/128, rows] view: the layout the fused GEMMs of a `rows`-row forward use."""
-        return self.sumsq_buf[: self.tiles * rows].view(self.tiles, rows)
 
 
 def decode_forward(model: Qwen25VLDecoder, ws: Workspace, cache: torch.Tensor, *, B: int, n: int, rows: int,

@@ -317,90 +317,6 @@ def gemm_silu_mul(x: torch.Tensor, w_gu: torch.Tensor, out: torch.Tensor):
     return out
 
 
-# ----------------------------------------------------------------------------
-# decode-layer GEMMs with their neighbours folded in (one launch each)
-# ----------------------------------------------------------------------------
-
-def _fused_ws(M: int, N: int, K: int, device: torch.device) -> torch.Tensor:
-    """Split-K partials of the norm + SiLU / argmax GEMMs (their separate
-    reduction kernel runs only when K is split)."""
-    return workspace("gemm", _lib.query("std_gemm_fused_workspace_bytes", M, N, K), device)
-
-
-def embed_sumsq(table: torch.Tensor, tok: torch.Tensor, tok_start: int, n: int, out: torch.Tensor,
-                sumsq: torch.Tensor):
-    """out[b*n + j] = table[tok[b, tok_start + j]]; sumsq [H/128, ld] per-tile sums of squares (ld = its rows)."""
-    B, stride = tok.shape
-    _check(sumsq, torch.float32, "sumsq")
-    _lib.call("std_embed_sumsq", table.data_ptr(), table.shape[0], table.shape[1], tok.data_ptr(), stride, tok_start, n,
-              B, out.data_ptr(), sumsq.data_ptr(), sumsq.shape[1], _stream())
-    return out
-
-
-def gemm_norm_rope_append(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Tensor, eps: float, w: torch.Tensor,
-                          bias: Optional[torch.Tensor], B: int, n: int, Hq: int, Hkv: int, D: int,
-                          pos_base: torch.Tensor, pos_off: int, slot_base: torch.Tensor, slot_off: int,
-                          cos_t: torch.Tensor, sin_t: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor,
-                          v_cache: torch.Tensor):
-    """rmsnorm(x) -> QKV projection (+bias) -> RoPE + KV append for rows < B*n, one launch."""
-    M, K = x.shape
-    N = w.shape[0]
-    for t, nm in ((x, "x"), (w, "w"), (norm_w, "norm_w")):
-        _check(t, torch.bfloat16, nm)
-    _lib.call("std_gemm_norm_rope_append", x.data_ptr(), sumsq.data_ptr(), norm_w.data_ptr(), float(eps), w.data_ptr(),
-              _p(bias), M, K, B, n, Hq, Hkv, D, pos_base.data_ptr(), int(pos_off), slot_base.data_ptr(), int(slot_off),
-              cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape[0], q_out.data_ptr(), k_cache.data_ptr(),
-              v_cache.data_ptr(), k_cache.shape[-2], _stream())
-    return q_out
-
-
-def gemm_residual(a: torch.Tensor, w: torch.Tensor, resid: torch.Tensor, sumsq_out: torch.Tensor,
-                  bias: Optional[torch.Tensor] = None):
-    """resid <- bf16(resid + bf16(a @ w^T + bias)); sumsq_out [N/128, M] of the new resid; one launch."""
-    M, K = a.shape
-    N = w.shape[0]
-    for t, nm in ((a, "a"), (w, "w"), (resid, "resid")):
-        _check(t, torch.bfloat16, nm)
-    _check(sumsq_out, torch.float32, "sumsq_out")
-    _lib.call("std_gemm_residual", a.data_ptr(), w.data_ptr(), _p(bias), resid.data_ptr(), sumsq_out.data_ptr(), M, N, K,
-              _stream())
-    return resid
-
-
-def gemm_norm_silu_mul(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Tensor, eps: float, w_gu: torch.Tensor,
-                       out: torch.Tensor):
-    """act = silu(rmsnorm(x) @ gate^T) * (rmsnorm(x) @ up^T), w_gu in 64-row [gate | up] blocks."""
-    M, K = x.shape
-    N = w_gu.shape[0]
-    for t, nm in ((x, "x"), (w_gu, "w_gu"), (out, "out"), (norm_w, "norm_w")):
-        _check(t, torch.bfloat16, nm)
-    ws = _fused_ws(M, N, K, x.device)
-    _lib.call("std_gemm_norm_silu_mul", x.data_ptr(), sumsq.data_ptr(), norm_w.data_ptr(), float(eps), w_gu.data_ptr(),
-              M, N // 2, K, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
-    return out
-
-
-def gemm_norm_argmax(x: torch.Tensor, sumsq: torch.Tensor, norm_w: torch.Tensor, eps: float, w: torch.Tensor,
-                     out: torch.Tensor, rows_out: Optional[int] = None, n: int = 1, out_stride: int = 1,
-                     out_start: int = 0, margin_out: Optional[torch.Tensor] = None):
-    """Greedy argmax of rmsnorm(x) @ w^T's bf16 rows without storing the logits
-    (with margin_out, fp32 indexed like out: top-1 minus top-2 logit)."""
-    M, K = x.shape
-    N = w.shape[0]
-    for t, nm in ((x, "x"), (w, "w"), (norm_w, "norm_w")):
-        _check(t, torch.bfloat16, nm)
-    _check(out, torch.int32, "out")
-    rows_out = M if rows_out is None else rows_out
-    keys = workspace("argmax_keys", M * 8, x.device)  # zero-initialised, left zero by every call
-    ws = _fused_ws(M, N, K, x.device)
-    if margin_out is not None:
-        _check(margin_out, torch.float32, "margin_out")
-    _lib.call("std_gemm_norm_argmax", x.data_ptr(), sumsq.data_ptr(), norm_w.data_ptr(), float(eps), w.data_ptr(), M, N,
-              K, rows_out, n, out_stride, out_start, out.data_ptr(), _p(margin_out), keys.data_ptr(), ws.data_ptr(),
-              ws.numel(), _stream())
-    return out
-
-
 def add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor):
     _lib.call("std_add", a.data_ptr(), b.data_ptr(), a.numel(), out.data_ptr(), _stream())
     return out
