@@ -227,6 +227,20 @@ int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, 
                          const void* cos_t, const void* sin_t, int max_pos, void* q_out, void* k_cache,
                          void* v_cache, int cap, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- (f) verification-guided re-selection: the collector ------------- */
+
+/* Replaces: RuntimeVerificationCollector._hook (dynamic_selection.py:290-308).
+ * For the nq verify rows of one layer's dense forward: q_kv[t] = fp32 mean of
+ * the G = Hq/Hkv query heads of each KV group (q [B, nq, Hq, D] bf16, after
+ * RoPE), l[t, v] = q_kv[t] . k[visual_pos[v]] / sqrt(D) over the layer's K
+ * cache k_cache [B, Hkv, cap, D], and rel_out[b][h][visual_pos[v]] =
+ * sum_t softmax over v of l[t, :] (fp32; rel_out rows of rel_stride floats,
+ * positions outside visual_pos untouched).  D = 128, nq <= 32. */
+size_t std_collect_workspace_bytes(int B, int Hkv, int nq, int V);
+int std_collect_relevance(const void* q, const void* k_cache, const int32_t* visual_pos, int V, int B, int nq, int Hq,
+                          int Hkv, int D, int cap, float* rel_out, long long rel_stride, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* ---- GEMM tuning and plan --------------------------------------------- */
 
 /* Tuning (no reference counterpart): the per-CTA shared-memory budget of the

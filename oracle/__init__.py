@@ -15,6 +15,7 @@ What is restated here (reference file:line in brackets):
 * parallel-verify attention (causal)    [modeling_qwen2_5_vl.py:65-101,
                                           :1096-1133]
 * greedy acceptance / commit / rollback [std_qwen25vl.py:806-815, :910-931]
+* verification collector v1             [dynamic_selection.py:290-308]
 
 Parity status: the selection restatement is pinned against the reference's
 own functions run on CPU (tests/golden/make_golden.py); attention against the
@@ -235,6 +236,24 @@ def verify_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, lens_after: Se
                 o[b, t, h] = e @ vv / e.sum()
                 lse[b, t, h] = mx + math.log(e.sum())
     return o, lse
+
+
+def collect_relevance(q: np.ndarray, k: np.ndarray, visual_pos: np.ndarray) -> np.ndarray:
+    """RuntimeVerificationCollector._hook (dynamic_selection.py:290-308) in
+    fp64: q [B, Hq, nq, D], k [B, Hkv, P, D] (any float dtype) ->
+    [B, Hkv, V] = sum over the nq rows of softmax over the visual keys of
+    (mean of the group's query heads . k) / sqrt(D)."""
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    B, Hq, nq, D = q.shape
+    Hkv = k.shape[1]
+    qk = q.reshape(B, Hkv, Hq // Hkv, nq, D).mean(axis=2)              # [B, Hkv, nq, D]
+    kv = k[:, :, np.asarray(visual_pos, dtype=np.int64)]              # [B, Hkv, V, D]
+    logits = np.einsum("bhtd,bhvd->bhtv", qk, kv) / math.sqrt(D)
+    logits -= logits.max(axis=-1, keepdims=True)
+    w = np.exp(logits)
+    w /= w.sum(axis=-1, keepdims=True)
+    return w.sum(axis=2)
 
 
 def merge_partials(o_parts: Sequence[np.ndarray], lse_parts: Sequence[np.ndarray]):

@@ -50,6 +50,8 @@ SIGNATURES: Dict[str, tuple] = {
     "std_gemm_rope_append": (I, [P, P, P, I, I, I, I, I, I, P, I, P, I, P, P, I, P, P, P, I, P, SZ, P]),
     "std_embed": (I, [P, I, I, PI32, I, I, I, I, P, P]),
     "std_gemm_set_smem_budget": (I, [I]),
+    "std_collect_workspace_bytes": (SZ, [I, I, I, I]),
+    "std_collect_relevance": (I, [P, P, PI32, I, I, I, I, I, I, I, PF, I64, P, SZ, P]),
     "std_gemm_plan": (I, [I, I, P]),
     "std_verify_policy": (I, [I, I, I, PI32, I, PI32, I, PI32, I, PI32, PI32, PI32, PF, F, I, I, I, PI32, PI32, PI32, PF,
                               I, PI32, ctypes.c_ulonglong, I, P]),

@@ -13,6 +13,7 @@
 #include "verify_attn.cu"
 #include "gemm.cu"
 #include "graph_loop.cu"
+#include "collect.cu"
 
 extern "C" int std_version(void) { return 100; }
 

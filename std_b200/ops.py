@@ -129,6 +129,24 @@ def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out: Optional
     return out
 
 
+def collect_relevance(q: torch.Tensor, k_cache: torch.Tensor, visual_pos: torch.Tensor, rel_out: torch.Tensor):
+    """Collector v1 for one layer: rel_out [B, Hkv, P] fp32 at the visual
+    positions gets sum over the verify rows of softmax over the visual keys of
+    (group-mean query . k) / sqrt(D).  q [B, nq, Hq, D] bf16; k_cache [B, Hkv,
+    cap, D] bf16; visual_pos [V] int32."""
+    B, nq, Hq, D = q.shape
+    _, Hkv, cap, _ = k_cache.shape
+    _check(q, torch.bfloat16, "q")
+    _check(k_cache, torch.bfloat16, "k_cache")
+    _check(visual_pos, torch.int32, "visual_pos")
+    _check(rel_out, torch.float32, "rel_out")
+    V = visual_pos.numel()
+    ws = workspace("collect", _lib.query("std_collect_workspace_bytes", B, Hkv, nq, V), q.device)
+    _lib.call("std_collect_relevance", q.data_ptr(), k_cache.data_ptr(), visual_pos.data_ptr(), V, B, nq, Hq, Hkv, D,
+              cap, rel_out.data_ptr(), rel_out.shape[-1], ws.data_ptr(), ws.numel(), _stream())
+    return rel_out
+
+
 # ----------------------------------------------------------------------------
 # selection
 # ----------------------------------------------------------------------------

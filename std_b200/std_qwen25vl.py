@@ -362,12 +362,9 @@ class STDRunner:
         self.device_loop = device_loop and use_graphs and shard is None and not self.dynamic
         self.prefill_done = False
         if self.dynamic:
-            vp = layout.visual_pos
-            v0, nvis = int(vp[0].item()), int(vp.numel())
             # relevance over prompt positions (only visual ones are ranked)
             self.relevance = torch.zeros(c.num_hidden_layers, batch_size, c.num_key_value_heads, P,
                                          dtype=torch.float32, device=dev)
-            self.vis_range = (v0, nvis) if int(vp[-1].item()) == v0 + nvis - 1 else None
             self.sel_stats = torch.zeros(batch_size, 2, dtype=torch.float32, device=dev)  # updates, changed sum
             self.update_flag = torch.zeros(batch_size, dtype=torch.bool, device=dev)
 
@@ -456,22 +453,10 @@ class STDRunner:
 
     def _collect(self, li: int, q4: torch.Tensor) -> None:
         """Collector v1 (dynamic_selection.py:290-308) for layer li of a verify
-        forward: A[b, h, v] = sum over the verify queries of softmax over the
-        visual keys of (group-mean query . k_v) / sqrt(D)."""
-        B, nq, Hq, D = q4.shape
-        Hkv = self.model.config.num_key_value_heads
-        qk = q4.view(B, nq, Hkv, Hq // Hkv, D).float().mean(dim=3).permute(0, 2, 1, 3).to(q4.dtype)
-        if self.vis_range is not None:
-            v0, nvis = self.vis_range
-            kv = self.dense[li, 0, :, :, v0:v0 + nvis]
-        else:
-            kv = self.dense[li, 0].index_select(2, self.layout.visual_pos.long())
-        logits = torch.matmul(qk, kv.transpose(-1, -2)).float() * (1.0 / math.sqrt(D))
-        rel = torch.softmax(logits, dim=-1).sum(dim=2)  # [B, Hkv, V]
-        if self.vis_range is not None:
-            self.relevance[li, :, :, v0:v0 + nvis] = rel
-        else:
-            self.relevance[li].index_copy_(2, self.layout.visual_pos.long(), rel)
+        forward, on the device in fp32 (libstd_b200 collect.cu): A[b, h, v] =
+        sum over the verify queries of softmax over the visual keys of
+        (group-mean query . k_v) / sqrt(D), written at the visual positions."""
+        ops.collect_relevance(q4, self.dense[li, 0], self.layout.visual_pos, self.relevance[li])
 
     def _update_selection(self) -> None:
         """S_{t+1} = TopK(A_t) per (layer, request, KV head), applied to request

@@ -686,3 +686,50 @@ def test_gemm_argmax_margin(ops, M, N, K):
     assert torch.equal(marg, top2.values[:, 0] - top2.values[:, 1])
     assert torch.equal(out.long(), logits.float().argmax(-1))
     _no_device_error(ops)
+
+
+# ------------------------------------------------------------------ collector (f)
+def test_collect_relevance_matches_reference_and_oracle(ops):
+    """Collector v1 on the device (fp32) against the reference's own
+    RuntimeVerificationCollector on the same inputs (tests/golden/
+    collector_layer.npz) and against the fp64 restatement, with the visual
+    keys given as an index list; positions outside it are left untouched."""
+    import sys
+
+    sys.path.insert(0, GOLDEN)
+    from make_golden import COLLECT, collector_inputs
+
+    g = np.load(os.path.join(GOLDEN, "collector_layer.npz"))
+    q, k, vis = collector_inputs()  # q [1, Hq, nq, D], k [1, Hkv, P, D] bf16
+    qd = q.permute(0, 2, 1, 3).contiguous().cuda()  # [B, nq, Hq, D]
+    kd = k.contiguous().cuda()
+    rel = torch.full((1, COLLECT["Hkv"], COLLECT["P"]), -1.0, device="cuda")
+    ops.collect_relevance(qd, kd, vis.to(torch.int32).cuda(), rel)
+    torch.cuda.synchronize()
+    got = rel[0, :, vis].cpu().numpy()
+    ref = g["rel"]
+    assert np.abs(got - ref).max() <= 2e-5 * max(1.0, np.abs(ref).max())
+    want = oracle.collect_relevance(q.float().numpy(), k.float().numpy(), vis.numpy())[0]
+    assert np.abs(got - want).max() <= 2e-5 * max(1.0, np.abs(want).max())
+    others = torch.ones(COLLECT["P"], dtype=torch.bool)
+    others[vis] = False
+    assert torch.all(rel[0][:, others.cuda()] == -1.0)
+    _no_device_error(ops)
+
+
+@pytest.mark.parametrize("B,nq,V", [(2, 10, 32768), (3, 1, 300)])
+def test_collect_relevance_shapes_vs_oracle(ops, B, nq, V):
+    g = torch.Generator(device="cuda").manual_seed(V + nq)
+    P = V + 200
+    q = torch.randn(B, nq, 28, 128, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, 4, P + 64, 128, generator=g, device="cuda").to(torch.bfloat16)
+    vis = torch.arange(50, 50 + V, dtype=torch.int32, device="cuda")
+    rel = torch.zeros(B, 4, P + 64, device="cuda")
+    ops.collect_relevance(q, k, vis, rel)
+    torch.cuda.synchronize()
+    got = rel[:, :, 50:50 + V].cpu().numpy()
+    want = oracle.collect_relevance(q.permute(0, 2, 1, 3).float().cpu().numpy(), k.float().cpu().numpy(),
+                                    vis.cpu().numpy())
+    assert np.abs(got - want).max() <= 2e-5 * max(1.0, np.abs(want).max())
+    assert np.allclose(got.sum(-1), nq, rtol=1e-4)
+    _no_device_error(ops)

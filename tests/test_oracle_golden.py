@@ -208,3 +208,27 @@ def test_selection_matches_reference_config3_sizes():
         for p in diff:
             assert p in ref_score and abs(ref_score[p] - kth) <= band * kth, (h, p)
     assert n_diff <= 16  # a handful of boundary positions out of 4 x 3968
+
+
+def test_collector_oracle_matches_reference():
+    """The collector restatement (fp64) against the reference's own
+    RuntimeVerificationCollector._hook (fp32 torch) on the same bf16 inputs."""
+    import torch
+
+    from oracle.inputs import bf16_bits, digest
+
+    sys_path_golden = os.path.join(os.path.dirname(__file__), "golden")
+    import sys
+
+    sys.path.insert(0, sys_path_golden)
+    from make_golden import collector_inputs
+
+    g = np.load(os.path.join(GOLDEN, "collector_layer.npz"))
+    q, k, vis = collector_inputs()
+    assert digest(bf16_bits(q)) == str(g["q_digest"]) and digest(bf16_bits(k)) == str(g["k_digest"])
+    rel = oracle.collect_relevance(q.float().numpy(), k.float().numpy(), vis.numpy())[0]
+    ref = g["rel"]
+    assert np.abs(rel - ref).max() <= 1e-6 * max(1.0, np.abs(ref).max())
+    # the top of the ranking (what re-selection keeps) agrees
+    for h in range(ref.shape[0]):
+        assert set(np.argsort(-rel[h])[:64]) == set(np.argsort(-ref[h])[:64])
