@@ -110,6 +110,19 @@ int std_verify_attn_noalloc(const void* q, const void* k_cache, const void* v_ca
                             int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out,
                             float* lse, void* stream);
 
+/* std_verify_attn with an fp32 output (out_f32 [B, nq, Hq, D]) and a
+ * required natural-log LSE: the partial of one key range for a
+ * sequence-sharded verify, merged with std_merge_partials_f32 (no reference
+ * counterpart). */
+int std_verify_attn_partial(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
+                            int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap, float* out_f32,
+                            float* lse, void* workspace, size_t workspace_bytes, void* stream);
+/* Exact (O, LSE) merge of fp32 partials packed one buffer per part: part i
+ * is [rows * D O | rows LSE] at parts + i * part_stride floats; out [rows, D]
+ * bf16, lse_out [rows] (optional).  The merge step of sequence-sharded verify
+ * after one all-gather of the packed partials. */
+int std_merge_partials_f32(const float* parts, long long part_stride, int n_parts, int rows, int D, void* out,
+                           float* lse_out, void* stream);
 /* Exact (O, LSE) merge of attention partials computed over disjoint key
  * ranges (sequence shards).  Replaces nothing in the reference (it has no
  * sequence parallelism); it is the exchange step of sharded verify.

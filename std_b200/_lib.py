@@ -36,6 +36,8 @@ SIGNATURES: Dict[str, tuple] = {
     "std_verify_attn": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, P, PF, P, SZ, P]),
     "std_verify_attn_noalloc": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, P, PF, P]),
     "std_merge_partials": (I, [P, PF, I, I, I, P, PF, P]),
+    "std_verify_attn_partial": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, PF, PF, P, SZ, P]),
+    "std_merge_partials_f32": (I, [PF, I64, I, I, I, P, PF, P]),
     "std_select_workspace_bytes": (SZ, [I, I, I]),
     "std_select_scores": (I, [P, P, I64, I, I, I, I, I, I, F, PF, I, P, SZ, P]),
     "std_select_probs_view": (I, [I, I, I, P]),

@@ -52,6 +52,7 @@ struct VerifyParams {
   int causal;              // 1: row t sees keys <= L-nq+t ; 0: every row sees all L keys
   float scale_log2;
   __nv_bfloat16* out;      // [B, nq, Hq, D]
+  float* out_f32;          // non-null: fp32 output [B, nq, Hq, D] instead of out (sharded partials)
   float* lse;              // [B, nq, Hq] natural log, may be null
   float* ws_ml;            // [B, Hkv, max_splits, 128, 2]
   float* ws_o;             // [B, Hkv, max_splits, 128, D]
@@ -327,7 +328,12 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
           v[j] = x * inv;
         }
         if (valid_row) {
-          if (single) {
+          if (single && p.out_f32 != nullptr) {
+            float4* dst = reinterpret_cast<float4*>(
+                p.out_f32 + ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + piece * 32);
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) dst[c4] = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+          } else if (single) {
             uint4* dst = reinterpret_cast<uint4*>(
                 p.out + ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + piece * 32);
 #pragma unroll
@@ -402,11 +408,15 @@ __global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p)
   }
   const float inv = l > 0.f ? 1.f / l : 0.f;
   const int t = r / VF_G, g = r % VF_G;
-  uint2 pk;
-  pk.x = pack_bf16x2(a.x * inv, a.y * inv);
-  pk.y = pack_bf16x2(a.z * inv, a.w * inv);
-  *reinterpret_cast<uint2*>(p.out + ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + 4 * d4) =
-      pk;
+  const size_t o = ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + 4 * d4;
+  if (p.out_f32 != nullptr) {
+    *reinterpret_cast<float4*>(p.out_f32 + o) = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+  } else {
+    uint2 pk;
+    pk.x = pack_bf16x2(a.x * inv, a.y * inv);
+    pk.y = pack_bf16x2(a.z * inv, a.w * inv);
+    *reinterpret_cast<uint2*>(p.out + o) = pk;
+  }
   if (d4 == 0 && p.lse != nullptr)
     p.lse[(static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g] =
         l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
@@ -454,11 +464,32 @@ extern "C" size_t std_verify_attn_workspace_bytes(int B, int Hkv, int cap) {
   return bytes;
 }
 
+static int verify_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens, int len_offset,
+                         int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out, float* out_f32,
+                         float* lse, void* workspace, size_t workspace_bytes, void* stream);
+
 extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
                                int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out,
                                float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+  if (out == nullptr) return 1;
+  return verify_launch(q, k_cache, v_cache, lens, len_offset, nq, causal, B, Hq, Hkv, D, cap, out, nullptr, lse,
+                       workspace, workspace_bytes, stream);
+}
+
+extern "C" int std_verify_attn_partial(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens,
+                                       int len_offset, int nq, int causal, int B, int Hq, int Hkv, int D, int cap,
+                                       float* out_f32, float* lse, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  if (out_f32 == nullptr || lse == nullptr) return 1;
+  return verify_launch(q, k_cache, v_cache, lens, len_offset, nq, causal, B, Hq, Hkv, D, cap, nullptr, out_f32, lse,
+                       workspace, workspace_bytes, stream);
+}
+
+static int verify_launch(const void* q, const void* k_cache, const void* v_cache, const int32_t* lens, int len_offset,
+                         int nq, int causal, int B, int Hq, int Hkv, int D, int cap, void* out, float* out_f32,
+                         float* lse, void* workspace, size_t workspace_bytes, void* stream) {
   if (D != stdb::VF_D || Hq != Hkv * stdb::VF_G || nq < 1 || stdb::VF_G * nq > 128 || B <= 0 || cap <= 0) return 1;
-  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || lens == nullptr || out == nullptr) return 1;
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || lens == nullptr) return 1;
   if (((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(q)) &
        15) != 0)
     return 1;
@@ -481,6 +512,7 @@ extern "C" int std_verify_attn(const void* q, const void* k_cache, const void* v
   p.causal = causal;
   p.scale_log2 = (1.0f / sqrtf(static_cast<float>(D))) * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_f32 = out_f32;
   p.lse = lse;
   p.split_keys = verify_split_keys(B, Hkv, cap);
   p.max_splits = (cap + p.split_keys - 1) / p.split_keys;

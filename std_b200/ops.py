@@ -116,6 +116,33 @@ def verify_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out
 
 
+def verify_attention_partial(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lens: torch.Tensor,
+                             len_offset: int, causal: bool, out_f32: torch.Tensor, lse: torch.Tensor):
+    """verify_attention with an fp32 output and its LSE (one key range's
+    partial of a sequence-sharded verify)."""
+    B, nq, Hq, D = q.shape
+    _, Hkv, cap, _ = k_cache.shape
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _check(t, torch.bfloat16, n)
+    _check(out_f32, torch.float32, "out_f32")
+    _check(lse, torch.float32, "lse")
+    nb = _lib.query("std_verify_attn_workspace_bytes", B, Hkv, cap)
+    ws = workspace("verify", nb, q.device)
+    _lib.call("std_verify_attn_partial", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lens.data_ptr(),
+              int(len_offset), nq, 1 if causal else 0, B, Hq, Hkv, D, cap, out_f32.data_ptr(), lse.data_ptr(),
+              ws.data_ptr(), ws.numel(), _stream())
+    return out_f32
+
+
+def merge_partials_f32(parts: torch.Tensor, rows: int, D: int, out: torch.Tensor,
+                       lse_out: Optional[torch.Tensor] = None):
+    """parts [n, stride] fp32, each [rows*D O | rows LSE] -> out [rows, D] bf16."""
+    n, stride = parts.shape
+    _check(parts, torch.float32, "parts")
+    _lib.call("std_merge_partials_f32", parts.data_ptr(), stride, n, rows, D, out.data_ptr(), _p(lse_out), _stream())
+    return out
+
+
 def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out: Optional[torch.Tensor] = None,
                    lse_out: Optional[torch.Tensor] = None):
     """o_parts [n, rows, D] bf16, lse_parts [n, rows] fp32 -> out [rows, D]."""

@@ -13,13 +13,14 @@ request is split by sequence position across the ranks of one node:
 
 A dense forward on the owner (a verify block or an AR step) exchanges, per
 layer: the owner broadcasts the layer's queries, every rank computes the
-(O, LSE) partial of its key range with the verify kernel (the owner causal
-over its local keys, the servers non-causal), the partials are all-gathered
-and the owner merges them in rank order with std_merge_partials.  Attention
-over disjoint key ranges combines exactly through LSE, so the only difference
-from the unsharded result is fp32 rounding at fixed boundaries -- identical for
-a token verified in a block and the same token decoded alone, which keeps
-STD == AR.
+(O, LSE) partial of its key range with the verify kernel in fp32 (the owner
+causal over its local keys, the servers non-causal) into one packed buffer
+[O | LSE], the packed partials are all-gathered in one collective and the
+owner merges them in rank order with std_merge_partials_f32: two collectives
+per layer.  Attention over disjoint key ranges combines exactly through LSE,
+so the only difference from the unsharded result is fp32 rounding at fixed
+boundaries -- identical for a token verified in a block and the same token
+decoded alone, which keeps STD == AR.
 
 Each forward starts with a 2-int header broadcast ([1, nq]); [0, 0] ends the
 servers' loop.  The collectives run on NCCL over NVLink (gloo on CPU for the
@@ -65,16 +66,16 @@ class ShardPlan:
         return ShardPlan(world=world, shard=s, cap=cap)
 
 
-def _verify_partial(q4, kc, vc, lens, len_offset, causal, out, lse):
+def _verify_partial(q4, kc, vc, lens, len_offset, causal, out_f32, lse):
     from . import ops
 
-    ops.verify_attention(q4, kc, vc, lens, len_offset, causal=causal, out=out, lse=lse)
+    ops.verify_attention_partial(q4, kc, vc, lens, len_offset, causal, out_f32, lse)
 
 
-def _merge(o_parts, lse_parts, out):
+def _merge(parts, rows, D, out):
     from . import ops
 
-    ops.merge_partials(o_parts, lse_parts, out=out)
+    ops.merge_partials_f32(parts, rows, D, out)
 
 
 class ShardExchange:
@@ -93,10 +94,9 @@ class ShardExchange:
         N = plan.world
         rows = B * max_nq * Hq
         self.q = torch.zeros(rows * D, dtype=torch.bfloat16, device=self.device)
-        self.o_loc = torch.zeros(rows * D, dtype=torch.bfloat16, device=self.device)
-        self.lse_loc = torch.zeros(rows, dtype=torch.float32, device=self.device)
-        self.o_all = torch.zeros(N * rows * D, dtype=torch.bfloat16, device=self.device)
-        self.lse_all = torch.zeros(N * rows, dtype=torch.float32, device=self.device)
+        # packed fp32 partial of this rank, [rows * D O | rows LSE], and all ranks'
+        self.part = torch.zeros(rows * (D + 1), dtype=torch.float32, device=self.device)
+        self.parts = torch.zeros(N * rows * (D + 1), dtype=torch.float32, device=self.device)
         self.hdr = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.is_owner = rank == plan.owner
 
@@ -114,16 +114,15 @@ class ShardExchange:
                   out4: Optional[torch.Tensor]) -> None:
         B, Hq, D, N = self.B, self.Hq, self.D, self.plan.world
         rows = B * nq * Hq
+        n = rows * (D + 1)
         self._bcast(q4)
-        o_loc = self.o_loc[: rows * D].view(B, nq, Hq, D)
-        lse_loc = self.lse_loc[:rows].view(B, nq, Hq)
-        self.partial_fn(q4, kc, vc, lens, len_offset, causal, o_loc, lse_loc)
-        o_all = self.o_all[: N * rows * D]
-        lse_all = self.lse_all[: N * rows]
-        self._all_gather(o_all, self.o_loc[: rows * D])
-        self._all_gather(lse_all, self.lse_loc[:rows])
+        part = self.part[:n]
+        self.partial_fn(q4, kc, vc, lens, len_offset, causal, part[: rows * D].view(B, nq, Hq, D),
+                        part[rows * D:].view(B, nq, Hq))
+        parts = self.parts[: N * n]
+        self._all_gather(parts, part)
         if out4 is not None:
-            self.merge_fn(o_all.view(N, rows, D), lse_all.view(N, rows), out4.view(rows, D))
+            self.merge_fn(parts.view(N, n), rows, D, out4.view(rows, D))
 
     # ------------------------------------------------------------ owner side
     def begin(self, nq: int) -> None:

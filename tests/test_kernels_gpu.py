@@ -649,6 +649,19 @@ def test_configs3_sizes_verify_sharded_merge_and_draft(ops):
     merged = ops.merge_partials(parts.view(2, nq * 28, 128), lse.view(2, nq * 28))
     err = (merged.view(nq, 28, 128).float().permute(1, 0, 2) - ref).abs()
     assert err.max().item() <= ATOL_MAX and err.mean().item() <= ATOL_MEAN
+    # the same with fp32 partials packed [O | LSE] per shard (the sharded verify's exchange format)
+    rows = nq * 28
+    packed = torch.empty(2, rows * 129, dtype=torch.float32, device="cuda")
+    ops.verify_attention_partial(q, kp, vp, torch.tensor([S], dtype=torch.int32, device="cuda"), 0, False,
+                                 packed[0, : rows * 128].view(1, nq, 28, 128), packed[0, rows * 128:].view(1, nq, 28))
+    ops.verify_attention_partial(q, kt, vt, torch.tensor([L - nq - S], dtype=torch.int32, device="cuda"), nq, True,
+                                 packed[1, : rows * 128].view(1, nq, 28, 128), packed[1, rows * 128:].view(1, nq, 28))
+    assert torch.allclose(packed[:, rows * 128:], lse.view(2, rows), atol=1e-5)
+    assert (packed[:, : rows * 128].view(2, nq, 28, 128) - parts[:, 0].float()).abs().max().item() < 1e-2
+    merged32 = torch.empty(rows, 128, dtype=torch.bfloat16, device="cuda")
+    ops.merge_partials_f32(packed, rows, 128, merged32)
+    err32 = (merged32.view(nq, 28, 128).float().permute(1, 0, 2) - ref).abs()
+    assert err32.max().item() <= ATOL_MAX and err32.mean().item() <= err.mean().item() * 1.05
     # draft over the configs[3] sparse cache length
     Ls = 4224
     qd = torch.randn(1, 28, 128, generator=g, device="cuda").to(torch.bfloat16)

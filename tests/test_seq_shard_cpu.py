@@ -2,9 +2,10 @@
 per-layer exchange protocol, on CPU ranks over gloo (world sizes 2 and 3).
 
 The attention partial and the merge are torch fp32 stand-ins of the verify
-kernel and std_merge_partials (same conventions: keys L = lens[b] +
-len_offset, causal row t sees keys <= L - nq + t, natural-log LSE); the
-collective order, buffers and rank roles are the product code's."""
+kernel's fp32 partial and std_merge_partials_f32 (same conventions: keys L =
+lens[b] + len_offset, causal row t sees keys <= L - nq + t, natural-log LSE,
+one packed [O | LSE] buffer per rank); the collective order, buffers and rank
+roles are the product code's."""
 import os
 import socket
 
@@ -36,7 +37,9 @@ def ref_partial(q4, kc, vc, lens, len_offset, causal, out, lse):
         lse[b] = m.transpose(0, 1)
 
 
-def ref_merge(o_parts, lse_parts, out):
+def ref_merge(parts, rows, D, out):
+    o_parts = parts[:, : rows * D].view(-1, rows, D)
+    lse_parts = parts[:, rows * D: rows * (D + 1)]
     mx = lse_parts.max(dim=0).values
     w = torch.exp(lse_parts - mx)
     w = torch.where(torch.isfinite(lse_parts), w, torch.zeros_like(w))
@@ -115,7 +118,7 @@ def test_sharded_attention_protocol(world):
     assert all(m[2] == len(nqs) for m in served)
     assert [m[1] for m in owner] == nqs
     for _, nq, worst in owner:
-        assert worst <= 2e-2, (nq, worst)   # bf16 partials merged in fp32
+        assert worst <= 2e-2, (nq, worst)   # fp32 partials merged, bf16 output
 
 
 def test_shard_plan():
