@@ -150,13 +150,11 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   const int row0 = (b * p.Hkv + kvh) * p.cap;
 
   if (warp == 8) {
-    // ---------------- TMA producer ----------------
-    // K and V have rings of their own: S of chunk c (which needs K) is issued
-    // two chunks ahead of P V of chunk c (which needs V), and a K stage is
-    // free as soon as its S retires, so K is requested VF_LEAD chunks ahead
-    // of V: K(0) .. K(LEAD-1), then V(c) and K(c + LEAD) alternately.
-    if (lane == 0) {
-      constexpr int VF_LEAD = 2;
+    // ---------------- TMA producers ----------------
+    // K and V have rings of their own, each filled by its own thread (lane 0:
+    // K, lane 1: V), so a full V ring never holds back a K load: a K stage is
+    // free as soon as S of its chunk retires, a V stage once P V does.
+    if (lane < 2) {
       const uint64_t pol = l2_policy_evict_first();  // each K/V row is read once per forward
       int k_issued = 0, v_issued = 0;
       bool ok = true;
@@ -182,11 +180,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         v_issued = c + 1;
         return true;
       };
-      for (int c = 0; ok && c < min(VF_LEAD, nchunks); ++c) ok = issue_k(c);
-      for (int c = 0; ok && c < nchunks; ++c) {
-        ok = issue_v(c);
-        if (ok && c + VF_LEAD < nchunks) ok = issue_k(c + VF_LEAD);
-      }
+      for (int c = 0; ok && c < nchunks; ++c) ok = lane == 0 ? issue_k(c) : issue_v(c);
       // never leave a copy in flight: wait for the last load of each stage
       for (int c = k_issued - VF_KSTAGES < 0 ? 0 : k_issued - VF_KSTAGES; c < k_issued; ++c)
         mbar_wait(&bar_k_full[c % VF_KSTAGES], (c / VF_KSTAGES) & 1);
