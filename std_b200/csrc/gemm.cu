@@ -31,6 +31,7 @@ constexpr int GM_MAX_STAGES = 8;
 constexpr uint32_t GM_SMEM_BUDGET = 104 * 1024;  // per CTA: two CTAs per SM
 constexpr int GM_THREADS = 128;
 constexpr uint32_t GM_WTILE = GM_BM * GM_BK * 2;  // 16 KB
+constexpr int GM_SUM_BATCH = 8;                    // split partials loaded per batch by the epilogues
 
 struct GemmParams {
   int M, N, K, nmma, splits, kblocks, stages;
@@ -251,12 +252,20 @@ __global__ void gemm_reduce_kernel(const float* __restrict__ partial, int splits
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     float4 a = reinterpret_cast<const float4*>(partial)[i];
-    for (int s = 1; s < splits; ++s) {
-      const float4 b = reinterpret_cast<const float4*>(partial + static_cast<size_t>(s) * M * N)[i];
-      a.x += b.x;
-      a.y += b.y;
-      a.z += b.z;
-      a.w += b.w;
+    for (int s0 = 1; s0 < splits; s0 += GM_SUM_BATCH) {  // batched loads, adds in split order
+      float4 b[GM_SUM_BATCH];
+#pragma unroll
+      for (int j = 0; j < GM_SUM_BATCH; ++j)
+        if (s0 + j < splits) b[j] = reinterpret_cast<const float4*>(partial + static_cast<size_t>(s0 + j) * M * N)[i];
+#pragma unroll
+      for (int j = 0; j < GM_SUM_BATCH; ++j) {
+        if (s0 + j < splits) {
+          a.x += b[j].x;
+          a.y += b[j].y;
+          a.z += b[j].z;
+          a.w += b[j].w;
+        }
+      }
     }
     const int f = static_cast<int>((i * 4) % N);
     if (bias != nullptr) {
@@ -289,20 +298,35 @@ struct GemmOut {
       return;
     }
     const size_t off = row * N + col;
+    const size_t MN = static_cast<size_t>(M) * N;
     float4 a = __ldcg(reinterpret_cast<const float4*>(partial + off));
     float4 b = __ldcg(reinterpret_cast<const float4*>(partial + off + 4));
-    for (int s = 1; s < splits; ++s) {
-      const float* ps = partial + static_cast<size_t>(s) * M * N + off;
-      const float4 c = __ldcg(reinterpret_cast<const float4*>(ps));
-      const float4 d = __ldcg(reinterpret_cast<const float4*>(ps + 4));
-      a.x += c.x;
-      a.y += c.y;
-      a.z += c.z;
-      a.w += c.w;
-      b.x += d.x;
-      b.y += d.y;
-      b.z += d.z;
-      b.w += d.w;
+    // splits 1.. in batches of GM_SUM_BATCH: every load of a batch is issued
+    // before the first add (one L2 latency per batch), then the adds run in
+    // split order, so the sum is the same as a one-at-a-time loop
+    for (int s0 = 1; s0 < splits; s0 += GM_SUM_BATCH) {
+      float4 c[GM_SUM_BATCH], d[GM_SUM_BATCH];
+#pragma unroll
+      for (int j = 0; j < GM_SUM_BATCH; ++j) {
+        if (s0 + j < splits) {
+          const float* ps = partial + static_cast<size_t>(s0 + j) * MN + off;
+          c[j] = __ldcg(reinterpret_cast<const float4*>(ps));
+          d[j] = __ldcg(reinterpret_cast<const float4*>(ps + 4));
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < GM_SUM_BATCH; ++j) {
+        if (s0 + j < splits) {
+          a.x += c[j].x;
+          a.y += c[j].y;
+          a.z += c[j].z;
+          a.w += c[j].w;
+          b.x += d[j].x;
+          b.y += d[j].y;
+          b.z += d[j].z;
+          b.w += d[j].w;
+        }
+      }
     }
     float t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     if (bias != nullptr) {
