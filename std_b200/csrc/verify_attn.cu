@@ -15,11 +15,9 @@
 //   O   += P_c V_c    tcgen05.mma into one TMEM accumulator, V MN-major
 // m_row is a running row max; O is rescaled in TMEM only when a chunk raises
 // the max by more than 2^8 (lazy rescale), so the softmax threads normally
-// touch TMEM once per chunk.  Warp roles: warps 0-7 are two softmax
-// warpgroups (one TMEM row per thread, alternate chunks); warp 8 lane 0
-// issues TMA into separate K and V rings (a K stage frees when S of its chunk
-// retires, a V stage when P V does); warp 9 allocates TMEM and lane 0 issues
-// the MMAs.  Splits write (O, m, l) partials that a
+// touch TMEM once per chunk.  Warp roles: warps 0-3 own TMEM lanes 0-127 (one
+// row per thread); warp 4 lane 0 issues TMA (2 K/V stages); warp 5 allocates
+// TMEM and lane 0 issues the MMAs.  Splits write (O, m, l) partials that a
 // second kernel combines; a request whose keys fit one split writes its output
 // directly.
 //
@@ -37,15 +35,13 @@ namespace stdb {
 
 constexpr int VF_D = 128;
 constexpr int VF_CHUNK = 64;       // keys per chunk (MMA N of S, K of P V)
-constexpr int VF_KSTAGES = 4;      // K ring depth (a K stage is free once S of its chunk retires)
-constexpr int VF_VSTAGES = 5;      // V ring depth (a V stage is free once P V of its chunk retires)
+constexpr int VF_STAGES = 4;       // K/V ring depth
 constexpr int VF_THREADS = 320;    // 2 softmax warpgroups + TMA warp + MMA warp
 constexpr int VF_G = 7;
 constexpr uint32_t VF_QTILE = 32768;  // 128 rows x 256 B (two 64-d K-blocks)
 constexpr uint32_t VF_KV = 16384;     // one K or V chunk: 64 keys x 256 B (two 8 KB d-blocks)
 constexpr uint32_t VF_PTILE = 16384;  // 128 rows x 64 keys bf16 (one K-block)
-constexpr uint32_t VF_SMEM = VF_QTILE + (VF_KSTAGES + VF_VSTAGES) * VF_KV + 2 * VF_PTILE + 1024;
-static_assert(VF_SMEM <= 227 * 1024, "verify shared memory");
+constexpr uint32_t VF_SMEM = VF_QTILE + 2 * VF_STAGES * VF_KV + 2 * VF_PTILE + 1024;
 constexpr float VF_RESCALE = 8.0f;    // log2 units
 
 struct VerifyParams {
@@ -72,8 +68,7 @@ STD_DEV int verify_len(const VerifyParams& p, int b) {
 }
 
 // Chunk c of a split goes to softmax warpgroup / TMEM accumulator (c & 1);
-// S buffer (c & 1), P buffer (c & 1), K stage (c % VF_KSTAGES), V stage
-// (c % VF_VSTAGES).
+// S buffer (c & 1), P buffer (c & 1), K/V stage (c % 4).
 __global__ void __launch_bounds__(VF_THREADS, 1)
     verify_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const VerifyParams p) {
@@ -96,12 +91,12 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = smem + VF_QTILE;                       // [VF_KSTAGES][VF_KV]
-  uint8_t* sV = sK + VF_KSTAGES * VF_KV;               // [VF_VSTAGES][VF_KV]
-  uint8_t* sP = sV + VF_VSTAGES * VF_KV;               // [2][VF_PTILE]
+  uint8_t* sK = smem + VF_QTILE;                       // [VF_STAGES][VF_KV]
+  uint8_t* sV = sK + VF_STAGES * VF_KV;                // [VF_STAGES][VF_KV]
+  uint8_t* sP = sV + VF_STAGES * VF_KV;                // [2][VF_PTILE]
 
-  __shared__ __align__(8) uint64_t bar_q, bar_k_full[VF_KSTAGES], bar_k_empty[VF_KSTAGES], bar_v_full[VF_VSTAGES],
-      bar_v_empty[VF_VSTAGES], bar_s_full[2], bar_s_free[2], bar_p_full[2], bar_mma_done;
+  __shared__ __align__(8) uint64_t bar_q, bar_kv_full[VF_STAGES], bar_kv_empty[VF_STAGES], bar_s_full[2],
+      bar_s_free[2], bar_p_full[2], bar_mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ float s_mB[128], s_lB[128];
 
@@ -111,13 +106,9 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   }
   if (tid == 256) {
     mbar_init(&bar_q, 128);
-    for (int i = 0; i < VF_KSTAGES; ++i) {
-      mbar_init(&bar_k_full[i], 1);
-      mbar_init(&bar_k_empty[i], 1);
-    }
-    for (int i = 0; i < VF_VSTAGES; ++i) {
-      mbar_init(&bar_v_full[i], 1);
-      mbar_init(&bar_v_empty[i], 1);
+    for (int i = 0; i < VF_STAGES; ++i) {
+      mbar_init(&bar_kv_full[i], 1);
+      mbar_init(&bar_kv_empty[i], 1);
     }
     // only the warps that hold query rows take part in the softmax handshakes
     const uint32_t live_threads = 32u * static_cast<uint32_t>(min(4, (nrows + 31) / 32));
@@ -150,42 +141,26 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   const int row0 = (b * p.Hkv + kvh) * p.cap;
 
   if (warp == 8) {
-    // ---------------- TMA producers ----------------
-    // K and V have rings of their own, each filled by its own thread (lane 0:
-    // K, lane 1: V), so a full V ring never holds back a K load: a K stage is
-    // free as soon as S of its chunk retires, a V stage once P V does.
-    if (lane < 2) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();  // each K/V row is read once per forward
-      int k_issued = 0, v_issued = 0;
-      bool ok = true;
-      auto issue_k = [&](int c) {
-        const int st = c % VF_KSTAGES;
-        if (c >= VF_KSTAGES && !mbar_wait(&bar_k_empty[st], ((c / VF_KSTAGES) - 1) & 1)) return false;
-        mbar_arrive_expect_tx(&bar_k_full[st], VF_KV);
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % VF_STAGES;
+        if (c >= VF_STAGES && !mbar_wait(&bar_kv_empty[st], ((c / VF_STAGES) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&bar_kv_full[st], 2 * VF_KV);
         const int y = row0 + k0 + c * VF_CHUNK;
         uint8_t* kd = sK + st * VF_KV;
-        tma_load_2d_hint(kd, &tmK, &bar_k_full[st], 0, y, pol);
-        tma_load_2d_hint(kd + VF_KV / 2, &tmK, &bar_k_full[st], 64, y, pol);
-        k_issued = c + 1;
-        return true;
-      };
-      auto issue_v = [&](int c) {
-        const int st = c % VF_VSTAGES;
-        if (c >= VF_VSTAGES && !mbar_wait(&bar_v_empty[st], ((c / VF_VSTAGES) - 1) & 1)) return false;
-        mbar_arrive_expect_tx(&bar_v_full[st], VF_KV);
-        const int y = row0 + k0 + c * VF_CHUNK;
         uint8_t* vd = sV + st * VF_KV;
-        tma_load_2d_hint(vd, &tmV, &bar_v_full[st], 0, y, pol);
-        tma_load_2d_hint(vd + VF_KV / 2, &tmV, &bar_v_full[st], 64, y, pol);
-        v_issued = c + 1;
-        return true;
-      };
-      for (int c = 0; ok && c < nchunks; ++c) ok = lane == 0 ? issue_k(c) : issue_v(c);
+        tma_load_2d_hint(kd, &tmK, &bar_kv_full[st], 0, y, pol);
+        tma_load_2d_hint(kd + VF_KV / 2, &tmK, &bar_kv_full[st], 64, y, pol);
+        tma_load_2d_hint(vd, &tmV, &bar_kv_full[st], 0, y, pol);
+        tma_load_2d_hint(vd + VF_KV / 2, &tmV, &bar_kv_full[st], 64, y, pol);
+        issued = c + 1;
+      }
       // never leave a copy in flight: wait for the last load of each stage
-      for (int c = k_issued - VF_KSTAGES < 0 ? 0 : k_issued - VF_KSTAGES; c < k_issued; ++c)
-        mbar_wait(&bar_k_full[c % VF_KSTAGES], (c / VF_KSTAGES) & 1);
-      for (int c = v_issued - VF_VSTAGES < 0 ? 0 : v_issued - VF_VSTAGES; c < v_issued; ++c)
-        mbar_wait(&bar_v_full[c % VF_VSTAGES], (c / VF_VSTAGES) & 1);
+      for (int c = issued - VF_STAGES < 0 ? 0 : issued - VF_STAGES; c < issued; ++c)
+        mbar_wait(&bar_kv_full[c % VF_STAGES], (c / VF_STAGES) & 1);
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
@@ -196,8 +171,8 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
       bool ok = mbar_wait(&bar_q, 0);
       tc_fence_after();
       auto issue_S = [&](int c) -> bool {
-        const int st = c % VF_KSTAGES, w = c & 1;
-        if (!mbar_wait(&bar_k_full[st], (c / VF_KSTAGES) & 1)) return false;
+        const int st = c % VF_STAGES, w = c & 1;
+        if (!mbar_wait(&bar_kv_full[st], (c / VF_STAGES) & 1)) return false;
         if (c >= 2 && !mbar_wait(&bar_s_free[w], ((c >> 1) - 1) & 1)) return false;
         tc_fence_after();
         const uint32_t aK = smem_u32(sK + st * VF_KV);
@@ -209,14 +184,13 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
                     ks > 0 ? 1u : 0u);
         }
         umma_commit(&bar_s_full[w]);
-        umma_commit(&bar_k_empty[st]);  // K of chunk c is free once these MMAs retire
         return true;
       };
       if (ok) ok = issue_S(0);
       if (ok && nchunks > 1) ok = issue_S(1);
       for (int c = 0; ok && c < nchunks; ++c) {
-        const int w = c & 1, st = c % VF_VSTAGES;
-        if (!mbar_wait(&bar_p_full[w], (c >> 1) & 1) || !mbar_wait(&bar_v_full[st], (c / VF_VSTAGES) & 1)) {
+        const int w = c & 1, st = c % VF_STAGES;
+        if (!mbar_wait(&bar_p_full[w], (c >> 1) & 1)) {
           ok = false;
           break;
         }
@@ -227,7 +201,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
           umma_bf16(tmem + 128 + 128 * w, sdesc_sw128(aP + ks * 32u, 16, 1024),
                     sdesc_sw128(aV + ks * 2048u, VF_KV / 2, 1024), idO, (c >= 2 || ks > 0) ? 1u : 0u);
         }
-        umma_commit(&bar_v_empty[st]);
+        umma_commit(&bar_kv_empty[st]);
         if (c + 2 < nchunks && !issue_S(c + 2)) {
           ok = false;
           break;

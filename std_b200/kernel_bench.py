@@ -4,6 +4,7 @@
     python -m std_b200.kernel_bench --kernel draft  --B 8 --L 1025
     python -m std_b200.kernel_bench --kernel gemm   --M 8 --N 4608 --K 3584 [--cublas]
     python -m std_b200.kernel_bench --kernel forward --B 8 --L 32906 [--gamma 9]
+    python -m std_b200.kernel_bench --kernel select --L 32896 --text 128 --k 896
 
 Each repetition cycles through `--caches` distinct K/V caches (default: as
 many as keep the total above 256 MB, i.e. larger than the 126 MB L2), so the
@@ -20,6 +21,11 @@ adds the host cost of each call).  Prints achieved algorithmic GB/s:
           runs them (CUDA graph, one launch sequence each), with sparse
           caches of L_s = K+text+1 keys and dense caches of L keys; the weight
           bytes (14.1 GB) dominate.
+  select: the prefill-time selection of one request at the 7B shape -- per
+          layer the score chain over its P keys (select_logits, row_stats,
+          colsum; 2*T*Hq*P*D FMA flops on CUDA cores, fp16 probabilities
+          written), then one top-K over all layers' heads and the gather into
+          the sparse cache; eager, each piece timed alone.
 This is also the target command of the ncu captures summarised in profiles/.
 """
 
@@ -36,7 +42,7 @@ from .timing import graph_time_us
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["verify", "draft", "gemm", "forward"], default="verify")
+    ap.add_argument("--kernel", choices=["verify", "draft", "gemm", "forward", "select"], default="verify")
     ap.add_argument("--gamma", type=int, default=9)
     ap.add_argument("--sparse-len", type=int, default=1025)
     ap.add_argument("--only", choices=["sparse", "dense"], default=None, help="forward: time one of the two")
@@ -51,6 +57,8 @@ def main() -> None:
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--eager", action="store_true", help="time eager calls (includes host launch cost)")
+    ap.add_argument("--text", type=int, default=128, help="select: text queries after the last video token")
+    ap.add_argument("--k", type=int, default=896, help="select: visual keys kept per (layer, KV head)")
     a = ap.parse_args()
 
     dev = torch.device("cuda", 0)
@@ -59,6 +67,8 @@ def main() -> None:
         return gemm_bench(a, dev)
     if a.kernel == "forward":
         return forward_bench(a, dev)
+    if a.kernel == "select":
+        return select_bench(a, dev)
     B, L = a.B, a.L
     cap = (L + 255) // 256 * 256
     per_cache = 2 * B * 4 * cap * 128 * 2
@@ -171,6 +181,58 @@ def forward_bench(a, dev) -> None:
                weight_stream_us=wbytes / 6548.5e3)
     assert ops.device_error() == 0
     print(json.dumps(res))
+
+
+def _event_us(fn, reps: int) -> float:
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / reps
+
+
+def select_bench(a, dev) -> None:
+    """Selection of one request: 28 layers' score chains, the top-K, the gather."""
+    from .model import QWEN25_VL_7B
+
+    c = QWEN25_VL_7B
+    Lyr, Hq, Hkv, D = c.num_hidden_layers, c.num_attention_heads, c.num_key_value_heads, c.head_dim
+    P, T, K = a.L, a.text, a.k
+    V = P - T  # visual keys first, the text (queries) last
+    cap = (P + 127) // 128 * 128
+    cap_s = (T + K + 64 + 63) // 64 * 64
+    g = torch.Generator(device=dev).manual_seed(0)
+    dense = torch.randn(Lyr, 2, 1, Hkv, cap, D, generator=g, device=dev).to(torch.bfloat16)
+    sparse = torch.zeros(Lyr, 2, 1, Hkv, cap_s, D, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(Lyr, T, Hq, D, generator=g, device=dev).to(torch.bfloat16)
+    scores = torch.empty(Lyr, Hkv, P, device=dev, dtype=torch.float32)
+    visual_pos = torch.arange(V, device=dev, dtype=torch.int32)
+    non_visual = torch.arange(V, P, device=dev, dtype=torch.int32)
+    topk = torch.empty(Lyr, Hkv, K, device=dev, dtype=torch.int32)
+
+    def scores_all():
+        for li in range(Lyr):
+            ops.select_scores(q[li], dense[li, 0, 0], P, P - T, scores=scores[li], write_probs=True)
+
+    reps = max(1, a.reps // 5)
+    us_scores = _event_us(scores_all, reps)
+    us_topk = _event_us(lambda: ops.topk_select(scores.view(Lyr * Hkv, P), visual_pos, K, out=topk.view(-1, K)),
+                        a.reps)
+    us_gather = _event_us(lambda: ops.compact_gather(dense, sparse, 0, non_visual, topk), a.reps)
+    assert ops.device_error() == 0
+    flops = 2.0 * T * Hq * P * D * Lyr
+    probs_bytes = 2.0 * Hq * T * P * Lyr
+    gather_bytes = 2.0 * Lyr * 2 * Hkv * (T + K) * D * 2  # read + write of the kept rows
+    print(json.dumps({"kernel": "select", "P": P, "T": T, "K": K, "layers": Lyr,
+                      "scores_us": us_scores, "scores_tflops": flops / us_scores / 1e6,
+                      "probs_write_gbs": probs_bytes / us_scores / 1e3,
+                      "topk_us": us_topk, "topk_read_gbs": 4.0 * Lyr * Hkv * P / us_topk / 1e3,
+                      "gather_us": us_gather, "gather_gbs": gather_bytes / us_gather / 1e3,
+                      "total_ms": (us_scores + us_topk + us_gather) / 1e3}))
 
 
 if __name__ == "__main__":
