@@ -43,10 +43,12 @@ VIDEO_TOKEN_ID = 151656
 VERIFY_TRAFFIC = {(8, 32906, 10): 550.2e6}
 # sm__pipe_tensor_cycles_active (fraction of peak sustained) of the same capture
 VERIFY_TENSOR_ACTIVE = {(8, 32906, 10): 0.27}
-# DRAM read+write bytes of one sparse forward's GEMM launches at M = 8 (the
-# five shapes' per-launch ncu figures x their launches per forward); None
-# until captured for the current kernels.
-GEMM_TRAFFIC = {8: None}
+# DRAM read+write bytes of one sparse forward's gemm_kernel launches at M = 8:
+# the five shapes' per-launch `ncu --metrics dram__bytes_read.sum,
+# dram__bytes_write.sum -k regex:gemm_kernel -c 1` figures of
+# `python -m std_b200.kernel_bench --kernel gemm --M 8 --N <N> --K <K>` times
+# their launches per forward (28 x QKV, O, gate/up, down + 1 lm_head).
+GEMM_TRAFFIC = {8: 28 * (33_167_616 + 25_827_584 + 275_444_480 + 140_990_976) + 1_094_170_368}
 
 WORKLOADS = {
     "config4": dict(batch=8, visual=32768, text=128, k_plus_text=1024, gamma=9, max_new=128,
