@@ -76,6 +76,8 @@ def _args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ar", action="store_true")
+    ap.add_argument("--host-loop", action="store_true",
+                    help="one graph launch per round from the host instead of the device-side loop (for profilers)")
     return ap.parse_args()
 
 
@@ -333,8 +335,9 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     runner.capture()
 
     # ---- warmup + timed STD decode ----
+    loop = False if a.host_loop else None
     for _ in range(a.warmup):
-        runner.run_std()
+        runner.run_std(device_loop=loop)
     rounds_per_step = int(runner.stats[:, 0].max().item())
     uuid = None
     try:
@@ -348,7 +351,7 @@ def b200_arm(a, w, rank: int, world: int, local_rank: int) -> None:
     ev0.record()
     torch.cuda.nvtx.range_push("std_timed")
     for _ in range(a.steps):
-        runner.run_std()
+        runner.run_std(device_loop=loop)
     torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize()
