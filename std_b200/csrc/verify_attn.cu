@@ -10,14 +10,20 @@
 // One CTA = one (request, KV head, split of split_keys keys).  The 7 query
 // heads of the group times nq tokens form the rows of a 128-row tile
 // (row = t*7 + g, zero-padded), so each K/V byte is read once for all 7 heads:
-//   S_c  = Q K_c^T    tcgen05.mma M=128 N=128 K=128 (8 x K16), fp32 in TMEM
-//   P_c  = exp2(S_c*scale*log2e - m_row), bf16, written to smem (SW128, 2 buffers)
-//   O   += P_c V_c    tcgen05.mma into one TMEM accumulator, V MN-major
+//   S_c  = Q K_c^T    tcgen05.mma M=128 N=64 K=128 (8 x K16), fp32 in TMEM;
+//                     Q is the A operand held in TMEM (stored there once)
+//   P_c  = exp2(S_c*scale*log2e - m_row), bf16, written back into TMEM over
+//          the first half of S_c's columns
+//   O   += P_c V_c    tcgen05.mma with P as the A operand in TMEM, V MN-major
+//                     from shared memory
+// Only K and V cross shared memory: with Q and P read from shared memory as
+// well, the operand traffic (~128 KB of shared-memory bandwidth per 64-key
+// chunk) held each MMA issue to ~100 cycles and the chunk to ~1670 cycles.
 // m_row is a running row max; O is rescaled in TMEM only when a chunk raises
 // the max by more than 2^8 (lazy rescale), so the softmax threads normally
-// touch TMEM once per chunk.  Warp roles: warps 0-3 own TMEM lanes 0-127 (one
-// row per thread); warp 4 lane 0 issues TMA (2 K/V stages); warp 5 allocates
-// TMEM and lane 0 issues the MMAs.  Splits write (O, m, l) partials that a
+// touch TMEM once per chunk.  Warp roles: two softmax warpgroups (warps 0-3 and
+// 4-7, one row per thread, chunks alternating); warp 8 lane 0 issues TMA (a
+// 6-stage K/V ring); warp 9 allocates TMEM and lane 0 issues the MMAs.  Splits write (O, m, l) partials that a
 // second kernel combines; a request whose keys fit one split writes its output
 // directly.
 //
@@ -35,13 +41,14 @@ namespace stdb {
 
 constexpr int VF_D = 128;
 constexpr int VF_CHUNK = 64;       // keys per chunk (MMA N of S, K of P V)
-constexpr int VF_STAGES = 4;       // K/V ring depth
+constexpr int VF_STAGES = 6;       // K/V ring depth
 constexpr int VF_THREADS = 320;    // 2 softmax warpgroups + TMA warp + MMA warp
 constexpr int VF_G = 7;
-constexpr uint32_t VF_QTILE = 32768;  // 128 rows x 256 B (two 64-d K-blocks)
 constexpr uint32_t VF_KV = 16384;     // one K or V chunk: 64 keys x 256 B (two 8 KB d-blocks)
-constexpr uint32_t VF_PTILE = 16384;  // 128 rows x 64 keys bf16 (one K-block)
-constexpr uint32_t VF_SMEM = VF_QTILE + 2 * VF_STAGES * VF_KV + 2 * VF_PTILE + 1024;
+constexpr uint32_t VF_SMEM = 2 * VF_STAGES * VF_KV + 1024;
+// TMEM columns: S[w] (w = chunk & 1) at 64 w, with P[w] over its first 32
+// columns; O[w] at 128 + 128 w; Q (128 d as 64 bf16 pairs) at 384
+constexpr uint32_t VF_TQ = 384;
 constexpr float VF_RESCALE = 8.0f;    // log2 units
 
 struct VerifyParams {
@@ -90,10 +97,8 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + VF_QTILE;                       // [VF_STAGES][VF_KV]
+  uint8_t* sK = smem;                                  // [VF_STAGES][VF_KV]
   uint8_t* sV = sK + VF_STAGES * VF_KV;                // [VF_STAGES][VF_KV]
-  uint8_t* sP = sV + VF_STAGES * VF_KV;                // [2][VF_PTILE]
 
   __shared__ __align__(8) uint64_t bar_q, bar_kv_full[VF_STAGES], bar_kv_empty[VF_STAGES], bar_s_full[2],
       bar_s_free[2], bar_p_full[2], bar_mma_done;
@@ -121,14 +126,6 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
     fence_barrier_init();
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
-  }
-  if (warp < 4 && warp * 32 >= nrows) {
-    // P rows of the all-padding warps are never written by the softmax:
-    // zero them once so every P V tile reads defined values
-    for (int buf = 0; buf < 2; ++buf)
-      for (int c8 = 0; c8 < 8; ++c8)
-        *reinterpret_cast<uint4*>(sP + buf * VF_PTILE + sw128_offset(tid, c8)) = make_uint4(0u, 0u, 0u, 0u);
-    fence_async_smem();
   }
   tc_fence_before();
   __syncthreads();
@@ -167,7 +164,6 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
     if (lane == 0) {
       const uint32_t idS = idesc_bf16_f32(128, VF_CHUNK, 0, 0);
       const uint32_t idO = idesc_bf16_f32(128, VF_D, 0, 1);
-      const uint32_t aQ = smem_u32(sQ);
       bool ok = mbar_wait(&bar_q, 0);
       tc_fence_after();
       auto issue_S = [&](int c) -> bool {
@@ -178,10 +174,9 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         const uint32_t aK = smem_u32(sK + st * VF_KV);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t offQ = (ks >> 2) * 16384u + (ks & 3) * 32u;
           const uint32_t offK = (ks >> 2) * (VF_KV / 2) + (ks & 3) * 32u;
-          umma_bf16(tmem + w * VF_CHUNK, sdesc_sw128(aQ + offQ, 16, 1024), sdesc_sw128(aK + offK, 16, 1024), idS,
-                    ks > 0 ? 1u : 0u);
+          umma_bf16_ts(tmem + w * VF_CHUNK, tmem + VF_TQ + ks * 8, sdesc_sw128(aK + offK, 16, 1024), idS,
+                       ks > 0 ? 1u : 0u);
         }
         umma_commit(&bar_s_full[w]);
         return true;
@@ -195,11 +190,11 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t aV = smem_u32(sV + st * VF_KV), aP = smem_u32(sP + w * VF_PTILE);
+        const uint32_t aV = smem_u32(sV + st * VF_KV);
 #pragma unroll
         for (int ks = 0; ks < VF_CHUNK / 16; ++ks) {
-          umma_bf16(tmem + 128 + 128 * w, sdesc_sw128(aP + ks * 32u, 16, 1024),
-                    sdesc_sw128(aV + ks * 2048u, VF_KV / 2, 1024), idO, (c >= 2 || ks > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + 128 + 128 * w, tmem + w * VF_CHUNK + ks * 8,
+                       sdesc_sw128(aV + ks * 2048u, VF_KV / 2, 1024), idO, (c >= 2 || ks > 0) ? 1u : 0u);
         }
         umma_commit(&bar_kv_empty[st]);
         if (c + 2 < nchunks && !issue_S(c + 2)) {
@@ -215,25 +210,34 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
     const int r = tid & 127;
     const int t = r / VF_G, g = r % VF_G;
     const bool valid_row = r < nrows;
+    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     if (wg == 0) {
+      // this row's query (zero for padding rows) into the Q columns of TMEM
       const uint4* src = reinterpret_cast<const uint4*>(
           p.q + ((static_cast<size_t>(b) * p.nq + (valid_row ? t : 0)) * p.Hq + kvh * VF_G + g) * VF_D);
+      uint32_t qw[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 v = valid_row ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sQ + (c >> 3) * 16384u + sw128_offset(r, c & 7)) = v;
+      for (int half = 0; half < 2; ++half) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = valid_row ? src[half * 8 + c] : make_uint4(0, 0, 0, 0);
+          qw[4 * c] = v.x;
+          qw[4 * c + 1] = v.y;
+          qw[4 * c + 2] = v.z;
+          qw[4 * c + 3] = v.w;
+        }
+        tmem_st32(trow + VF_TQ + half * 32, qw);
       }
-      fence_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(&bar_q);
     }
     const int limit = min(p.causal ? (L - p.nq + t) : (L - 1), k1 - 1);  // last visible key
-    const uint32_t trow = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t tO = trow + 128 + 128 * wg;
     const float sc = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     uint32_t s[VF_CHUNK];
-    uint8_t* P = sP + wg * VF_PTILE;
     // a warp whose 32 rows are all padding (rows >= 7*nq) skips the softmax
     const bool live = (warp & 3) * 32 < nrows;
 
@@ -279,22 +283,18 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
       if (m_run == -INFINITY) m_run = m_c;
       const float nm = -m_run;
       const bool any = m_run != -INFINITY;
+      // P as bf16 pairs (keys j, j+1 in column j/2) over S's first 32 columns
+      uint32_t pk[VF_CHUNK / 2];
 #pragma unroll
-      for (int piece = 0; piece < VF_CHUNK / 16; ++piece) {  // 16 keys = 2 x 16 B
-        uint32_t pk[8];
-#pragma unroll
-        for (int q2 = 0; q2 < 8; ++q2) {
-          const int j = piece * 16 + 2 * q2;
-          float e0 = (any && j < nvis) ? ex2_approx(fmaf(__uint_as_float(s[j]), sc, nm)) : 0.f;
-          float e1 = (any && j + 1 < nvis) ? ex2_approx(fmaf(__uint_as_float(s[j + 1]), sc, nm)) : 0.f;
-          l_run += e0 + e1;
-          pk[q2] = pack_bf16x2(e0, e1);
-        }
-        *reinterpret_cast<uint4*>(P + sw128_offset(r, 2 * piece)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(P + sw128_offset(r, 2 * piece + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      for (int j = 0; j < VF_CHUNK; j += 2) {
+        float e0 = (any && j < nvis) ? ex2_approx(fmaf(__uint_as_float(s[j]), sc, nm)) : 0.f;
+        float e1 = (any && j + 1 < nvis) ? ex2_approx(fmaf(__uint_as_float(s[j + 1]), sc, nm)) : 0.f;
+        l_run += e0 + e1;
+        pk[j / 2] = pack_bf16x2(e0, e1);
       }
+      tmem_st32(trow + wg * VF_CHUNK, pk);
+      tmem_wait_st();
       tc_fence_before();
-      fence_async_smem();
       mbar_arrive(&bar_p_full[wg]);
     }
     // ---- combine the two accumulators (row-local), write output or partial ----
