@@ -12,22 +12,25 @@
 // (row = t*7 + g, zero-padded), so each K/V byte is read once for all 7 heads:
 //   S_c  = Q K_c^T    tcgen05.mma M=128 N=64 K=128 (8 x K16), fp32 in TMEM;
 //                     Q is the A operand held in TMEM (stored there once)
-//   P_c  = exp2(S_c*scale*log2e - m_row), bf16, written back into TMEM over
-//          the first half of S_c's columns
+//   P_c  = exp2(S_c*scale*log2e - m_row), bf16, written into TMEM
 //   O   += P_c V_c    tcgen05.mma with P as the A operand in TMEM, V MN-major
 //                     from shared memory
-// Only K and V cross shared memory: with Q and P read from shared memory as
-// well, the operand traffic (~128 KB of shared-memory bandwidth per 64-key
-// chunk) held each MMA issue to ~100 cycles and the chunk to ~1670 cycles.
+// Only K and V cross shared memory.  Two threads issue the MMAs: one the S
+// MMAs, one the P.V MMAs (P has its own TMEM columns, so the chains share no
+// operand).  A tcgen05.mma costs its issuing thread ~100 cycles; from one
+// thread the 12 MMAs of a 64-key chunk and the wait for P serialised into
+// ~1670 cycles per chunk.  The softmax waits for P_{c-2} V_{c-2} (its
+// group's previous P.V) before it rescales O or rewrites P.
 // m_row is a running row max; O is rescaled in TMEM only when a chunk raises
 // the max by more than 2^8 (lazy rescale), so the softmax threads normally
 // touch TMEM once per chunk.  Warp roles: two softmax warpgroups (warps 0-3 and
 // 4-7, one row per thread, chunks alternating); warp 8 lane 0 issues TMA (a
-// 6-stage K/V ring); warp 9 allocates TMEM and lane 0 issues the MMAs.  Splits write (O, m, l) partials that a
+// 6-stage K/V ring); warp 9 allocates TMEM and lane 0 issues the S MMAs;
+// warp 10 lane 0 issues the P.V MMAs.  Splits write (O, m, l) partials that a
 // second kernel combines; a request whose keys fit one split writes its output
 // directly.
 //
-// Row invariance.  Chunk boundaries (128 keys) and split boundaries
+// Row invariance.  Chunk boundaries (64 keys) and split boundaries
 // (split_keys, a function of the cache shape only) sit at fixed absolute key
 // positions, and every per-row decision (running max, rescale, masking) uses
 // only that row's scores; fully masked chunks and splits contribute exact
@@ -42,13 +45,14 @@ namespace stdb {
 constexpr int VF_D = 128;
 constexpr int VF_CHUNK = 64;       // keys per chunk (MMA N of S, K of P V)
 constexpr int VF_STAGES = 6;       // K/V ring depth
-constexpr int VF_THREADS = 320;    // 2 softmax warpgroups + TMA warp + MMA warp
+constexpr int VF_THREADS = 352;    // 2 softmax warpgroups + TMA warp + S-MMA warp + PV-MMA warp
 constexpr int VF_G = 7;
 constexpr uint32_t VF_KV = 16384;     // one K or V chunk: 64 keys x 256 B (two 8 KB d-blocks)
 constexpr uint32_t VF_SMEM = 2 * VF_STAGES * VF_KV + 1024;
-// TMEM columns: S[w] (w = chunk & 1) at 64 w, with P[w] over its first 32
-// columns; O[w] at 128 + 128 w; Q (128 d as 64 bf16 pairs) at 384
+// TMEM columns (all 512): S[w] (w = chunk & 1) at 64 w; O[w] at 128 + 128 w;
+// Q (128 d as 64 bf16 pairs) at 384; P[w] (64 keys as 32 bf16 pairs) at 448 + 32 w
 constexpr uint32_t VF_TQ = 384;
+constexpr uint32_t VF_TP = 448;
 constexpr float VF_RESCALE = 8.0f;    // log2 units
 
 struct VerifyParams {
@@ -101,7 +105,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
   uint8_t* sV = sK + VF_STAGES * VF_KV;                // [VF_STAGES][VF_KV]
 
   __shared__ __align__(8) uint64_t bar_q, bar_kv_full[VF_STAGES], bar_kv_empty[VF_STAGES], bar_s_full[2],
-      bar_s_free[2], bar_p_full[2], bar_mma_done;
+      bar_s_free[2], bar_p_full[2], bar_pv_done[2], bar_mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ float s_mB[128], s_lB[128];
 
@@ -121,6 +125,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
       mbar_init(&bar_s_full[i], 1);
       mbar_init(&bar_s_free[i], live_threads);
       mbar_init(&bar_p_full[i], live_threads);
+      mbar_init(&bar_pv_done[i], 1);
     }
     mbar_init(&bar_mma_done, 1);
     fence_barrier_init();
@@ -160,16 +165,16 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         mbar_wait(&bar_kv_full[c % VF_STAGES], (c / VF_STAGES) & 1);
     }
   } else if (warp == 9) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- S issuer: S_c = Q K_c^T into S[c & 1] ----------------
     if (lane == 0) {
       const uint32_t idS = idesc_bf16_f32(128, VF_CHUNK, 0, 0);
-      const uint32_t idO = idesc_bf16_f32(128, VF_D, 0, 1);
       bool ok = mbar_wait(&bar_q, 0);
       tc_fence_after();
-      auto issue_S = [&](int c) -> bool {
+      for (int c = 0; ok && c < nchunks; ++c) {
         const int st = c % VF_STAGES, w = c & 1;
-        if (!mbar_wait(&bar_kv_full[st], (c / VF_STAGES) & 1)) return false;
-        if (c >= 2 && !mbar_wait(&bar_s_free[w], ((c >> 1) - 1) & 1)) return false;
+        // K_c landed; S[w] read by the softmax of chunk c - 2
+        if (!mbar_wait(&bar_kv_full[st], (c / VF_STAGES) & 1)) break;
+        if (c >= 2 && !mbar_wait(&bar_s_free[w], ((c >> 1) - 1) & 1)) break;
         tc_fence_after();
         const uint32_t aK = smem_u32(sK + st * VF_KV);
 #pragma unroll
@@ -179,29 +184,27 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
                        ks > 0 ? 1u : 0u);
         }
         umma_commit(&bar_s_full[w]);
-        return true;
-      };
-      if (ok) ok = issue_S(0);
-      if (ok && nchunks > 1) ok = issue_S(1);
-      for (int c = 0; ok && c < nchunks; ++c) {
-        const int w = c & 1, st = c % VF_STAGES;
-        if (!mbar_wait(&bar_p_full[w], (c >> 1) & 1)) {
-          ok = false;
-          break;
-        }
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------- P.V issuer: O[c & 1] += P_c V_c ----------------
+    if (lane == 0) {
+      const uint32_t idO = idesc_bf16_f32(128, VF_D, 0, 1);
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % VF_STAGES, w = c & 1;
+        if (!mbar_wait(&bar_p_full[w], (c >> 1) & 1)) break;
         tc_fence_after();
         const uint32_t aV = smem_u32(sV + st * VF_KV);
 #pragma unroll
         for (int ks = 0; ks < VF_CHUNK / 16; ++ks) {
-          umma_bf16_ts(tmem + 128 + 128 * w, tmem + w * VF_CHUNK + ks * 8,
+          umma_bf16_ts(tmem + 128 + 128 * w, tmem + VF_TP + w * 32 + ks * 8,
                        sdesc_sw128(aV + ks * 2048u, VF_KV / 2, 1024), idO, (c >= 2 || ks > 0) ? 1u : 0u);
         }
+        // S_c retired before P_c existed, so both halves of the stage are free
         umma_commit(&bar_kv_empty[st]);
-        if (c + 2 < nchunks && !issue_S(c + 2)) {
-          ok = false;
-          break;
-        }
+        umma_commit(&bar_pv_done[w]);
       }
+      // the last P V retires after every S (each P needs its S)
       umma_commit(&bar_mma_done);
     }
   } else {
@@ -228,6 +231,13 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         }
         tmem_st32(trow + VF_TQ + half * 32, qw);
       }
+      if (warp * 32 >= nrows) {
+        // an all-padding warp never writes P: zero its rows of both P buffers
+#pragma unroll
+        for (int j = 0; j < 32; ++j) qw[j] = 0u;
+        tmem_st32(trow + VF_TP, qw);
+        tmem_st32(trow + VF_TP + 32, qw);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_q);
@@ -243,7 +253,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
 
     for (int c = wg; live && c < nchunks; c += 2) {
       const int kk = c >> 1;
-      if (ok) ok = mbar_wait(&bar_s_full[wg], kk & 1);  // also: O[wg] and P[wg] no longer in use
+      if (ok) ok = mbar_wait(&bar_s_full[wg], kk & 1);  // S_c in TMEM
       __syncwarp();
       tc_fence_after();
       tmem_ld32(trow + wg * VF_CHUNK, s);
@@ -262,6 +272,10 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
           if (j < nvis) mraw = fmaxf(mraw, __uint_as_float(s[j]));
       }
       const float m_c = mraw * sc;  // scale > 0: max commutes with the scaling
+      // O[wg] and P[wg] are free once this group's previous P V has retired
+      if (c >= 2 && ok) ok = mbar_wait(&bar_pv_done[wg], ((c >> 1) - 1) & 1);
+      __syncwarp();
+      tc_fence_after();
       const bool need = (m_run != -INFINITY) && (m_c > m_run + VF_RESCALE);
       if (__any_sync(0xffffffffu, need)) {
         const float alpha = need ? exp2f(m_run - m_c) : 1.0f;
@@ -292,7 +306,7 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
         l_run += e0 + e1;
         pk[j / 2] = pack_bf16x2(e0, e1);
       }
-      tmem_st32(trow + wg * VF_CHUNK, pk);
+      tmem_st32(trow + VF_TP + wg * 32, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p_full[wg]);
