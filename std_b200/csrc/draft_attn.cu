@@ -19,8 +19,8 @@
 // the MMAs and registers).
 //
 //   grid = (DR_CLUSTER, Hkv, B), cluster = (DR_CLUSTER, 1, 1), 8 warps/CTA.
-//   CTA rank i owns keys [i*per, (i+1)*per) of the request's live length
-//   (per = ceil(L/8) rounded up to 16).  TMA (2-D tensor maps, 128-byte
+//   CTA rank i owns keys [i*per, (i+1)*per) of the request's live length,
+//   the last rank also the remainder (per a multiple of 16, draft_split).  TMA (2-D tensor maps, 128-byte
 //   swizzle, no multicast; 64-row boxes for a full sub-tile, 16-row boxes for
 //   a partial one) streams its K and V rows through a three-stage ring of
 //   64-key sub-tiles; only rows of boxes that hold live keys are fetched.  The
@@ -230,6 +230,18 @@ struct DraftRecv {
   uint64_t bar;
 };
 
+// Keys [k0, k1) of cluster rank `rank`: shares of `per` keys, a multiple of
+// 16 (the TMA box height), the last rank also taking the remainder; `per` is
+// floor(L/8) rounded down or up to 16, whichever gives the smaller largest
+// share (L = 1025: 7 x 128 + 129 rather than 7 x 144 + 17).
+STD_DEV void draft_split(int L, int rank, int& k0, int& k1) {
+  const int dn = (L / DR_CLUSTER) & ~15, up = dn + 16;
+  const int load_dn = dn > 0 ? max(dn, L - (DR_CLUSTER - 1) * dn) : L;
+  const int per = (dn > 0 && load_dn <= up) ? dn : up;
+  k0 = min(L, rank * per);
+  k1 = rank == DR_CLUSTER - 1 ? L : min(L, k0 + per);
+}
+
 // heads whose 128 outputs overlap output slice q ([112 q, 112 q + 112))
 STD_DEV int draft_slice_head0(int q) { return (q * DR_OUT_PER_RANK) / DR_D; }
 STD_DEV int draft_slice_head1(int q) { return (q * DR_OUT_PER_RANK + DR_OUT_PER_RANK - 1) / DR_D; }
@@ -397,10 +409,8 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     if (rank == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
     L = L < 0 ? 0 : p.cap;
   }
-  int per = (L + DR_CLUSTER - 1) / DR_CLUSTER;
-  per = (per + 15) & ~15;
-  const int k0 = min(L, rank * per);
-  const int k1 = min(L, k0 + per);
+  int k0, k1;
+  draft_split(L, rank, k0, k1);
   const int nkeys = k1 - k0;
   const int nsub = (nkeys + DR_SUB - 1) / DR_SUB;
   const int row0 = (b * p.Hkv + kvh) * p.cap + k0;  // first tensor-map row of this CTA
@@ -584,10 +594,8 @@ __global__ void __cluster_dims__(DR_CLUSTER, 1, 1) __launch_bounds__(DR_THREADS,
     if (rank == 0 && tid == 0) std_set_error(STD_DEVERR_LENGTH);
     L = L < 0 ? 0 : p.cap;
   }
-  int per = (L + DR_CLUSTER - 1) / DR_CLUSTER;
-  per = (per + 15) & ~15;
-  const int k0 = min(L, rank * per);
-  const int k1 = min(L, k0 + per);
+  int k0, k1;
+  draft_split(L, rank, k0, k1);
   const int nkeys = k1 - k0;
   const int nsub = (nkeys + DR_SUB - 1) / DR_SUB;
   const size_t head = static_cast<size_t>(b) * p.Hkv + kvh;
