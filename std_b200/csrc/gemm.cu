@@ -251,15 +251,17 @@ __global__ void gemm_reduce_kernel(const float* __restrict__ partial, int splits
   const size_t total = static_cast<size_t>(M) * N / 4;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    float4 a = reinterpret_cast<const float4*>(partial)[i];
-    for (int s0 = 1; s0 < splits; s0 += GM_SUM_BATCH) {  // batched loads, adds in split order
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < splits; s0 += GM_SUM_BATCH) {  // batched loads, adds in split order
       float4 b[GM_SUM_BATCH];
 #pragma unroll
       for (int j = 0; j < GM_SUM_BATCH; ++j)
         if (s0 + j < splits) b[j] = reinterpret_cast<const float4*>(partial + static_cast<size_t>(s0 + j) * M * N)[i];
 #pragma unroll
       for (int j = 0; j < GM_SUM_BATCH; ++j) {
-        if (s0 + j < splits) {
+        if (s0 + j == 0) {
+          a = b[0];
+        } else if (s0 + j < splits) {
           a.x += b[j].x;
           a.y += b[j].y;
           a.z += b[j].z;
@@ -299,12 +301,11 @@ struct GemmOut {
     }
     const size_t off = row * N + col;
     const size_t MN = static_cast<size_t>(M) * N;
-    float4 a = __ldcg(reinterpret_cast<const float4*>(partial + off));
-    float4 b = __ldcg(reinterpret_cast<const float4*>(partial + off + 4));
-    // splits 1.. in batches of GM_SUM_BATCH: every load of a batch is issued
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    // the splits in batches of GM_SUM_BATCH: every load of a batch is issued
     // before the first add (one L2 latency per batch), then the adds run in
     // split order, so the sum is the same as a one-at-a-time loop
-    for (int s0 = 1; s0 < splits; s0 += GM_SUM_BATCH) {
+    for (int s0 = 0; s0 < splits; s0 += GM_SUM_BATCH) {
       float4 c[GM_SUM_BATCH], d[GM_SUM_BATCH];
 #pragma unroll
       for (int j = 0; j < GM_SUM_BATCH; ++j) {
@@ -316,7 +317,10 @@ struct GemmOut {
       }
 #pragma unroll
       for (int j = 0; j < GM_SUM_BATCH; ++j) {
-        if (s0 + j < splits) {
+        if (s0 + j == 0) {
+          a = c[0];
+          b = d[0];
+        } else if (s0 + j < splits) {
           a.x += c[j].x;
           a.y += c[j].y;
           a.z += c[j].z;
