@@ -314,11 +314,11 @@ def prefill_segment(model: Qwen25VLDecoder, cache: torch.Tensor, b: int, x: torc
             if selection.get("observe") is not None:  # (layer, post-RoPE text queries, K rows, keys, first query pos)
                 selection["observe"](li, q, cache[li, 0, b], L, start)
             G = Hq // Hkv
-            attn = torch.empty(S, Hq, D, device=dev, dtype=model.dtype)
-            for kv in range(Hkv):
-                pr = probs[kv * G:(kv + 1) * G].float()  # [G, S, L]
-                o = pr @ v_all[kv].float()                 # [G, S, D]
-                attn[:, kv * G:(kv + 1) * G] = o.permute(1, 0, 2).to(model.dtype)
+            # probs [Hq, S, L] fp16 @ V [Hkv, L, D] in fp32: one batched matmul
+            # over the KV groups (the G heads of a group share its V)
+            pr = probs.float().reshape(Hkv, G * S, L)
+            o = torch.bmm(pr, v_all.float())                 # [Hkv, G*S, D]
+            attn = o.view(Hq, S, D).permute(1, 0, 2).to(model.dtype).contiguous()
         elif start == 0:
             attn = _sdpa(q, k_all, v_all, causal=True, mask=None)
         else:
