@@ -551,6 +551,7 @@ def b200_sharded_arm(a, w, rank: int, world: int, local_rank: int) -> None:
                             dtype=torch.bfloat16, device=dev)
         ex.distribute(None, local, P)
         ex.serve(local, c.num_hidden_layers)
+        ex.release()
     else:
         model = Qwen25VLDecoder(c, seed=2, device=str(dev))
         ids = torch.full((B, P), VIDEO_TOKEN_ID, dtype=torch.int64)
@@ -593,6 +594,8 @@ def b200_sharded_arm(a, w, rank: int, world: int, local_rank: int) -> None:
             extra["token_exact_vs_ar"] = bool(torch.equal(std_tokens, runner.out_tokens))
         extra["device_error"] = ops.device_error()
         ex.close()
+        ex.release()
+        extra["exchange"] = ex.transport
     t = torch.tensor([t_local, tokens_local], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     if rank == plan.owner:

@@ -240,6 +240,36 @@ int std_gemm_rope_append(const void* x, const void* w, const void* bias, int K, 
                          const void* cos_t, const void* sin_t, int max_pos, void* q_out, void* k_cache,
                          void* v_cache, int cap, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- (e) sequence-sharded verify over peer memory (one node) ---------- */
+
+/* No reference counterpart (the reference has no sequence parallelism): the
+ * exchange of the sequence-sharded verify without collectives.  Buffers that
+ * another rank maps come from std_device_alloc (zero-filled cudaMalloc, so
+ * their base can be exported); std_ipc_handle writes the allocation's
+ * std_ipc_handle_bytes()-byte handle, std_ipc_open maps a peer's handle
+ * (peer access enabled lazily), std_ipc_close unmaps it.  Every rank must be
+ * a process on its own GPU of the same node. */
+size_t std_ipc_handle_bytes(void);
+int std_device_alloc(size_t bytes, void** ptr_out);
+int std_device_free(void* ptr);
+int std_ipc_handle(const void* base, void* handle_out);
+int std_ipc_open(const void* handle, void** ptr_out);
+int std_ipc_close(void* ptr);
+/* Copy `bytes` (multiple of 16, may be 0) from src to dst on this GPU, then
+ * publish epoch e = ++*counter (a device int of this rank) to each of the
+ * n_flags <= 8 device ints `flags` (typically peers' flags) with system-scope
+ * release stores, after the copy. */
+int std_p2p_post(const void* src, void* dst, size_t bytes, const unsigned long long* flags, int n_flags,
+                 int* counter, void* stream);
+/* Wait until flags[0..n_flags) (device ints of this rank that peers post to)
+ * all reach e = *counter + 1, then advance *counter.  Gives up after about
+ * one second: std_get_device_error then reports a wait timeout. */
+int std_p2p_wait(const int* flags, int n_flags, int* counter, void* stream);
+/* std_merge_partials_f32 with part i at parts[i] (n_parts <= 8 pointers, on
+ * any GPU of the node): the same arithmetic, byte-identical results. */
+int std_merge_partials_f32_list(const unsigned long long* parts, int n_parts, int rows, int D, void* out,
+                                float* lse_out, void* stream);
+
 /* ---- (f) verification-guided re-selection: the collector ------------- */
 
 /* Replaces: RuntimeVerificationCollector._hook (dynamic_selection.py:290-308).

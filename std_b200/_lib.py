@@ -38,6 +38,15 @@ SIGNATURES: Dict[str, tuple] = {
     "std_merge_partials": (I, [P, PF, I, I, I, P, PF, P]),
     "std_verify_attn_partial": (I, [P, P, P, PI32, I, I, I, I, I, I, I, I, PF, PF, P, SZ, P]),
     "std_merge_partials_f32": (I, [PF, I64, I, I, I, P, PF, P]),
+    "std_ipc_handle_bytes": (SZ, []),
+    "std_device_alloc": (I, [SZ, P]),
+    "std_device_free": (I, [P]),
+    "std_ipc_handle": (I, [P, P]),
+    "std_ipc_open": (I, [P, P]),
+    "std_ipc_close": (I, [P]),
+    "std_p2p_post": (I, [P, P, SZ, P, I, P, P]),
+    "std_p2p_wait": (I, [P, I, P, P]),
+    "std_merge_partials_f32_list": (I, [P, I, I, I, P, PF, P]),
     "std_select_workspace_bytes": (SZ, [I, I, I]),
     "std_select_scores": (I, [P, P, I64, I, I, I, I, I, I, F, PF, I, P, SZ, P]),
     "std_select_probs_view": (I, [I, I, I, P]),

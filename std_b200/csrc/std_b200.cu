@@ -9,6 +9,7 @@
 #include "decode_ops.cu"
 #include "draft_attn.cu"
 #include "merge.cu"
+#include "p2p.cu"
 #include "select.cu"
 #include "verify_attn.cu"
 #include "gemm.cu"

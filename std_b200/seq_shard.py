@@ -23,12 +23,31 @@ boundaries -- identical for a token verified in a block and the same token
 decoded alone, which keeps STD == AR.
 
 Each forward starts with a 2-int header broadcast ([1, nq]); [0, 0] ends the
-servers' loop.  The collectives run on NCCL over NVLink (gloo on CPU for the
-protocol tests); every rank issues them in the same order.
+servers' loop.
+
+Two transports carry the per-layer exchange:
+
+  "p2p" (GPUs of one node, the default on CUDA): no collective inside a
+      forward.  The ranks map each other's exported buffers with CUDA IPC
+      (std_b200/csrc/p2p.cu): the owner copies the layer's queries into its
+      exported query buffer and posts an epoch flag to every server; a server
+      waits for it, runs the verify kernel on the queries read straight from
+      the owner's memory over NVLink, writing its fp32 partial into its own
+      exported buffer, and posts its flag; the owner waits for every server
+      and merges with a kernel that reads each partial from its server's
+      memory.  Waits are bounded (about a second).  The owner's layer steps
+      are kernels and copies only, so its dense forward can be captured in a
+      CUDA graph: begin() announces a forward only outside capture, and a
+      caller replaying such a graph calls announce(nq) first.
+  "collective" (any backend; gloo on CPU for the protocol tests): the owner
+      broadcasts the queries, every rank computes its partial into one packed
+      buffer [O | LSE], and one all-gather moves them; every rank issues the
+      collectives in the same order.
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable, Optional
 
@@ -79,26 +98,110 @@ def _merge(parts, rows, D, out):
 
 
 class ShardExchange:
-    """Buffers and collective steps shared by the owner and the shard servers.
+    """Buffers and exchange steps shared by the owner and the shard servers.
 
     partial_fn / merge_fn default to the CUDA kernels; the CPU protocol tests
-    pass torch stand-ins and run over gloo."""
+    pass torch stand-ins and run over gloo with the collective transport."""
 
     def __init__(self, plan: ShardPlan, rank: int, B: int, Hq: int, D: int, max_nq: int, device,
-                 group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None):
+                 group=None, partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
+                 transport: Optional[str] = None):
         self.plan, self.rank, self.group = plan, rank, group
         self.B, self.Hq, self.D, self.max_nq = B, Hq, D, max_nq
         self.device = torch.device(device)
         self.partial_fn = partial_fn or _verify_partial
         self.merge_fn = merge_fn or _merge
+        if transport is None:
+            transport = "p2p" if self.device.type == "cuda" and partial_fn is None and merge_fn is None \
+                else "collective"
+        if transport not in ("p2p", "collective"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
         N = plan.world
         rows = B * max_nq * Hq
+        self.hdr = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.is_owner = rank == plan.owner
+        if transport == "p2p":
+            self._p2p_setup(rows)
+            return
         self.q = torch.zeros(rows * D, dtype=torch.bfloat16, device=self.device)
         # packed fp32 partial of this rank, [rows * D O | rows LSE], and all ranks'
         self.part = torch.zeros(rows * (D + 1), dtype=torch.float32, device=self.device)
         self.parts = torch.zeros(N * rows * (D + 1), dtype=torch.float32, device=self.device)
-        self.hdr = torch.zeros(2, dtype=torch.int32, device=self.device)
-        self.is_owner = rank == plan.owner
+
+    # ------------------------------------------------------------ p2p set-up
+    def _p2p_setup(self, rows: int) -> None:
+        """Export this rank's buffers, map the peers' (one GPU per rank, one node)."""
+        from . import _lib
+
+        N, D = self.plan.world, self.D
+        if N > 8:
+            raise ValueError("the p2p transport takes at most 8 ranks")
+        ids = [None] * N
+        dist.all_gather_object(ids, str(torch.cuda.get_device_properties(self.device).uuid), group=self.group)
+        if len(set(ids)) != N:
+            raise RuntimeError("the p2p transport needs every rank on its own GPU of one node")
+        hb = int(_lib.query("std_ipc_handle_bytes"))
+
+        def alloc(nbytes: int) -> int:
+            ptr = ctypes.c_void_p(0)
+            _lib.call("std_device_alloc", int(nbytes), ctypes.byref(ptr))
+            self._allocs.append(ptr.value)
+            return ptr.value
+
+        def export(ptr: int) -> bytes:
+            buf = ctypes.create_string_buffer(hb)
+            _lib.call("std_ipc_handle", ptr, buf)
+            return buf.raw
+
+        def open_peer(handle: bytes) -> int:
+            ptr = ctypes.c_void_p(0)
+            _lib.call("std_ipc_open", ctypes.create_string_buffer(handle, hb), ctypes.byref(ptr))
+            self._opened.append(ptr.value)
+            return ptr.value
+
+        self._allocs, self._opened = [], []
+        with torch.cuda.device(self.device):
+            self._ctr = alloc(16)  # [query epoch, partial epoch] of this rank
+            if self.is_owner:
+                self._q_ipc = alloc(rows * D * 2)        # the layer's queries, read by the servers
+                self._pflags = alloc(4 * max(1, N - 1))  # slot r: server r's partial epoch
+                exports = (export(self._q_ipc), export(self._pflags))
+            else:
+                self._part_ipc = alloc(rows * (D + 1) * 4)  # this server's [O | LSE] partial, read by the owner
+                self._qflag = alloc(16)                     # the owner's query epoch
+                exports = (export(self._part_ipc), export(self._qflag))
+            every = [None] * N
+            dist.all_gather_object(every, exports, group=self.group)
+            if self.is_owner:
+                servers = range(self.plan.owner)
+                self._peer_parts = [open_peer(every[r][0]) for r in servers]
+                self._peer_qflags = [open_peer(every[r][1]) for r in servers]
+                self._own_part = torch.zeros(rows * (D + 1), dtype=torch.float32, device=self.device)
+            else:
+                self._peer_q = open_peer(every[self.plan.owner][0])
+                self._peer_pflag = open_peer(every[self.plan.owner][1]) + 4 * self.rank
+            self.q = None
+        dist.barrier(group=self.group)
+
+    def release(self) -> None:
+        """Unmap the peers' buffers and free this rank's exported ones (p2p);
+        every rank calls it after the servers' loop has ended."""
+        if self.transport != "p2p":
+            return
+        from . import _lib
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                _lib.call("std_ipc_close", ptr)
+            self._opened = []
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for ptr in self._allocs:
+                _lib.call("std_device_free", ptr)
+            self._allocs = []
 
     # ------------------------------------------------------------ collectives
     def _bcast(self, t: torch.Tensor) -> None:
@@ -125,16 +228,51 @@ class ShardExchange:
             self.merge_fn(parts.view(N, n), rows, D, out4.view(rows, D))
 
     # ------------------------------------------------------------ owner side
-    def begin(self, nq: int) -> None:
-        """Owner: announce a dense forward of nq tokens per request."""
+    @property
+    def capturable(self) -> bool:
+        """The owner's dense forward can be captured in a CUDA graph (p2p)."""
+        return self.transport == "p2p"
+
+    def announce(self, nq: int) -> None:
+        """Owner: tell the servers that a dense forward of nq tokens per request follows."""
         if not 1 <= nq <= self.max_nq:
             raise ValueError(f"nq={nq} outside [1, {self.max_nq}]")
         self.hdr.copy_(torch.tensor([1, nq], dtype=torch.int32))
         self._bcast(self.hdr)
 
+    def begin(self, nq: int) -> None:
+        """Owner: announce a dense forward of nq tokens per request (the start
+        of decode_forward).  Under graph capture (p2p) nothing is sent: the
+        caller announces before each replay."""
+        if self.capturable and self.device.type == "cuda" and torch.cuda.is_current_stream_capturing():
+            if not 1 <= nq <= self.max_nq:
+                raise ValueError(f"nq={nq} outside [1, {self.max_nq}]")
+            return
+        self.announce(nq)
+
     def attend(self, li: int, q4: torch.Tensor, kc, vc, lens, len_offset: int, out4: torch.Tensor) -> None:
         """Owner: one layer's dense attention over all shards into out4 [B, nq, Hq, D]."""
+        if self.transport == "p2p":
+            self._attend_p2p(q4.contiguous(), kc, vc, lens, len_offset, out4)
+            return
         self._exchange(q4.shape[1], q4.contiguous(), kc, vc, lens, len_offset, True, out4)
+
+    def _attend_p2p(self, q4: torch.Tensor, kc, vc, lens, len_offset: int, out4: torch.Tensor) -> None:
+        from . import _lib
+
+        B, nq, Hq, D = q4.shape
+        rows = B * nq * Hq
+        N = self.plan.world
+        s = torch.cuda.current_stream().cuda_stream
+        # queries -> the exported buffer, then epoch -> every server
+        flags = (ctypes.c_ulonglong * (N - 1))(*self._peer_qflags)
+        _lib.call("std_p2p_post", q4.data_ptr(), self._q_ipc, rows * D * 2, flags, N - 1, self._ctr, s)
+        part = self._own_part[: rows * (D + 1)]
+        self.partial_fn(q4, kc, vc, lens, len_offset, True, part[: rows * D].view(B, nq, Hq, D),
+                        part[rows * D:].view(B, nq, Hq))
+        _lib.call("std_p2p_wait", self._pflags, N - 1, self._ctr + 4, s)
+        parts = (ctypes.c_ulonglong * N)(*self._peer_parts, part.data_ptr())  # rank order: servers, then owner
+        _lib.call("std_merge_partials_f32_list", parts, N, rows, D, out4.data_ptr(), None, s)
 
     def close(self) -> None:
         """Owner: end the servers' loop."""
@@ -154,10 +292,31 @@ class ShardExchange:
             op, nq = (int(v) for v in self.hdr.tolist())
             if op == 0:
                 return served
-            q4 = self.q[: self.B * nq * self.Hq * self.D].view(self.B, nq, self.Hq, self.D)
-            for li in range(n_layers):
-                self._exchange(nq, q4, cache[li, 0], cache[li, 1], lens, 0, False, None)
+            if self.transport == "p2p":
+                for li in range(n_layers):
+                    self._serve_layer_p2p(nq, cache[li, 0], cache[li, 1], lens)
+            else:
+                q4 = self.q[: self.B * nq * self.Hq * self.D].view(self.B, nq, self.Hq, self.D)
+                for li in range(n_layers):
+                    self._exchange(nq, q4, cache[li, 0], cache[li, 1], lens, 0, False, None)
             served += 1
+
+    def _serve_layer_p2p(self, nq: int, kc: torch.Tensor, vc: torch.Tensor, lens: torch.Tensor) -> None:
+        """Wait for the owner's queries, compute this key range's partial from
+        them (read in the owner's memory) into the exported buffer, post it."""
+        from . import _lib, ops
+
+        B, Hq, D = self.B, self.Hq, self.D
+        _, Hkv, cap, _ = kc.shape
+        rows = B * nq * Hq
+        s = torch.cuda.current_stream().cuda_stream
+        _lib.call("std_p2p_wait", self._qflag, 1, self._ctr, s)
+        nb = _lib.query("std_verify_attn_workspace_bytes", B, Hkv, cap)
+        ws = ops.workspace("verify", nb, self.device)
+        _lib.call("std_verify_attn_partial", self._peer_q, kc.data_ptr(), vc.data_ptr(), lens.data_ptr(), 0, nq, 0,
+                  B, Hq, Hkv, D, cap, self._part_ipc, self._part_ipc + rows * D * 4, ws.data_ptr(), ws.numel(), s)
+        flags = (ctypes.c_ulonglong * 1)(self._peer_pflag)
+        _lib.call("std_p2p_post", None, None, 0, flags, 1, self._ctr + 4, s)
 
     # ------------------------------------------------------------ prefill
     def distribute(self, full: Optional[torch.Tensor], local: torch.Tensor, filled: int) -> None:

@@ -628,7 +628,7 @@ class STDRunner:
         if self.policy_active and self._if_stream is None:
             self._if_stream = _lib_capture_stream("if_body")
         want_std, want_ar = mode in ("std", "all"), mode in ("ar", "all")
-        if self.shard is not None:
+        if self.shard is not None and not self._shard_rounds_captured():
             # collectives stay outside the graphs: the dense forwards (verify,
             # AR steps) run eagerly between captured local phases
             steps = [("drafts", self._drafts), ("post_first", lambda: self._post(0)), ("post", lambda: self._post(1))]
@@ -792,7 +792,7 @@ class STDRunner:
         start.record()
         steps = 0
         while True:
-            self._replay_or_run("ar", self.ar_step)
+            self._replay_or_run("ar", self.ar_step, 1)
             steps += 1
             if steps >= self.max_new:
                 if self._all_done():
@@ -888,19 +888,33 @@ class STDRunner:
         """Selection updates run after rounds round_id % interval == 0 (one-based)."""
         return self.dynamic and round_id % self.update_interval == 0
 
+    def _shard_rounds_captured(self) -> bool:
+        """A sequence-sharded owner whose exchange runs over peer memory
+        (kernels only) captures whole rounds and AR steps like an unsharded
+        runner, announcing each replay's one dense forward to the shard
+        servers first.  Rounds whose number of dense forwards is decided on
+        the device (policy re-verifies) or that run several (sequential
+        verify) keep the eager dense forwards."""
+        return (self.shard is not None and self.shard.capturable and self.verify_mode == "parallel"
+                and not self.policy_active and not self.dynamic)
+
     def _round(self, first: bool, update: bool = False) -> None:
-        if self.shard is None:
-            name = ("std_first" if first else "std") + ("_upd" if update else "")
-            self._replay_or_run(name, lambda: self.std_round(first, update))
-            return
         pending = 0 if first else 1
+        if self.shard is None or self._shard_rounds_captured():
+            name = ("std_first" if first else "std") + ("_upd" if update else "")
+            self._replay_or_run(name, lambda: self.std_round(first, update), self.gamma + pending)
+            return
         self._replay_or_run("drafts", self._drafts)
         self._verify_phase(pending)
         self._replay_or_run("post_first" if first else "post", lambda: self._post(pending))
 
-    def _replay_or_run(self, name: str, fn) -> None:
+    def _replay_or_run(self, name: str, fn, dense_nq: int = 0) -> None:
+        """Replay graph `name` (announcing its dense forward of dense_nq
+        tokens to the shard servers first, when sharded) or run fn eagerly."""
         g = self._graphs.get(name)
         if g is not None:
+            if self.shard is not None and dense_nq:
+                self.shard.announce(dense_nq)
             g.replay()
         else:
             fn()

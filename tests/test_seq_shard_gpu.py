@@ -1,6 +1,8 @@
-"""Sequence-sharded verify on 2 GPUs (NCCL): STD == AR token for token when the
+"""Sequence-sharded verify on 2 GPUs: STD == AR token for token when the
 dense cache is split across ranks (the owner holds the tail and runs the
-model, the other rank serves its key range every dense forward).
+model, the other rank serves its key range every dense forward), with the
+per-layer exchange over peer memory (p2p: IPC-mapped buffers, epoch flags,
+the owner's rounds captured in CUDA graphs) and over NCCL collectives.
 
 Needs two visible GPUs; skipped otherwise (the protocol itself is covered on
 CPU by test_seq_shard_cpu.py)."""
@@ -25,7 +27,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, B, gamma, max_new, q):
+def _worker(rank, world, port, B, gamma, max_new, transport, q):
     import torch.distributed as dist
 
     from std_b200 import ops
@@ -45,12 +47,14 @@ def _worker(rank, world, port, B, gamma, max_new, q):
         P = V + T
         cap = STDRunner.dense_capacity(P, max_new, gamma)
         plan = ShardPlan.make(P, cap, world)
-        ex = ShardExchange(plan, rank, B, TINY.num_attention_heads, TINY.head_dim, gamma + 1, dev)
+        ex = ShardExchange(plan, rank, B, TINY.num_attention_heads, TINY.head_dim, gamma + 1, dev, transport=transport)
         if not ex.is_owner:
             local = torch.zeros(TINY.num_hidden_layers, 2, B, TINY.num_key_value_heads, plan.local_cap(rank),
                                 TINY.head_dim, dtype=torch.bfloat16, device=dev)
             ex.distribute(None, local, P)
-            q.put(("served", rank, ex.serve(local, TINY.num_hidden_layers)))
+            served = ex.serve(local, TINY.num_hidden_layers)
+            ex.release()
+            q.put(("served", rank, served, ops.device_error()))
             return
         g = torch.Generator().manual_seed(31)
         ids = torch.randint(10, TINY.vocab_size, (B, P), generator=g)
@@ -67,6 +71,7 @@ def _worker(rank, world, port, B, gamma, max_new, q):
         runner.run_ar()
         ar_tokens = runner.out_tokens.cpu().clone()
         ex.close()
+        ex.release()
         torch.cuda.synchronize()
         q.put(("owner", bool(torch.equal(std_tokens, ar_tokens)), int(runner.n_gen.min()), sum(st["rounds"]),
                ops.device_error()))
@@ -75,13 +80,13 @@ def _worker(rank, world, port, B, gamma, max_new, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("B,gamma", [(1, 9), (2, 5)])
-def test_sharded_std_equals_ar(B, gamma):
+@pytest.mark.parametrize("B,gamma,transport", [(1, 9, "p2p"), (2, 5, "p2p"), (2, 5, "collective")])
+def test_sharded_std_equals_ar(B, gamma, transport):
     world, max_new = 2, 24
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, B, gamma, max_new, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, B, gamma, max_new, transport, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -101,3 +106,4 @@ def test_sharded_std_equals_ar(B, gamma):
     # every STD round has one verify forward and every AR step one dense
     # forward; each of them reached the server
     assert served[2] >= max_new + 1
+    assert served[3] == 0
