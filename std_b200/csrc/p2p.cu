@@ -6,16 +6,17 @@
 //   owner : p2p_post   copies the layer's queries into its exported query
 //                      buffer and publishes epoch e to every server's flag;
 //   server: p2p_wait   waits for e, then its verify kernel reads the queries
-//                      from the owner's memory over NVLink and writes its
-//                      (O, LSE) partial into its own exported buffer;
+//                      from the owner's memory over NVLink and stores its
+//                      (O, LSE) partial into its slot of the owner's inbox;
 //           p2p_post   publishes e to its slot of the owner's flag array;
 //   owner : p2p_wait   waits for every server's e, then the list merge reads
-//                      each server's partial from that server's memory.
-// Nothing is copied twice and no rank writes another's data: the only remote
-// stores are the flags.  A rank overwrites an exported buffer only after the
-// peer that reads it has signalled a later step (the owner posts the next
-// layer's queries after merging this layer's partials, which the servers
-// wrote after reading these queries), so reuse needs no extra handshake.
+//                      every partial from its own memory.
+// Loads cross NVLink only for the queries (a few round trips at the start of
+// the verify kernel); the partials cross as stores, which do not stall the
+// writer.  A buffer is rewritten only after the peer that reads it has
+// signalled a later step (the owner posts the next layer's queries after
+// merging this layer's partials, which the servers stored after reading
+// these queries), so reuse needs no extra handshake.
 // Epochs are device-side counters advanced by the kernels, so the steps can
 // be captured in a CUDA graph and replayed.  Waits give up after about one
 // second (STD_DEVERR_WAIT_TIMEOUT) instead of spinning for ever.
@@ -32,11 +33,12 @@ struct P2PFlags {
   int n;
 };
 
-STD_DEV int ld_acquire_sys(const int* p) {
+STD_DEV int ld_relaxed_sys(const int* p) {
   int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+STD_DEV void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 STD_DEV void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -47,8 +49,10 @@ STD_DEV void st_release_sys(int* p, int v) {
 // it completes, so stream order holds transitively.
 
 // dst <- src (n16 16-byte vectors, one block), then epoch = ++*counter is
-// published to every flag: after the barrier, one system-scope fence by the
-// publishing thread orders the whole block's copies before the flag stores.
+// published to every flag.  The barrier orders the block's copies before the
+// publishing thread's system-scope release stores (release is cumulative), and
+// pdl_wait has ordered everything the stream wrote before this kernel (the
+// partial a server's verify stored into the owner's memory) before it too.
 __global__ void __launch_bounds__(1024) p2p_post_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                                         size_t n16, P2PFlags flags, int* counter) {
   pdl_wait();
@@ -58,7 +62,6 @@ __global__ void __launch_bounds__(1024) p2p_post_kernel(const uint4* __restrict_
   if (threadIdx.x == 0) {
     const int e = *counter + 1;
     *counter = e;
-    __threadfence_system();
     for (int i = 0; i < flags.n; ++i) st_release_sys(flags.flag[i], e);
   }
 }
@@ -78,7 +81,7 @@ __global__ void p2p_wait_kernel(const int* flags, int n, int* counter) {
   e = *counter + 1;
   for (int i = 0; i < n && !timed_out; ++i) {
     uint32_t polls = 0;
-    while (ld_acquire_sys(flags + i) < e) {
+    while (ld_relaxed_sys(flags + i) < e) {
       if ((++polls & 255u) == 0u && globaltimer_ns() - t0 > 1000000000ull) {
         std_set_error(STD_DEVERR_WAIT_TIMEOUT);
         timed_out = true;
@@ -86,7 +89,7 @@ __global__ void p2p_wait_kernel(const int* flags, int n, int* counter) {
       }
     }
   }
-  __threadfence_system();
+  fence_acq_rel_sys();  // with the relaxed polls above: acquire of every flag seen
   *counter = e;
 }
 

@@ -387,42 +387,91 @@ __global__ void __launch_bounds__(VF_THREADS, 1)
 }
 
 // Combine split partials: m = max_s m_s, w_s = exp2(m_s - m) (0 for splits a
-// row cannot see), out = (sum_s w_s o_s) / (sum_s w_s l_s), split order.
-// One thread per (row, 4 dims); requests whose keys fit one split are skipped
-// (the split kernel wrote them).
-__global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p) {
+// row cannot see), out = (sum_s w_s o_s) / (sum_s w_s l_s).  One block of nw
+// warps per query row (nw = ceil(max_splits / VM_PER), at most VM_WARPS: a
+// function of the cache shape); requests whose keys fit one split are skipped
+// (the split kernel wrote them).  At small batches this kernel is a chain of
+// dependent memory round trips, so it is laid out for latency: warp w takes
+// splits w, w + nw, ... (lane = 4 dims) and loads its first VM_PER of them
+// while the block reduces the split maxima, so up to nw * VM_PER splits cost
+// one round trip; the warps' sums are added in warp order -- a fixed order,
+// so the result depends only on the split boundaries (an AR step and a
+// verify block on the same cache combine identically).
+constexpr int VM_WARPS = 8, VM_PER = 8;
+
+__global__ void __launch_bounds__(VM_WARPS * 32) verify_merge_kernel(const VerifyParams p) {
   pdl_launch_dependents();  // followed by the O projection GEMM (weights before its wait)
   pdl_wait();
-  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int r = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int L = verify_len(p, b);
   const int n_splits = (L + p.split_keys - 1) / p.split_keys;
-  if (n_splits <= 1) return;
-  const int nrows = VF_G * p.nq;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  const int r = idx / (VF_D / 4), d4 = idx % (VF_D / 4);
-  if (r >= nrows) return;
+  if (n_splits <= 1 || r >= VF_G * p.nq) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
   const size_t slot0 = (static_cast<size_t>(b) * p.Hkv + kvh) * p.max_splits * 128 + r;
+  const float2* ml = reinterpret_cast<const float2*>(p.ws_ml) + slot0;                  // split s: ml[s * 128]
+  const float4* os = reinterpret_cast<const float4*>(p.ws_o) + slot0 * (VF_D / 4) + lane;  // split s: os[s * 4096]
+  float2 mlv[VM_PER];
+  float4 ov[VM_PER];
+#pragma unroll
+  for (int j = 0; j < VM_PER; ++j) {
+    const int s = warp + nw * j;
+    mlv[j] = s < n_splits ? __ldcg(ml + static_cast<size_t>(s) * 128) : make_float2(-INFINITY, 0.f);
+    ov[j] = s < n_splits ? __ldcg(os + static_cast<size_t>(s) * 128 * (VF_D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __shared__ float s_m[VM_WARPS];
+  __shared__ float s_l[VM_WARPS];
+  __shared__ float4 s_a[VM_WARPS][32];
   float m = -INFINITY;
-#pragma unroll 8
-  for (int s = 0; s < n_splits; ++s) m = fmaxf(m, __ldcg(&p.ws_ml[(slot0 + static_cast<size_t>(s) * 128) * 2]));
+  for (int s = tid; s < n_splits; s += nw * 32) m = fmaxf(m, __ldcg(&ml[static_cast<size_t>(s) * 128].x));
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, sh));
+  if (lane == 0) s_m[warp] = m;
+  __syncthreads();
+  m = s_m[0];
+  for (int w = 1; w < nw; ++w) m = fmaxf(m, s_m[w]);
   float l = 0.f;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-  for (int s = 0; s < n_splits; ++s) {
-    const size_t sl = slot0 + static_cast<size_t>(s) * 128;
-    const float ms = __ldcg(&p.ws_ml[sl * 2]);
-    if (ms == -INFINITY) continue;
-    const float w = exp2f(ms - m);
-    l += w * __ldcg(&p.ws_ml[sl * 2 + 1]);
-    const float4 o = __ldcg(reinterpret_cast<const float4*>(p.ws_o + sl * VF_D) + d4);
-    a.x += w * o.x;
-    a.y += w * o.y;
-    a.z += w * o.z;
-    a.w += w * o.w;
+  for (int s0 = 0; s0 < n_splits; s0 += nw * VM_PER) {
+    if (s0 > 0) {
+#pragma unroll
+      for (int j = 0; j < VM_PER; ++j) {
+        const int s = s0 + warp + nw * j;
+        mlv[j] = s < n_splits ? __ldcg(ml + static_cast<size_t>(s) * 128) : make_float2(-INFINITY, 0.f);
+        ov[j] = s < n_splits ? __ldcg(os + static_cast<size_t>(s) * 128 * (VF_D / 4))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VM_PER; ++j) {
+      // past the last split, or a split the row cannot see (m_s = -inf, l_s =
+      // 0, o_s = 0: the split kernel writes every row): weight 0 adds +-0 to
+      // sums that start at +0
+      const bool live = mlv[j].x != -INFINITY;
+      const float w = live ? exp2f(mlv[j].x - m) : 0.f;
+      l += w * mlv[j].y;
+      a.x += w * ov[j].x;
+      a.y += w * ov[j].y;
+      a.z += w * ov[j].z;
+      a.w += w * ov[j].w;
+    }
+  }
+  s_a[warp][lane] = a;
+  if (lane == 0) s_l[warp] = l;
+  __syncthreads();
+  if (warp != 0) return;
+  a = s_a[0][lane];
+  l = s_l[0];
+  for (int w = 1; w < nw; ++w) {
+    const float4 t = s_a[w][lane];
+    a.x += t.x;
+    a.y += t.y;
+    a.z += t.z;
+    a.w += t.w;
+    l += s_l[w];
   }
   const float inv = l > 0.f ? 1.f / l : 0.f;
   const int t = r / VF_G, g = r % VF_G;
-  const size_t o = ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + 4 * d4;
+  const size_t o = ((static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g) * VF_D + 4 * lane;
   if (p.out_f32 != nullptr) {
     *reinterpret_cast<float4*>(p.out_f32 + o) = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
   } else {
@@ -431,7 +480,7 @@ __global__ void __launch_bounds__(128) verify_merge_kernel(const VerifyParams p)
     pk.y = pack_bf16x2(a.z * inv, a.w * inv);
     *reinterpret_cast<uint2*>(p.out + o) = pk;
   }
-  if (d4 == 0 && p.lse != nullptr)
+  if (lane == 0 && p.lse != nullptr)
     p.lse[(static_cast<size_t>(b) * p.nq + t) * p.Hq + kvh * VF_G + g] =
         l > 0.f ? (m + log2f(l)) * 0.69314718055994530942f : -INFINITY;
 }
@@ -541,8 +590,9 @@ static int verify_launch(const void* q, const void* k_cache, const void* v_cache
   if (launch_pdl(stdb::verify_attn_kernel, grid, dim3(stdb::VF_THREADS), stdb::VF_SMEM, s, tk, tv, p) != cudaSuccess)
     return 4;
   if (p.max_splits > 1) {
-    dim3 mgrid((stdb::VF_G * nq * (stdb::VF_D / 4) + 127) / 128, Hkv, B);
-    if (launch_pdl(stdb::verify_merge_kernel, mgrid, dim3(128), 0, s, p) != cudaSuccess) return 4;
+    dim3 mgrid(stdb::VF_G * nq, Hkv, B);  // one block per row
+    const int nw = std::min<int>(stdb::VM_WARPS, (p.max_splits + stdb::VM_PER - 1) / stdb::VM_PER);
+    if (launch_pdl(stdb::verify_merge_kernel, mgrid, dim3(32 * nw), 0, s, p) != cudaSuccess) return 4;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : 4;
 }

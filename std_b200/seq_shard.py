@@ -32,10 +32,10 @@ Two transports carry the per-layer exchange:
       (std_b200/csrc/p2p.cu): the owner copies the layer's queries into its
       exported query buffer and posts an epoch flag to every server; a server
       waits for it, runs the verify kernel on the queries read straight from
-      the owner's memory over NVLink, writing its fp32 partial into its own
-      exported buffer, and posts its flag; the owner waits for every server
-      and merges with a kernel that reads each partial from its server's
-      memory.  Waits are bounded (about a second).  The owner's layer steps
+      the owner's memory over NVLink, storing its fp32 partial into its slot
+      of the owner's exported inbox, and posts its flag; the owner waits for
+      every server and merges from its own memory.  Waits are bounded (about
+      a second).  The owner's layer steps
       are kernels and copies only, so its dense forward can be captured in a
       CUDA graph: begin() announces a forward only outside capture, and a
       caller replaying such a graph calls announce(nq) first.
@@ -160,27 +160,29 @@ class ShardExchange:
             self._opened.append(ptr.value)
             return ptr.value
 
+        # one server's [O | LSE] partial in the owner's inbox, 256-byte aligned slots
+        self._slot_bytes = (rows * (D + 1) * 4 + 255) // 256 * 256
         self._allocs, self._opened = [], []
         with torch.cuda.device(self.device):
             self._ctr = alloc(16)  # [query epoch, partial epoch] of this rank
             if self.is_owner:
-                self._q_ipc = alloc(rows * D * 2)        # the layer's queries, read by the servers
-                self._pflags = alloc(4 * max(1, N - 1))  # slot r: server r's partial epoch
-                exports = (export(self._q_ipc), export(self._pflags))
+                self._q_ipc = alloc(rows * D * 2)                       # the layer's queries, read by the servers
+                self._pflags = alloc(4 * max(1, N - 1))                 # slot r: server r's partial epoch
+                self._inbox = alloc(max(1, N - 1) * self._slot_bytes)   # slot r: server r's partial
+                exports = (export(self._q_ipc), export(self._pflags), export(self._inbox))
             else:
-                self._part_ipc = alloc(rows * (D + 1) * 4)  # this server's [O | LSE] partial, read by the owner
-                self._qflag = alloc(16)                     # the owner's query epoch
-                exports = (export(self._part_ipc), export(self._qflag))
+                self._qflag = alloc(16)  # the owner's query epoch
+                exports = (export(self._qflag),)
             every = [None] * N
             dist.all_gather_object(every, exports, group=self.group)
             if self.is_owner:
-                servers = range(self.plan.owner)
-                self._peer_parts = [open_peer(every[r][0]) for r in servers]
-                self._peer_qflags = [open_peer(every[r][1]) for r in servers]
+                self._peer_qflags = [open_peer(every[r][0]) for r in range(self.plan.owner)]
                 self._own_part = torch.zeros(rows * (D + 1), dtype=torch.float32, device=self.device)
             else:
-                self._peer_q = open_peer(every[self.plan.owner][0])
-                self._peer_pflag = open_peer(every[self.plan.owner][1]) + 4 * self.rank
+                owner = every[self.plan.owner]
+                self._peer_q = open_peer(owner[0])
+                self._peer_pflag = open_peer(owner[1]) + 4 * self.rank
+                self._peer_slot = open_peer(owner[2]) + self.rank * self._slot_bytes
             self.q = None
         dist.barrier(group=self.group)
 
@@ -271,7 +273,8 @@ class ShardExchange:
         self.partial_fn(q4, kc, vc, lens, len_offset, True, part[: rows * D].view(B, nq, Hq, D),
                         part[rows * D:].view(B, nq, Hq))
         _lib.call("std_p2p_wait", self._pflags, N - 1, self._ctr + 4, s)
-        parts = (ctypes.c_ulonglong * N)(*self._peer_parts, part.data_ptr())  # rank order: servers, then owner
+        # rank order: the servers' inbox slots, then the owner's own partial
+        parts = (ctypes.c_ulonglong * N)(*[self._inbox + r * self._slot_bytes for r in range(N - 1)], part.data_ptr())
         _lib.call("std_merge_partials_f32_list", parts, N, rows, D, out4.data_ptr(), None, s)
 
     def close(self) -> None:
@@ -303,7 +306,8 @@ class ShardExchange:
 
     def _serve_layer_p2p(self, nq: int, kc: torch.Tensor, vc: torch.Tensor, lens: torch.Tensor) -> None:
         """Wait for the owner's queries, compute this key range's partial from
-        them (read in the owner's memory) into the exported buffer, post it."""
+        them (read in the owner's memory) into this rank's slot of the owner's
+        inbox, post it."""
         from . import _lib, ops
 
         B, Hq, D = self.B, self.Hq, self.D
@@ -314,7 +318,7 @@ class ShardExchange:
         nb = _lib.query("std_verify_attn_workspace_bytes", B, Hkv, cap)
         ws = ops.workspace("verify", nb, self.device)
         _lib.call("std_verify_attn_partial", self._peer_q, kc.data_ptr(), vc.data_ptr(), lens.data_ptr(), 0, nq, 0,
-                  B, Hq, Hkv, D, cap, self._part_ipc, self._part_ipc + rows * D * 4, ws.data_ptr(), ws.numel(), s)
+                  B, Hq, Hkv, D, cap, self._peer_slot, self._peer_slot + rows * D * 4, ws.data_ptr(), ws.numel(), s)
         flags = (ctypes.c_ulonglong * 1)(self._peer_pflag)
         _lib.call("std_p2p_post", None, None, 0, flags, 1, self._ctr + 4, s)
 
