@@ -12,15 +12,14 @@ request is split by sequence position across the ranks of one node:
       sparse cache and runs the draft steps.
 
 A dense forward on the owner (a verify block or an AR step) exchanges, per
-layer: the owner broadcasts the layer's queries, every rank computes the
-(O, LSE) partial of its key range with the verify kernel in fp32 (the owner
-causal over its local keys, the servers non-causal) into one packed buffer
-[O | LSE], the packed partials are all-gathered in one collective and the
-owner merges them in rank order with std_merge_partials_f32: two collectives
-per layer.  Attention over disjoint key ranges combines exactly through LSE,
-so the only difference from the unsharded result is fp32 rounding at fixed
-boundaries -- identical for a token verified in a block and the same token
-decoded alone, which keeps STD == AR.
+layer: every rank computes the (O, LSE) partial of its key range for the
+owner's queries with the verify kernel in fp32 (the owner causal over its
+local keys, the servers non-causal), and the owner merges the partials in
+rank order (std_merge_partials_f32 / _list).  Attention over disjoint key
+ranges combines exactly through LSE, so the only difference from the
+unsharded result is fp32 rounding at fixed boundaries -- identical for a
+token verified in a block and the same token decoded alone, which keeps
+STD == AR.
 
 Each forward starts with a 2-int header broadcast ([1, nq]); [0, 0] ends the
 servers' loop.
