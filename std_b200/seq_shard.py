@@ -115,6 +115,8 @@ class ShardExchange:
                 else "collective"
         if transport not in ("p2p", "collective"):
             raise ValueError(f"unknown transport {transport!r}")
+        if transport == "p2p" and self.device.type != "cuda":
+            raise ValueError("the p2p transport maps GPU memory: it needs a CUDA device")
         self.transport = transport
         N = plan.world
         rows = B * max_nq * Hq

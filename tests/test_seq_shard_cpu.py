@@ -130,3 +130,13 @@ def test_shard_plan():
         ShardPlan.make(100, 256, 4)
     with pytest.raises(ValueError):
         ShardPlan.make(1000, 1024, 1)
+
+
+def test_transport_choice():
+    plan = ShardPlan.make(200, 256, 2)
+    ex = ShardExchange(plan, 0, 1, 4, 8, 2, "cpu", partial_fn=lambda *a: None, merge_fn=lambda *a: None)
+    assert ex.transport == "collective" and not ex.capturable  # CPU: only the collective exchange
+    with pytest.raises(ValueError):
+        ShardExchange(plan, 0, 1, 4, 8, 2, "cpu", transport="p2p")
+    with pytest.raises(ValueError):
+        ShardExchange(plan, 0, 1, 4, 8, 2, "cpu", transport="shm")
