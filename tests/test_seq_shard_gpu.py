@@ -79,10 +79,12 @@ def _worker(rank, world, port, B, gamma, max_new, transport, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("B,gamma,transport", [(1, 9, "p2p"), (2, 5, "p2p"), (2, 5, "collective")])
-def test_sharded_std_equals_ar(B, gamma, transport):
-    world, max_new = 2, 24
+@pytest.mark.parametrize("world,B,gamma,transport",
+                         [(2, 1, 9, "p2p"), (2, 2, 5, "p2p"), (2, 2, 5, "collective"), (4, 2, 5, "p2p")])
+def test_sharded_std_equals_ar(world, B, gamma, transport):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    max_new = 24
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -98,12 +100,14 @@ def test_sharded_std_equals_ar(B, gamma, transport):
     assert codes == [0] * world, codes
     msgs = [q.get(timeout=5) for _ in range(world)]
     owner = [m for m in msgs if m[0] == "owner"][0]
-    served = [m for m in msgs if m[0] == "served"][0]
+    servers = [m for m in msgs if m[0] == "served"]
+    assert sorted(m[1] for m in servers) == list(range(world - 1))
     _, equal, n_min, rounds, err = owner
     assert err == 0
     assert equal, "sharded STD tokens differ from sharded AR tokens"
     assert n_min == max_new
     # every STD round has one verify forward and every AR step one dense
     # forward; each of them reached the server
-    assert served[2] >= max_new + 1
-    assert served[3] == 0
+    for served in servers:
+        assert served[2] >= max_new + 1
+        assert served[3] == 0
