@@ -68,17 +68,17 @@ __global__ void __launch_bounds__(1024) p2p_post_kernel(const uint4* __restrict_
 
 // Wait until flags[0..n) all reach epoch = *counter + 1, then advance the
 // counter.  Bounded: after ~1 s the error word is set and the kernel returns.
-// The spin may start before the predecessor has finished; the kernel ends
-// only after it (pdl_wait), so its successor sees both the peers' data and
-// the predecessor's.
+// Launched early, it starts polling once its predecessor has finished
+// (pdl_wait: the counter was written by an earlier kernel of this stream), so
+// its successor sees both the peers' data and the predecessor's.  Polls are
+// relaxed loads; one acquire fence after the last orders what follows.
 __global__ void p2p_wait_kernel(const int* flags, int n, int* counter) {
   pdl_launch_dependents();
   if (threadIdx.x != 0) return;
+  pdl_wait();
   const uint64_t t0 = globaltimer_ns();
+  const int e = *counter + 1;
   bool timed_out = false;
-  int e = 0;
-  pdl_wait();  // the counter was last written by an earlier kernel of this stream
-  e = *counter + 1;
   for (int i = 0; i < n && !timed_out; ++i) {
     uint32_t polls = 0;
     while (ld_relaxed_sys(flags + i) < e) {
